@@ -1,0 +1,446 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 attention block for pickle (decode-attn KV GB/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N = 1: headline = Llama-3-8B-shaped decode, B=64, ctx 4096 (KV cache
+       2.15 GB > L2, so no flush between steps), plus B=1 / B=8 (L2 flushed
+       between steps), the 70B-shaped and long-context decodes on one GPU,
+       and causal prefill (TFLOP/s) as extras.
+N > 1: headline = Llama-3-70B-shaped decode sharded by KV-head group
+       (B=16, ctx 32768), head outputs all-gathered over NVLink (NCCL);
+       extra = long-context decode sharded by sequence chunk (ctx 131072),
+       partial (m, l, acc) triples all-gathered and merged by log-sum-exp.
+       Strong scaling: total work fixed. Time = max over ranks.
+
+One JSON line on rank 0. `--impl reference` times the reference's own
+OpenMP attention block (oracle/_ref, compiled from its sources) on the host
+cores on a bounded sample of the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from lestramanika_b200.workloads import C2_B1, C2_B8, C2_B64, C3, C4, C5, head_shard, seq_shard  # noqa: E402
+
+MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS = 6650.0, 1590.0
+L2_FLUSH_BYTES = 512 << 20
+
+
+def peaks():
+    try:
+        m = json.load(open(MEASURED))
+        return float(m["hbm_gbs"]), float(m["bf16_tflops"]), float(m.get("bf16_tflops_sustained", m["bf16_tflops"])), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
+
+
+def profile_traffic(name):
+    """dram read+write bytes per launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        parts = line.strip().split("\t")
+        if len(parts) >= 2 and parts[0] == name:
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.idx = str(device_index)
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", self.idx], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx.append(float(p[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, p[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------
+
+def _torch():
+    import torch
+    return torch
+
+
+def make_decode_state(w, device, H=None, HK=None, B=None, ctx_rows=None, seed=0):
+    """Handle with a seeded N(0,1) device cache for workload w (or a shard of it)."""
+    torch = _torch()
+    from lestramanika_b200 import PickleCuda
+    H = H or w.H
+    HK = HK or w.HK
+    B = B or w.B
+    rows = w.ctx if ctx_rows is None else ctx_rows
+    cu = PickleCuda(1, H, HK, w.D, rows + 1, rope_theta=w.theta, n_seqs=B, rope_len=w.ctx + 1, device=device)
+    kt, vt = cu.kv_tensors(0)
+    g = torch.Generator(device=f"cuda:{device}")
+    g.manual_seed(seed)
+    for b in range(B):
+        kt[b, :, :rows].normal_(generator=g)
+        vt[b, :, :rows].normal_(generator=g)
+    dev = torch.device("cuda", device)
+    q = torch.randn((B, H, w.D), generator=g, device=dev)
+    k = torch.randn((B, HK, w.D), generator=g, device=dev)
+    v = torch.randn((B, HK, w.D), generator=g, device=dev)
+    ao = torch.empty((B, H, w.D), device=dev)
+    torch.cuda.synchronize(device)
+    return cu, q, k, v, ao
+
+
+def time_decode(cu, w, q, k, v, ao, steps, warmup, flush=None):
+    """Device time of `steps` decode launches (ms list), CUDA events on the launching stream."""
+    torch = _torch()
+    st = torch.cuda.current_stream()
+    for _ in range(warmup):
+        cu.decode_batch_dev(0, q.shape[0], w.ctx, q, k, v, ao, st)
+    cu.sync(st)
+    if flush is None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            cu.decode_batch_dev(0, q.shape[0], w.ctx, q, k, v, ao, st)
+        e1.record(st)
+        cu.sync(st)
+        return [e0.elapsed_time(e1) / steps] * steps
+    # L2 flushed before every step, outside its event pair. Nothing syncs
+    # between steps: the decode launch is queued while the flush runs, so the
+    # events time the kernel, not the host's launch latency.
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in ev:
+        flush.add_(1)
+        e0.record(st)
+        cu.decode_batch_dev(0, q.shape[0], w.ctx, q, k, v, ao, st)
+        e1.record(st)
+    cu.sync(st)
+    return [e0.elapsed_time(e1) for e0, e1 in ev]
+
+
+def time_decode_e2e(cu, w, q, k, v, ao, steps, warmup):
+    """Same decode with every step's q/k/v copied in from pinned host memory and
+    the output read back to pinned host memory inside the timed region."""
+    torch = _torch()
+    st = torch.cuda.current_stream()
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    hao = torch.empty(ao.shape, dtype=ao.dtype).pin_memory()
+
+    def step():
+        q.copy_(hq, non_blocking=True)
+        k.copy_(hk, non_blocking=True)
+        v.copy_(hv, non_blocking=True)
+        cu.decode_batch_dev(0, q.shape[0], w.ctx, q, k, v, ao, st)
+        hao.copy_(ao, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    cu.sync(st)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        step()
+    e1.record(st)
+    cu.sync(st)
+    ms = e0.elapsed_time(e1) / steps
+    h2d = sum(x.numel() * 4 for x in (hq, hk, hv))
+    return ms, h2d, hao.numel() * 4
+
+
+def decode_line(w, device, steps, warmup, flush_l2):
+    torch = _torch()
+    cu, q, k, v, ao = make_decode_state(w, device)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=f"cuda:{device}") if flush_l2 else None
+    times = time_decode(cu, w, q, k, v, ao, steps, warmup, flush)
+    splits = cu.decode_plan(w.B, w.ctx)[0]
+    ms = sum(times) / len(times)
+    out = {"workload": w.name, "ms": ms, "GBps": w.kv_bytes / (ms * 1e-3) / 1e9, "splits": splits,
+           "l2": "flushed between steps" if flush_l2 else "inputs larger than L2"}
+    e2e = None
+    if not flush_l2:
+        e2e = time_decode_e2e(cu, w, q, k, v, ao, steps, warmup)
+    cu.close()
+    del q, k, v, ao, flush
+    torch.cuda.empty_cache()
+    return out, e2e
+
+
+def prefill_line(w, device, steps, warmup, precision):
+    torch = _torch()
+    from lestramanika_b200 import PickleCuda
+    dev = torch.device("cuda", device)
+    cu = PickleCuda(1, w.H, w.HK, w.D, w.T, rope_theta=w.theta, n_seqs=w.B, device=device)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    q = torch.randn((w.B, w.T, w.H, w.D), generator=g, device=dev)
+    k = torch.randn((w.B, w.T, w.HK, w.D), generator=g, device=dev)
+    v = torch.randn((w.B, w.T, w.HK, w.D), generator=g, device=dev)
+    ao = torch.empty_like(q)
+    st = torch.cuda.current_stream()
+    for _ in range(warmup):
+        cu.prefill_dev(0, w.B, 0, w.T, q, k, v, ao, precision, st)
+    cu.sync(st)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        cu.prefill_dev(0, w.B, 0, w.T, q, k, v, ao, precision, st)
+    e1.record(st)
+    cu.sync(st)
+    ms = e0.elapsed_time(e1) / steps
+    cu.close()
+    return {"workload": w.name, "precision": "bf16-tcgen05" if precision else "f32-cuda-core", "ms": ms,
+            "TFLOPs": w.flops / (ms * 1e-3) / 1e12, "includes": "rope+cast+kv-cache write pre-pass"}
+
+
+def cpu_baseline(seconds=10.0):
+    """The reference's OpenMP attention (oracle/_ref, compiled from its sources)
+    on the host cores, on whole sequences of the C2 workload (ctx 4096)."""
+    ncores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(ncores))
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    import numpy as np
+    import oracle
+    w = C2_B64
+    rng = np.random.Generator(np.random.Philox(5))
+    if oracle.RefBlock.available():
+        blk, kind = oracle.RefBlock(1, w.H, w.HK, w.D, w.ctx + 1, w.theta), "reference"
+        lib = oracle.RefBlock.lib()
+        kptr, vptr = lib.ref_block_k_cache(blk._h), lib.ref_block_v_cache(blk._h)
+    else:
+        blk, kind = oracle.OracleAttn(1, w.H, w.HK, w.D, w.ctx + 1, w.theta), "port"
+        lo = oracle.oracle_lib()
+        kptr, vptr = lo.oracle_attn_k_cache(blk._h), lo.oracle_attn_v_cache(blk._h)
+    n = (w.ctx + 1) * w.HK * w.D
+    kc = np.ctypeslib.as_array(kptr, shape=(n,))
+    vc = np.ctypeslib.as_array(vptr, shape=(n,))
+    kc[:w.ctx * w.HK * w.D] = rng.standard_normal(w.ctx * w.HK * w.D, dtype=np.float32)
+    vc[:w.ctx * w.HK * w.D] = rng.standard_normal(w.ctx * w.HK * w.D, dtype=np.float32)
+    q = rng.standard_normal(w.H * w.D, dtype=np.float32)
+    k = rng.standard_normal(w.HK * w.D, dtype=np.float32)
+    v = rng.standard_normal(w.HK * w.D, dtype=np.float32)
+    blk.decode(0, w.ctx, q, k, v)                 # warm-up (also fills the RoPE table)
+    seqs, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        blk.decode(0, w.ctx, q, k, v)
+        seqs += 1
+    dt = time.perf_counter() - t0
+    blk.close()
+    per_seq = w.kv_bytes / w.B
+    return {"value": per_seq * seqs / dt / 1e9, "unit": "GB/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
+            "kind": kind, "sample": f"{seqs} sequences of {w.name} (one reference call each) in {dt:.1f} s",
+            "ms_per_sequence": dt / seqs * 1e3}
+
+
+def run_ours_single(args):
+    torch = _torch()
+    device = 0
+    torch.cuda.set_device(device)
+    hbm, bf16, bf16_sus, src = peaks()
+    with ClockSampler(device) as clk:
+        head, e2e = decode_line(C2_B64, device, args.steps, args.warmup, flush_l2=False)
+    extras = {}
+    for w, flush in ((C2_B1, True), (C2_B8, False), (C4, False), (C5, False)):
+        line, _ = decode_line(w, device, max(args.steps, 5), args.warmup, flush)
+        line["frac_of_measured_hbm"] = line["GBps"] / hbm
+        extras[w.name] = line
+    try:
+        from lestramanika_b200 import PREFILL_BF16
+        pf = prefill_line(C3, device, max(2, min(args.steps, 5)), max(args.warmup, 3), PREFILL_BF16)
+        pf["frac_of_measured_bf16"] = pf["TFLOPs"] / bf16
+        extras["prefill"] = pf
+    except Exception as exc:  # reported, not hidden
+        extras["prefill"] = {"error": str(exc)[:200]}
+    gbps = head["GBps"]
+    e2e_ms, h2d, d2h = e2e
+    out = {
+        "metric": "decode-attn KV GB/s", "value": gbps, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": head["ms"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) cache and q/k/v, seeded",
+        "config": {"workload": C2_B64.name, "B": 64, "H": 32, "HK": 8, "D": 128, "ctx": 4096,
+                   "l2": head["l2"], "splits": head["splits"], "parallelism": "single GPU"},
+        "frac_of_8TBps": gbps / 8000.0,
+        "roofline": {"bound": "hbm", "achieved": gbps, "peak": hbm, "unit": "GB/s", "frac": gbps / hbm,
+                     "peak_source": f"{src} (hbm_gbs, copy burst)",
+                     "traffic": profile_traffic("decode_splitkv C2 B=64"),
+                     "algorithmic_bytes_per_launch": C2_B64.kv_bytes},
+        "e2e": {"value": C2_B64.kv_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+        "extras": extras,
+    }
+    if not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    print(json.dumps(out), flush=True)
+
+
+def run_ours_multi(args, rank, world, local_rank):
+    torch = _torch()
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local_rank))
+    from lestramanika_b200 import dist as pdist
+    hbm, _, _, src = peaks()
+    res = pdist.bench_head_sharded(C4, rank, world, local_rank, args.steps, args.warmup)
+    res_seq = pdist.bench_seq_sharded(C5, rank, world, local_rank, args.steps, args.warmup)
+    clk = None
+    if rank == 0:
+        with ClockSampler(local_rank) as clk:
+            pass
+    if rank == 0:
+        gbps = C4.kv_bytes / (res["ms"] * 1e-3) / 1e9
+        out = {
+            "metric": "decode-attn KV GB/s", "value": gbps, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["ms"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) cache and q/k/v, seeded",
+            "config": {"workload": C4.name, "B": C4.B, "H": C4.H, "HK": C4.HK, "D": C4.D, "ctx": C4.ctx,
+                       "l2": "inputs larger than L2", "parallelism": f"kv-head shard x{world} + NCCL all-gather"},
+            "frac_of_8TBps_per_gpu": gbps / world / 8000.0,
+            "roofline": {"bound": "hbm", "achieved": res["kernel_GBps_per_gpu"], "peak": hbm, "unit": "GB/s",
+                         "frac": res["kernel_GBps_per_gpu"] / hbm, "peak_source": f"{src} (hbm_gbs)",
+                         "traffic": None, "note": "per-GPU decode kernel, collective excluded"},
+            "e2e": res["e2e"],
+            "gpu_launches": args.steps,
+            "clocks": res.get("clocks") or {"sm_mhz": None, "reasons": ["unsampled"]},
+            "extras": {"seq_sharded": {"workload": C5.name, "ms": res_seq["ms"],
+                                       "GBps": C5.kv_bytes / (res_seq["ms"] * 1e-3) / 1e9}},
+        }
+        print(json.dumps(out), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    import numpy as np  # noqa: F401
+    ncores = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(ncores)
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    import oracle
+    w = C2_B64 if args.gpus == 1 else C4
+    # Each step: a bounded sample of the workload's sequences, one reference call per sequence.
+    sample_seqs = 4 if args.gpus == 1 else 1
+    rng = np.random.Generator(np.random.Philox(5))
+    if not oracle.RefBlock.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built from the reference sources"}))
+        return
+    blk = oracle.RefBlock(1, w.H, w.HK, w.D, w.ctx + 1, w.theta)
+    lib = oracle.RefBlock.lib()
+    n = (w.ctx + 1) * w.HK * w.D
+    kc = np.ctypeslib.as_array(lib.ref_block_k_cache(blk._h), shape=(n,))
+    vc = np.ctypeslib.as_array(lib.ref_block_v_cache(blk._h), shape=(n,))
+    kc[:] = rng.standard_normal(n, dtype=np.float32)
+    vc[:] = rng.standard_normal(n, dtype=np.float32)
+    q = rng.standard_normal(w.H * w.D, dtype=np.float32)
+    k = rng.standard_normal(w.HK * w.D, dtype=np.float32)
+    v = rng.standard_normal(w.HK * w.D, dtype=np.float32)
+    for _ in range(args.warmup):
+        blk.decode(0, w.ctx, q, k, v)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for _ in range(sample_seqs):
+            blk.decode(0, w.ctx, q, k, v)
+    dt = time.perf_counter() - t0
+    blk.close()
+    per_seq = w.kv_bytes / w.B
+    gbps = per_seq * sample_seqs * args.steps / dt / 1e9
+    out = {"impl": "reference", "metric": "decode-attn KV GB/s", "value": gbps, "unit": "GB/s",
+           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+           "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) cache and q/k/v, seeded",
+           "config": {"workload": w.name, "B": w.B, "H": w.H, "HK": w.HK, "D": w.D, "ctx": w.ctx},
+           "cpu_baseline": {"value": gbps, "unit": "GB/s", "cores": ncores, "kind": "reference",
+                            "sample": f"{sample_seqs} of {w.B} sequences per step (reference has no batch "
+                                      f"dimension: one pickle attention call per sequence, OpenMP over heads)"},
+           "e2e": {"value": gbps, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        run_ours_multi(args, rank, world, local_rank)
+    else:
+        run_ours_single(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,183 @@
+/*
+ * pickle_cuda.h - C ABI of the B200 attention block for pickle.
+ *
+ * This library replaces the per-layer GQA attention block of pickle's
+ * host forward pass (lee-muriithi-kingori/lestramanika,
+ * src/pickle_fast.c:1910-2109): RoPE (NeoX half-split) on q and k, the
+ * KV-cache append, and causal softmax attention over positions [0, pos].
+ *
+ * Everything here is plain C: pointers, sizes and int status codes.
+ * Status codes are pickle's own (src/pickle.h:52-60) plus
+ * PICKLE_ERR_DEVICE for CUDA/NCCL failures.
+ *
+ * Ownership: host buffers (q, k, v, ao) belong to the caller. The device
+ * KV cache, the RoPE sin/cos tables and the split-KV workspace belong to
+ * the pickle_cuda_t handle. One handle is driven by one host thread and
+ * one CUDA stream at a time (pickle_fast_forward is not re-entrant either,
+ * src/pickle_fast.c:1857-1871 shares one set of work buffers).
+ *
+ * Device KV layout (head-major, 16-byte aligned rows):
+ *     k[layer][seq][kv_head][max_seq][head_dim]   float32
+ * replacing the host layout [layer][pos][kv_head][head_dim]
+ * (src/pickle_fast.h:145-157). A contiguous run of positions of one
+ * (layer, seq, kv_head) is one contiguous byte range, so a tile of keys
+ * is a single bulk copy.
+ */
+#ifndef PICKLE_CUDA_H
+#define PICKLE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes: the first nine mirror src/pickle.h:52-60. */
+#ifndef PICKLE_OK
+#define PICKLE_OK              0
+#define PICKLE_ERR_FORMAT     -1
+#define PICKLE_ERR_VERSION    -2
+#define PICKLE_ERR_MEMORY     -3
+#define PICKLE_ERR_TYPE       -4
+#define PICKLE_ERR_IO         -5
+#define PICKLE_ERR_ARG        -6
+#define PICKLE_ERR_RANGE      -7
+#define PICKLE_ERR_ARCH       -8
+#endif
+/* New: a CUDA runtime error, a device-side bounded wait that gave up, or a
+ * failed collective. The handle stays usable unless the CUDA context is
+ * lost (pickle_cuda_last_error tells which). */
+#define PICKLE_ERR_DEVICE     -9
+
+#define PICKLE_CUDA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define PICKLE_CUDA_API __attribute__((visibility("default")))
+#else
+#define PICKLE_CUDA_API
+#endif
+
+typedef struct pickle_cuda pickle_cuda_t;
+
+/* Model dimensions the attention block needs. The fields mirror
+ * pickle_fast_state_t (src/pickle_fast.h:55-123): n_layers, n_heads,
+ * n_kv_heads, head_dim, max_seq, half, rope_inv_freq. */
+typedef struct {
+    int          n_layers;      /* state->n_layers */
+    int          n_heads;       /* H: query heads */
+    int          n_kv_heads;    /* HK: KV heads; H % HK == 0 */
+    int          head_dim;      /* D: multiple of 4 (16-byte rows) */
+    int          max_seq;       /* positions per sequence slot */
+    int          half;          /* RoPE pairs per head: state->half = min(D/2, 64) */
+    const float* rope_inv_freq; /* host [half]: state->rope_inv_freq (src/pickle_fast.c:1638-1640);
+                                   NULL -> computed as 1/powf(theta, 2i/D) */
+    float        rope_theta;    /* used only when rope_inv_freq == NULL */
+    int          n_seqs;        /* sequence slots in the device cache (1 for pickle_fast_forward) */
+    int          rope_len;      /* RoPE table rows (absolute positions); 0 = max_seq. A
+                                   sequence-chunk shard holds max_seq cache rows but
+                                   rotates at absolute positions up to rope_len - 1. */
+} pickle_cuda_params_t;
+
+/* Create a handle on CUDA device `device`: allocates the device KV cache
+ * (zeroed, as calloc at src/pickle_fast.c:1793-1811), builds the RoPE
+ * sin/cos table for positions [0, max_seq) on the host exactly as
+ * pickle_fast_state_extend_rope does (src/pickle_fast.c:1772-1788) and
+ * uploads it. Replaces pickle_fast_kv_alloc for the attention path.
+ * Returns PICKLE_ERR_ARG on bad dimensions, PICKLE_ERR_MEMORY or
+ * PICKLE_ERR_DEVICE on allocation / CUDA failure. */
+PICKLE_CUDA_API int  pickle_cuda_init(const pickle_cuda_params_t* params, int device, pickle_cuda_t** out);
+PICKLE_CUDA_API void pickle_cuda_free(pickle_cuda_t* h);
+
+/* One decode step of one layer for sequence slot 0, host buffers.
+ * Replaces src/pickle_fast.c:1910-2094 for one token:
+ *   q [H*D] and k [HK*D] are rotated by RoPE at `pos` (not written back),
+ *   rotated k and v [HK*D] are appended to the device cache at `pos`,
+ *   ao [H*D] = softmax(q_h . K[0..pos] / sqrtf(D)) V[0..pos] per head h,
+ *   with kv_head = h * HK / H (src/pickle_fast.c:1963).
+ * Returns PICKLE_ERR_RANGE when pos >= max_seq (src/pickle_fast.c:1885). */
+PICKLE_CUDA_API int  pickle_cuda_attn_decode(pickle_cuda_t* h, int layer, size_t pos,
+                             const float* q, const float* k, const float* v,
+                             float* ao);
+
+/* Causal prefill of T tokens at positions [pos0, pos0+T) of sequence slot 0,
+ * host buffers: q [T][H*D], k/v [T][HK*D], ao [T][H*D]. Same result as T
+ * calls of pickle_cuda_attn_decode (the reference runs prefill token by
+ * token, src/pickle_fast.c:1881), computed as one batched causal kernel.
+ * `precision` selects PICKLE_CUDA_PREFILL_F32 (CUDA-core, FP32 parity) or
+ * PICKLE_CUDA_PREFILL_BF16 (tensor cores, BF16 operands, F32 accumulate). */
+#define PICKLE_CUDA_PREFILL_F32  0
+#define PICKLE_CUDA_PREFILL_BF16 1
+PICKLE_CUDA_API int  pickle_cuda_attn_prefill(pickle_cuda_t* h, int layer, size_t pos0, size_t T,
+                              const float* q, const float* k, const float* v,
+                              float* ao, int precision);
+
+/* Batched decode over device buffers on `stream` (a cudaStream_t, NULL =
+ * legacy default stream). All n_seqs sequences decode at the same `pos`:
+ *   q  [n_seqs][H][D], k/v [n_seqs][HK][D] (pre-RoPE), ao [n_seqs][H][D].
+ * Asynchronous: returns after the launch; errors of the launch itself are
+ * returned, device-side wait timeouts are reported by pickle_cuda_sync. */
+PICKLE_CUDA_API int  pickle_cuda_decode_batch_dev(pickle_cuda_t* h, int layer, int n_seqs, size_t pos,
+                                  const float* q, const float* k, const float* v,
+                                  float* ao, void* stream);
+
+/* Batched causal prefill over device buffers on `stream`, positions
+ * [pos0, pos0+T) of each of n_seqs sequences:
+ *   q [n_seqs][T][H][D], k/v [n_seqs][T][HK][D] (pre-RoPE, F32),
+ *   ao [n_seqs][T][H][D] (F32). The rotated k and v are written to the
+ *   device cache for later decode. */
+PICKLE_CUDA_API int  pickle_cuda_prefill_dev(pickle_cuda_t* h, int layer, int n_seqs, size_t pos0, size_t T,
+                             const float* q, const float* k, const float* v,
+                             float* ao, int precision, void* stream);
+
+/* Partial decode for sequence-chunk sharding: the n_seqs queries at
+ * absolute position `pos` (RoPE row) attend over the `n_local` cache rows
+ * [0, n_local) this handle holds for each sequence; when append != 0 the
+ * new (rotated) k/v are first stored at local row n_local and attended as
+ * well. Writes, per (seq, head), the unnormalised triple
+ *   m = max score, l = sum exp(s - m), acc[D] = sum exp(s - m) v
+ * into m_out/l_out [n_seqs][H] and acc_out [n_seqs][H][D]. Merge the
+ * triples of all shards with pickle_cuda_lse_merge_dev. */
+PICKLE_CUDA_API int  pickle_cuda_decode_partial_dev(pickle_cuda_t* h, int layer, int n_seqs, size_t pos,
+                                    size_t n_local, int append,
+                                    const float* q, const float* k, const float* v,
+                                    float* m_out, float* l_out, float* acc_out, void* stream);
+
+/* Log-sum-exp merge of n_parts partial triples laid out
+ * [n_parts][n_rows] (m, l) and [n_parts][n_rows][D] (acc):
+ *   M = max_i m_i,  o = sum_i e^(m_i - M) acc_i / sum_i e^(m_i - M) l_i. */
+PICKLE_CUDA_API int  pickle_cuda_lse_merge_dev(int n_parts, int n_rows, int head_dim,
+                               const float* m_in, const float* l_in, const float* acc_in,
+                               float* out, void* stream);
+
+/* Copy host K/V rows in pickle's own layout [n_pos][HK][D] (already
+ * rotated, as the host cache holds them) into the device cache at
+ * positions [pos0, pos0+n_pos) of (layer, seq). Lets a caller import a
+ * host pickle_fast_kv_t. */
+PICKLE_CUDA_API int  pickle_cuda_kv_write(pickle_cuda_t* h, int layer, int seq, size_t pos0, size_t n_pos,
+                          const float* k_host, const float* v_host);
+
+/* Device addresses of layer `layer`'s cache, for callers that fill or
+ * inspect it with their own kernels; *seq_stride, *head_stride are in
+ * floats (row stride is head_dim). */
+PICKLE_CUDA_API int  pickle_cuda_kv_layout(pickle_cuda_t* h, int layer, float** k_dev, float** v_dev,
+                           size_t* seq_stride, size_t* head_stride);
+
+/* Wait for all work on `stream` and report device-side errors (a bounded
+ * wait that gave up) recorded since the last call. */
+PICKLE_CUDA_API int  pickle_cuda_sync(pickle_cuda_t* h, void* stream);
+
+/* Number of KV splits the decode launch uses for (n_seqs, pos) on this
+ * handle, and how many kernels it launches (1: split-combine is fused). */
+PICKLE_CUDA_API int  pickle_cuda_decode_plan(pickle_cuda_t* h, int n_seqs, size_t pos, int* n_splits,
+                             int* n_launches);
+
+/* Last CUDA error string seen by this handle (never NULL). */
+PICKLE_CUDA_API const char* pickle_cuda_last_error(pickle_cuda_t* h);
+
+PICKLE_CUDA_API int  pickle_cuda_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PICKLE_CUDA_H */

@@ -1,0 +1,7 @@
+"""B200-native GQA attention block for pickle (lee-muriithi-kingori/lestramanika).
+
+The product is libpickle_cuda.so (C ABI: include/pickle_cuda.h) built from
+lestramanika_b200/csrc for sm_100a; this package loads it (api), shards it
+across GPUs (dist) and holds the pickle_fast.c integration hook (hook/).
+"""
+from .api import PickleCuda, PickleError, lse_merge_dev, abi_version, lib, PREFILL_F32, PREFILL_BF16  # noqa: F401

@@ -1,0 +1,231 @@
+"""Python mirror of the C ABI in include/pickle_cuda.h (ctypes).
+
+The attention block of pickle's forward pass
+(lee-muriithi-kingori/lestramanika src/pickle_fast.c:1910-2109) runs in
+libpickle_cuda.so; this module only loads it, declares the signatures and
+turns pickle's negative status codes (src/pickle.h:52-60) into exceptions.
+There is no fallback: if the library is missing, every call raises.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libpickle_cuda.so")
+
+PICKLE_OK = 0
+ERROR_NAMES = {
+    -1: "PICKLE_ERR_FORMAT", -2: "PICKLE_ERR_VERSION", -3: "PICKLE_ERR_MEMORY",
+    -4: "PICKLE_ERR_TYPE", -5: "PICKLE_ERR_IO", -6: "PICKLE_ERR_ARG",
+    -7: "PICKLE_ERR_RANGE", -8: "PICKLE_ERR_ARCH", -9: "PICKLE_ERR_DEVICE",
+}
+PREFILL_F32 = 0
+PREFILL_BF16 = 1
+
+
+class PickleError(RuntimeError):
+    """A negative PICKLE_ERR_* status from the library."""
+
+    def __init__(self, code, what="", detail=""):
+        self.code = code
+        name = ERROR_NAMES.get(code, str(code))
+        super().__init__(f"{what}: {name}" + (f" ({detail})" if detail else ""))
+
+
+class Params(ctypes.Structure):
+    _fields_ = [
+        ("n_layers", ctypes.c_int), ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int),
+        ("head_dim", ctypes.c_int), ("max_seq", ctypes.c_int), ("half", ctypes.c_int),
+        ("rope_inv_freq", ctypes.POINTER(ctypes.c_float)), ("rope_theta", ctypes.c_float),
+        ("n_seqs", ctypes.c_int), ("rope_len", ctypes.c_int),
+    ]
+
+
+_lib = None
+_vp, _fp, _i, _sz = ctypes.c_void_p, ctypes.POINTER(ctypes.c_float), ctypes.c_int, ctypes.c_size_t
+
+SIGNATURES = {
+    "pickle_cuda_abi_version": ([], _i),
+    "pickle_cuda_init": ([ctypes.POINTER(Params), _i, ctypes.POINTER(_vp)], _i),
+    "pickle_cuda_free": ([_vp], None),
+    "pickle_cuda_attn_decode": ([_vp, _i, _sz, _fp, _fp, _fp, _fp], _i),
+    "pickle_cuda_attn_prefill": ([_vp, _i, _sz, _sz, _fp, _fp, _fp, _fp, _i], _i),
+    "pickle_cuda_decode_batch_dev": ([_vp, _i, _i, _sz, _vp, _vp, _vp, _vp, _vp], _i),
+    "pickle_cuda_prefill_dev": ([_vp, _i, _i, _sz, _sz, _vp, _vp, _vp, _vp, _i, _vp], _i),
+    "pickle_cuda_decode_partial_dev": ([_vp, _i, _i, _sz, _sz, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp], _i),
+    "pickle_cuda_lse_merge_dev": ([_i, _i, _i, _vp, _vp, _vp, _vp, _vp], _i),
+    "pickle_cuda_kv_write": ([_vp, _i, _i, _sz, _sz, _fp, _fp], _i),
+    "pickle_cuda_kv_layout": ([_vp, _i, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
+                               ctypes.POINTER(_sz), ctypes.POINTER(_sz)], _i),
+    "pickle_cuda_sync": ([_vp, _vp], _i),
+    "pickle_cuda_decode_plan": ([_vp, _i, _sz, ctypes.POINTER(_i), ctypes.POINTER(_i)], _i),
+    "pickle_cuda_last_error": ([_vp], ctypes.c_char_p),
+}
+
+
+def lib():
+    """Load libpickle_cuda.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is not built; run `python -m lestramanika_b200.build`")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (args, res) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def _f32(a):
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    return a, a.ctypes.data_as(_fp)
+
+
+def _ptr(t):
+    """Device address of a torch tensor (or an int address, or None)."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+def _stream(s):
+    if s is None:
+        return None
+    if isinstance(s, int):
+        return s
+    return s.cuda_stream
+
+
+class _DevArray:
+    """Exposes a device address as __cuda_array_interface__ for torch.as_tensor."""
+
+    def __init__(self, ptr, shape, owner):
+        self.__cuda_array_interface__ = {
+            "shape": tuple(shape), "typestr": "<f4", "data": (ptr, False), "version": 3, "strides": None,
+        }
+        self._owner = owner
+
+
+class PickleCuda:
+    """One device KV cache + RoPE tables for a model's attention block.
+
+    Mirrors pickle_cuda_t: the dimensions are those of
+    pickle_fast_state_t (src/pickle_fast.h:55-123).
+    """
+
+    def __init__(self, n_layers, n_heads, n_kv_heads, head_dim, max_seq, *, half=None,
+                 rope_inv_freq=None, rope_theta=10000.0, n_seqs=1, rope_len=0, device=0):
+        self.n_layers, self.H, self.HK, self.D = n_layers, n_heads, n_kv_heads, head_dim
+        self.max_seq, self.n_seqs, self.device = max_seq, n_seqs, device
+        self.half = min(head_dim // 2, 64) if half is None else half
+        self.rope_len = rope_len if rope_len else max_seq
+        p = Params(n_layers, n_heads, n_kv_heads, head_dim, max_seq, self.half, None,
+                   float(rope_theta), n_seqs, rope_len)
+        if rope_inv_freq is not None:
+            self._inv, p.rope_inv_freq = _f32(rope_inv_freq)
+        h = _vp()
+        rc = lib().pickle_cuda_init(ctypes.byref(p), device, ctypes.byref(h))
+        if rc != PICKLE_OK:
+            raise PickleError(rc, "pickle_cuda_init")
+        self._h = h
+
+    # -- helpers ---------------------------------------------------------
+    def _check(self, rc, what):
+        if rc != PICKLE_OK:
+            msg = lib().pickle_cuda_last_error(self._h)
+            raise PickleError(rc, what, msg.decode() if msg else "")
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().pickle_cuda_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- host-buffer entry points (what pickle_fast_forward calls) -------
+    def attn_decode(self, layer, pos, q, k, v):
+        q, qp = _f32(q)
+        k, kp = _f32(k)
+        v, vp = _f32(v)
+        ao = np.empty(self.H * self.D, np.float32)
+        self._check(lib().pickle_cuda_attn_decode(self._h, layer, pos, qp, kp, vp, ao.ctypes.data_as(_fp)),
+                    "pickle_cuda_attn_decode")
+        return ao
+
+    def attn_prefill(self, layer, pos0, q, k, v, precision=PREFILL_F32):
+        q, qp = _f32(q)
+        k, kp = _f32(k)
+        v, vp = _f32(v)
+        T = q.size // (self.H * self.D)
+        ao = np.empty((T, self.H * self.D), np.float32)
+        self._check(lib().pickle_cuda_attn_prefill(self._h, layer, pos0, T, qp, kp, vp,
+                                                   ao.ctypes.data_as(_fp), precision),
+                    "pickle_cuda_attn_prefill")
+        return ao
+
+    def kv_write(self, layer, seq, pos0, k_rows, v_rows):
+        k_rows, kp = _f32(k_rows)
+        v_rows, vp = _f32(v_rows)
+        n = k_rows.size // (self.HK * self.D)
+        self._check(lib().pickle_cuda_kv_write(self._h, layer, seq, pos0, n, kp, vp), "pickle_cuda_kv_write")
+
+    # -- device-buffer entry points (torch tensors / addresses) ----------
+    def decode_batch_dev(self, layer, n_seqs, pos, q, k, v, ao, stream=None):
+        self._check(lib().pickle_cuda_decode_batch_dev(self._h, layer, n_seqs, pos, _ptr(q), _ptr(k), _ptr(v),
+                                                       _ptr(ao), _stream(stream)),
+                    "pickle_cuda_decode_batch_dev")
+
+    def prefill_dev(self, layer, n_seqs, pos0, T, q, k, v, ao, precision=PREFILL_F32, stream=None):
+        self._check(lib().pickle_cuda_prefill_dev(self._h, layer, n_seqs, pos0, T, _ptr(q), _ptr(k), _ptr(v),
+                                                  _ptr(ao), precision, _stream(stream)),
+                    "pickle_cuda_prefill_dev")
+
+    def decode_partial_dev(self, layer, n_seqs, pos, n_local, append, q, k, v, m, l, acc, stream=None):
+        self._check(lib().pickle_cuda_decode_partial_dev(self._h, layer, n_seqs, pos, n_local, int(bool(append)),
+                                                         _ptr(q), _ptr(k), _ptr(v), _ptr(m), _ptr(l), _ptr(acc),
+                                                         _stream(stream)),
+                    "pickle_cuda_decode_partial_dev")
+
+    def sync(self, stream=None):
+        self._check(lib().pickle_cuda_sync(self._h, _stream(stream)), "pickle_cuda_sync")
+
+    def decode_plan(self, n_seqs, pos):
+        s, n = ctypes.c_int(), ctypes.c_int()
+        self._check(lib().pickle_cuda_decode_plan(self._h, n_seqs, pos, ctypes.byref(s), ctypes.byref(n)),
+                    "pickle_cuda_decode_plan")
+        return s.value, n.value
+
+    def kv_layout(self, layer):
+        k, v, ss, hs = _vp(), _vp(), _sz(), _sz()
+        self._check(lib().pickle_cuda_kv_layout(self._h, layer, ctypes.byref(k), ctypes.byref(v),
+                                                ctypes.byref(ss), ctypes.byref(hs)), "pickle_cuda_kv_layout")
+        return k.value, v.value, ss.value, hs.value
+
+    def kv_tensors(self, layer):
+        """Torch views [n_seqs][HK][max_seq][D] of layer `layer`'s K and V cache."""
+        import torch
+        k, v, _, _ = self.kv_layout(layer)
+        shape = (self.n_seqs, self.HK, self.max_seq, self.D)
+        dev = torch.device("cuda", self.device)
+        return (torch.as_tensor(_DevArray(k, shape, self), device=dev),
+                torch.as_tensor(_DevArray(v, shape, self), device=dev))
+
+
+def lse_merge_dev(n_parts, n_rows, head_dim, m, l, acc, out, stream=None):
+    rc = lib().pickle_cuda_lse_merge_dev(n_parts, n_rows, head_dim, _ptr(m), _ptr(l), _ptr(acc), _ptr(out),
+                                         _stream(stream))
+    if rc != PICKLE_OK:
+        raise PickleError(rc, "pickle_cuda_lse_merge_dev")
+
+
+def abi_version():
+    return lib().pickle_cuda_abi_version()

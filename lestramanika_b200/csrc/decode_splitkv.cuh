@@ -1,0 +1,480 @@
+// decode_splitkv.cuh - split-KV flash-decoding for pickle's GQA attention
+// block on sm_100a (RoPE + KV append + attention + split combine in one
+// launch).
+//
+// Replaces lee-muriithi-kingori/lestramanika src/pickle_fast.c:1910-2094
+// for decode: RoPE on q and the new k (:1913-1936), the cache append
+// (:1939-1944), scores scaled by 1/sqrtf(D) (:1958-2032), softmax
+// (:2034-2044) and the weighted sum of V (:2046-2091), for every query
+// head h with kv_head = h * HK / H (:1963).
+//
+// Work decomposition. One CTA owns (split, kv_head, query z) and streams a
+// contiguous run of cache rows of that KV head: in the head-major layout
+// [seq][kv_head][pos][D] the run is one contiguous byte range, so each tile
+// of TP=32 rows of K (and of V) is a single 1-D bulk TMA copy into a
+// STAGES-deep shared-memory ring guarded by mbarriers. One producer lane
+// issues the copies; G consumer warps (G = H / HK query heads share each
+// KV head, so K/V are read from HBM once per KV head, not once per query
+// head as the reference's loop does) each take 32/G rows of every tile.
+// A lane holds a float4 slice of every query head in registers, the
+// per-row partial dots of all (row, head) pairs of the warp are summed by
+// a 5-level reduce-scatter (31 shuffles for 32 dot products), the online
+// softmax keeps a running (max, sum) per head and rescales the float4
+// accumulators, and P.V reuses the same float4 slices of V.
+//
+// The new token's row (RoPE'd k, v) is stored to the cache and attended
+// from shared memory by the CTA of the last split, so no CTA ever reads a
+// row another CTA of the same launch writes. Splits are merged by the last
+// CTA of each (kv_head, z) to finish (atomic ticket on a per-group
+// counter, reset by that CTA), so a decode step is one launch.
+#pragma once
+#include <cfloat>
+#include <cmath>
+#include "pcu_common.cuh"
+
+struct DecodeArgs {
+    const float* q;          // [n_z][H][D], z = seq * n_q + t
+    const float* k_new;      // [n_seqs][HK][D] (append)
+    const float* v_new;
+    float* kc;               // this layer's K cache
+    float* vc;
+    long long seq_stride;    // floats between sequences in the cache
+    long long head_stride;   // floats between KV heads (= max_seq * D)
+    const float* sin_tab;    // [max_seq][half]
+    const float* cos_tab;
+    int H, HK, half;
+    int n_q;                 // queries per sequence in this launch
+    long long q_pos0;        // absolute position of query t = 0 (RoPE row)
+    int rope;                // rotate q and k_new with the table row at the query position
+    int append;              // store + attend the new k/v row
+    long long append_idx;    // cache row of the new token
+    long long hist_len0;     // cached rows [0, hist) attended by query t = 0
+    int hist_step;           // query t attends hist_len0 + t * hist_step rows
+    int n_splits;
+    long long chunk;         // history rows per split
+    float scale;             // 1 / sqrtf(D)
+    int out_mode;            // 0: ao = normalised output; 1: unnormalised (m, l, acc)
+    float* ao;               // [n_z][H][D]
+    float* out_m;            // [n_z][H] (out_mode 1)
+    float* out_l;
+    float* ws_m;             // [n_groups][G][n_splits]
+    float* ws_l;
+    float* ws_acc;           // [n_groups][G][n_splits][D]
+    unsigned* counters;      // [n_groups], zero between launches
+    int* err;
+};
+
+constexpr int kMaxSplits = 256;
+
+template <int D, int G>
+struct DecodeCfg {
+    static constexpr int NW = G;                  // consumer warps
+    static constexpr int RPW = 32 / G;            // rows per warp per tile
+    static constexpr int TP = 32;                 // rows per tile
+    static constexpr int NCH = D / 4;             // float4 chunks per row
+    static constexpr int CPL = (NCH + 31) / 32;   // chunks per lane
+    static constexpr int ROW_BYTES = D * 4;
+    static constexpr int TILE_BYTES = TP * ROW_BYTES;
+    static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+    static constexpr int STAGES_RAW = 98304 / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
+    static constexpr int THREADS = (NW + 1) * 32;
+    static constexpr size_t RING_BYTES = (size_t)STAGES * STAGE_BYTES;
+    static constexpr size_t NEWROW_OFF = RING_BYTES;
+    static constexpr size_t PBUF_OFF = NEWROW_OFF + 2 * ROW_BYTES;
+    static constexpr size_t BAR_OFF = (PBUF_OFF + NW * 32 * 4 + 15) / 16 * 16;
+    static constexpr size_t SMEM = BAR_OFF + 2 * STAGES * 8;
+    // Epilogue scratch (reuses the ring): per-warp acc, m, l, then split weights.
+    static constexpr size_t EPI_BYTES = (size_t)NW * G * D * 4 + 2 * NW * G * 4 + 2 * G * 4 +
+                                        (size_t)G * kMaxSplits * 4;
+    static_assert(D % 4 == 0, "rows must be 16-byte multiples");
+    static_assert(32 % G == 0 && G <= 8, "G in {1, 2, 4, 8}");
+    static_assert(EPI_BYTES <= RING_BYTES, "epilogue scratch must fit in the ring");
+};
+
+// NeoX rotation of element d of a head row x (src/pickle_fast.c:1917-1924).
+PCU_DEV float rope_elem(const float* x, int d, int half, const float* sr, const float* cr) {
+    if (d < half) {
+        const float lo = x[d], hi = x[d + half];
+        return cr[d] * lo - sr[d] * hi;
+    }
+    if (d < 2 * half) {
+        const int i = d - half;
+        const float lo = x[i], hi = x[d];
+        return sr[i] * lo + cr[i] * hi;
+    }
+    return x[d];
+}
+
+// One reduce-scatter level: lanes exchange the half of their W+W values
+// they do not keep; afterwards v[0..W) hold sums over lane pairs (l, l^W).
+template <int W>
+PCU_DEV void rs_level(float (&v)[32], int lane) {
+    const bool up = (lane & W) != 0;
+    #pragma unroll
+    for (int i = 0; i < W; ++i) {
+        const float send = up ? v[i] : v[i + W];
+        const float keep = up ? v[i + W] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, W);
+    }
+}
+
+// After this, lane l holds the warp-wide sum of value index l.
+PCU_DEV float reduce_scatter32(float (&v)[32], int lane) {
+    rs_level<16>(v, lane);
+    rs_level<8>(v, lane);
+    rs_level<4>(v, lane);
+    rs_level<2>(v, lane);
+    rs_level<1>(v, lane);
+    return v[0];
+}
+
+// One warp attends `nvalid` (1..RPW) consecutive rows at Kw/Vw (shared
+// memory, row stride D) and folds them into its running softmax state.
+template <int D, int G>
+PCU_DEV void attend_rows(const float* __restrict__ Kw, const float* __restrict__ Vw, int nvalid,
+                         const float4 (&qr)[G][DecodeCfg<D, G>::CPL],
+                         float4 (&acc)[G][DecodeCfg<D, G>::CPL], float& m_run, float& l_run,
+                         float* pw, float scale, int lane) {
+    using C = DecodeCfg<D, G>;
+    float vals[32];
+    #pragma unroll
+    for (int r = 0; r < C::RPW; ++r) {
+        float4 kr[C::CPL];
+        #pragma unroll
+        for (int i = 0; i < C::CPL; ++i) {
+            const int c = lane + 32 * i;
+            kr[i] = (r < nvalid && c < C::NCH) ? reinterpret_cast<const float4*>(Kw + r * D)[c]
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        #pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float s = 0.f;
+            #pragma unroll
+            for (int i = 0; i < C::CPL; ++i) {
+                s = fmaf(qr[g][i].x, kr[i].x, s);
+                s = fmaf(qr[g][i].y, kr[i].y, s);
+                s = fmaf(qr[g][i].z, kr[i].z, s);
+                s = fmaf(qr[g][i].w, kr[i].w, s);
+            }
+            vals[r * G + g] = s;
+        }
+    }
+    float s = reduce_scatter32(vals, lane);          // lane l: row l / G, head l % G
+    s = (lane / G < nvalid) ? s * scale : -INFINITY;
+    float tmax = s;
+    #pragma unroll
+    for (int m = G; m < 32; m <<= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, m));
+    const float m_new = fmaxf(m_run, tmax);
+    const float p = expf(s - m_new);
+    const float alpha = expf(m_run - m_new);
+    float psum = p;
+    #pragma unroll
+    for (int m = G; m < 32; m <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, m);
+    l_run = l_run * alpha + psum;
+    m_run = m_new;
+    #pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float ag = __shfl_sync(0xffffffffu, alpha, g);
+        #pragma unroll
+        for (int i = 0; i < C::CPL; ++i) {
+            acc[g][i].x *= ag; acc[g][i].y *= ag; acc[g][i].z *= ag; acc[g][i].w *= ag;
+        }
+    }
+    pw[lane] = p;
+    __syncwarp();
+    #pragma unroll
+    for (int r = 0; r < C::RPW; ++r) {
+        if (r < nvalid) {
+            float pr[G];
+            #pragma unroll
+            for (int g = 0; g < G; ++g) pr[g] = pw[r * G + g];
+            #pragma unroll
+            for (int i = 0; i < C::CPL; ++i) {
+                const int c = lane + 32 * i;
+                if (c < C::NCH) {
+                    const float4 vv = reinterpret_cast<const float4*>(Vw + r * D)[c];
+                    #pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        acc[g][i].x = fmaf(pr[g], vv.x, acc[g][i].x);
+                        acc[g][i].y = fmaf(pr[g], vv.y, acc[g][i].y);
+                        acc[g][i].z = fmaf(pr[g], vv.z, acc[g][i].z);
+                        acc[g][i].w = fmaf(pr[g], vv.w, acc[g][i].w);
+                    }
+                }
+            }
+        }
+    }
+    __syncwarp();
+}
+
+template <int D, int G>
+__global__ void __launch_bounds__(DecodeCfg<D, G>::THREADS)
+decode_splitkv_kernel(const DecodeArgs a) {
+    using C = DecodeCfg<D, G>;
+    extern __shared__ __align__(128) unsigned char smem[];
+    float* ring = reinterpret_cast<float*>(smem);
+    float* newK = reinterpret_cast<float*>(smem + C::NEWROW_OFF);
+    float* newV = newK + D;
+    float* pbuf = reinterpret_cast<float*>(smem + C::PBUF_OFF);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+    uint64_t* empty = full + C::STAGES;
+    __shared__ int s_abort, s_last, s_issued;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int split = blockIdx.x, kvh = blockIdx.y, z = blockIdx.z;
+    const int seq = z / a.n_q, t = z % a.n_q;
+    const long long hist = a.hist_len0 + (long long)t * a.hist_step;
+    const long long row0 = (long long)split * a.chunk;
+    long long row1 = row0 + a.chunk;
+    if (row1 > hist) row1 = hist;
+    const int n_rows = row1 > row0 ? (int)(row1 - row0) : 0;
+    const bool do_append = a.append && split == a.n_splits - 1;
+    const long long qpos = a.q_pos0 + t;
+    const size_t head_off = (size_t)seq * a.seq_stride + (size_t)kvh * a.head_stride;
+    const float* kbase = a.kc + head_off + (size_t)row0 * D;
+    const float* vbase = a.vc + head_off + (size_t)row0 * D;
+    const int n_tiles = (n_rows + C::TP - 1) / C::TP;
+    const float* sr = a.sin_tab + (size_t)qpos * a.half;
+    const float* cr = a.cos_tab + (size_t)qpos * a.half;
+
+    if (tid == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], C::NW);
+        }
+        mbar_fence_init();
+        s_abort = 0;
+        s_last = 0;
+        s_issued = 0;
+    }
+    if (do_append) {
+        const float* kn = a.k_new + ((size_t)seq * a.HK + kvh) * D;
+        const float* vn = a.v_new + ((size_t)seq * a.HK + kvh) * D;
+        float* kdst = a.kc + head_off + (size_t)a.append_idx * D;
+        float* vdst = a.vc + head_off + (size_t)a.append_idx * D;
+        for (int d = tid; d < D; d += C::THREADS) {
+            const float kk = a.rope ? rope_elem(kn, d, a.half, sr, cr) : kn[d];
+            const float vv = vn[d];
+            newK[d] = kk;
+            newV[d] = vv;
+            kdst[d] = kk;
+            vdst[d] = vv;
+        }
+    }
+    __syncthreads();
+
+    float4 acc[G][C::CPL];
+    float m_run = -INFINITY, l_run = 0.f;
+
+    if (warp == C::NW) {
+        // Producer: one lane streams the K/V tiles of this split.
+        if (lane == 0) {
+            int issued = 0;
+            for (int it = 0; it < n_tiles; ++it) {
+                const int s = it % C::STAGES;
+                if (it >= C::STAGES && !mbar_wait(&empty[s], ((it / C::STAGES) - 1) & 1)) {
+                    record_error(a.err, PCU_DEVERR_EMPTY_WAIT);
+                    s_abort = 1;
+                    break;
+                }
+                if (*(volatile int*)&s_abort) break;
+                const int rows = min(C::TP, n_rows - it * C::TP);
+                const uint32_t bytes = (uint32_t)rows * C::ROW_BYTES;
+                float* ks = ring + (size_t)s * (C::STAGE_BYTES / 4);
+                float* vs = ks + C::TILE_BYTES / 4;
+                mbar_arrive_expect_tx(&full[s], 2u * bytes);
+                bulk_g2s(ks, kbase + (size_t)it * C::TP * D, bytes, &full[s]);
+                bulk_g2s(vs, vbase + (size_t)it * C::TP * D, bytes, &full[s]);
+                issued = it + 1;
+            }
+            s_issued = issued;
+        }
+    } else {
+        // Consumers: rotated query slices of this KV head's G query heads.
+        float4 qr[G][C::CPL];
+        const float* qh0 = a.q + ((size_t)z * a.H + (size_t)kvh * G) * D;
+        #pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float* qh = qh0 + (size_t)g * D;
+            #pragma unroll
+            for (int i = 0; i < C::CPL; ++i) {
+                const int c = lane + 32 * i;
+                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (c < C::NCH) {
+                    if (a.rope) {
+                        x.x = rope_elem(qh, 4 * c + 0, a.half, sr, cr);
+                        x.y = rope_elem(qh, 4 * c + 1, a.half, sr, cr);
+                        x.z = rope_elem(qh, 4 * c + 2, a.half, sr, cr);
+                        x.w = rope_elem(qh, 4 * c + 3, a.half, sr, cr);
+                    } else {
+                        x = reinterpret_cast<const float4*>(qh)[c];
+                    }
+                }
+                qr[g][i] = x;
+                acc[g][i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        float* pw = pbuf + warp * 32;
+        for (int it = 0; it < n_tiles; ++it) {
+            const int s = it % C::STAGES;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (it / C::STAGES) & 1));
+            if (!ok) {
+                if (lane == 0) { record_error(a.err, PCU_DEVERR_FULL_WAIT); s_abort = 1; }
+                break;
+            }
+            const int rows = min(C::TP, n_rows - it * C::TP);
+            const int nvalid = min(max(rows - warp * C::RPW, 0), C::RPW);
+            const float* ks = ring + (size_t)s * (C::STAGE_BYTES / 4);
+            const float* vs = ks + C::TILE_BYTES / 4;
+            if (nvalid > 0)
+                attend_rows<D, G>(ks + warp * C::RPW * D, vs + warp * C::RPW * D, nvalid, qr, acc,
+                                  m_run, l_run, pw, a.scale, lane);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        if (do_append && warp == 0 && !*(volatile int*)&s_abort)
+            attend_rows<D, G>(newK, newV, 1, qr, acc, m_run, l_run, pw, a.scale, lane);
+    }
+    __syncthreads();
+
+    if (s_abort) {
+        // Let the copies still in flight land before the CTA's shared memory goes away.
+        if (tid == 0) {
+            const int issued = s_issued;
+            for (int it = issued > C::STAGES ? issued - C::STAGES : 0; it < issued; ++it)
+                if (!mbar_wait(&full[it % C::STAGES], (it / C::STAGES) & 1))
+                    record_error(a.err, PCU_DEVERR_DRAIN_WAIT);
+        }
+        return;
+    }
+
+    // ---- merge the NW warps of this CTA (scratch reuses the ring) ----
+    float* sm_acc = ring;                               // [NW][G][D]
+    float* sm_m = sm_acc + C::NW * G * D;               // [NW][G]
+    float* sm_l = sm_m + C::NW * G;                     // [NW][G]
+    float* sm_M = sm_l + C::NW * G;                     // [G]
+    float* sm_L = sm_M + G;                             // [G]
+    float* sm_w = sm_L + G;                             // [G][kMaxSplits]
+    if (warp < C::NW) {
+        if (lane < G) {
+            sm_m[warp * G + lane] = m_run;
+            sm_l[warp * G + lane] = l_run;
+        }
+        #pragma unroll
+        for (int g = 0; g < G; ++g)
+            #pragma unroll
+            for (int i = 0; i < C::CPL; ++i) {
+                const int c = lane + 32 * i;
+                if (c < C::NCH) reinterpret_cast<float4*>(sm_acc + (warp * G + g) * D)[c] = acc[g][i];
+            }
+    }
+    __syncthreads();
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int w = 0; w < C::NW; ++w) M = fmaxf(M, sm_m[w * G + tid]);
+        float L = 0.f;
+        for (int w = 0; w < C::NW; ++w) {
+            const float mw = sm_m[w * G + tid];
+            const float e = (mw == -INFINITY) ? 0.f : expf(mw - M);
+            sm_w[tid * C::NW + w] = e;
+            L += sm_l[w * G + tid] * e;
+        }
+        sm_M[tid] = M;
+        sm_L[tid] = L;
+    }
+    __syncthreads();
+
+    const size_t gidx = (size_t)z * a.HK + kvh;
+    if (a.n_splits == 1) {
+        for (int idx = tid; idx < G * C::NCH; idx += C::THREADS) {
+            const int g = idx / C::NCH, c = idx % C::NCH;
+            float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int w = 0; w < C::NW; ++w) {
+                const float e = sm_w[g * C::NW + w];
+                const float4 x = reinterpret_cast<const float4*>(sm_acc + (w * G + g) * D)[c];
+                A.x = fmaf(e, x.x, A.x); A.y = fmaf(e, x.y, A.y);
+                A.z = fmaf(e, x.z, A.z); A.w = fmaf(e, x.w, A.w);
+            }
+            const size_t row = (size_t)z * a.H + (size_t)kvh * G + g;
+            float4* dst = reinterpret_cast<float4*>(a.ao + row * D) + c;
+            if (a.out_mode == 0) {
+                const float L = sm_L[g];
+                const float inv = 1.0f / (L == 0.0f ? 1.0f : L);
+                *dst = make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv);
+            } else {
+                *dst = A;
+                if (c == 0) { a.out_m[row] = sm_M[g]; a.out_l[row] = sm_L[g]; }
+            }
+        }
+        return;
+    }
+
+    // ---- several splits: publish this CTA's partial, last CTA merges ----
+    for (int idx = tid; idx < G * C::NCH; idx += C::THREADS) {
+        const int g = idx / C::NCH, c = idx % C::NCH;
+        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = 0; w < C::NW; ++w) {
+            const float e = sm_w[g * C::NW + w];
+            const float4 x = reinterpret_cast<const float4*>(sm_acc + (w * G + g) * D)[c];
+            A.x = fmaf(e, x.x, A.x); A.y = fmaf(e, x.y, A.y);
+            A.z = fmaf(e, x.z, A.z); A.w = fmaf(e, x.w, A.w);
+        }
+        const size_t prow = (gidx * G + g) * a.n_splits + split;
+        reinterpret_cast<float4*>(a.ws_acc + prow * D)[c] = A;
+        if (c == 0) { a.ws_m[prow] = sm_M[g]; a.ws_l[prow] = sm_L[g]; }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned prev = atomicAdd(&a.counters[gidx], 1u);
+        s_last = (prev == (unsigned)a.n_splits - 1u);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+
+    // Split weights: warp g handles head g.
+    if (warp < G) {
+        const int g = warp;
+        const size_t base = (gidx * G + g) * a.n_splits;
+        float M = -INFINITY;
+        for (int s = lane; s < a.n_splits; s += 32) M = fmaxf(M, __ldcg(a.ws_m + base + s));
+        #pragma unroll
+        for (int m = 16; m > 0; m >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, m));
+        float L = 0.f;
+        for (int s = lane; s < a.n_splits; s += 32) {
+            const float ms = __ldcg(a.ws_m + base + s);
+            const float e = (ms == -INFINITY) ? 0.f : expf(ms - M);
+            sm_w[g * kMaxSplits + s] = e;
+            L += __ldcg(a.ws_l + base + s) * e;
+        }
+        #pragma unroll
+        for (int m = 16; m > 0; m >>= 1) L += __shfl_xor_sync(0xffffffffu, L, m);
+        if (lane == 0) { sm_M[g] = M; sm_L[g] = L; }
+    }
+    __syncthreads();
+    for (int idx = tid; idx < G * C::NCH; idx += C::THREADS) {
+        const int g = idx / C::NCH, c = idx % C::NCH;
+        const float4* src = reinterpret_cast<const float4*>(a.ws_acc + (gidx * G + g) * a.n_splits * D) + c;
+        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+        #pragma unroll 4
+        for (int s = 0; s < a.n_splits; ++s) {
+            const float e = sm_w[g * kMaxSplits + s];
+            const float4 x = __ldcg(src + (size_t)s * C::NCH);
+            A.x = fmaf(e, x.x, A.x); A.y = fmaf(e, x.y, A.y);
+            A.z = fmaf(e, x.z, A.z); A.w = fmaf(e, x.w, A.w);
+        }
+        const size_t row = (size_t)z * a.H + (size_t)kvh * G + g;
+        float4* dst = reinterpret_cast<float4*>(a.ao + row * D) + c;
+        if (a.out_mode == 0) {
+            const float L = sm_L[g];
+            const float inv = 1.0f / (L == 0.0f ? 1.0f : L);
+            *dst = make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv);
+        } else {
+            *dst = A;
+            if (c == 0) { a.out_m[row] = sm_M[g]; a.out_l[row] = sm_L[g]; }
+        }
+    }
+    if (tid == 0) a.counters[gidx] = 0u;
+}

@@ -1,0 +1,88 @@
+// pcu_common.cuh - sm_100a PTX helpers shared by the attention kernels:
+// mbarriers with bounded waits, 1-D bulk (TMA) copies global -> shared,
+// and the device error word.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#define PCU_DEV __device__ __forceinline__
+
+// Device-side error codes written to the handle's error word.
+enum : int {
+    PCU_DEVERR_NONE = 0,
+    PCU_DEVERR_FULL_WAIT = 1,    // consumer gave up waiting for a tile
+    PCU_DEVERR_EMPTY_WAIT = 2,   // producer gave up waiting for a free stage
+    PCU_DEVERR_DRAIN_WAIT = 3,   // copies still in flight at exit after an abort
+    PCU_DEVERR_MMA_WAIT = 4,     // tensor-core completion never arrived
+};
+
+// Every spin on an mbarrier gives up after this long and records an error
+// instead of hanging the GPU.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;   // 1 s
+
+PCU_DEV uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+PCU_DEV uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+PCU_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Make initialised barriers visible to the async (TMA) proxy.
+PCU_DEV void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+PCU_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+PCU_DEV void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+PCU_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for the phase with `parity` to complete; false after kWaitLimitNs.
+PCU_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+        #pragma unroll 1
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+// 1-D bulk copy of `bytes` (multiple of 16, both addresses 16-byte
+// aligned) from global memory into this CTA's shared memory, completing
+// on `bar` as transaction bytes. No multicast.
+PCU_DEV void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+PCU_DEV void record_error(int* err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}

@@ -1,0 +1,115 @@
+#!/usr/bin/env python3
+"""Write the tiny Llama GGUF v3 model used for the end-to-end parity check.
+
+Shape (the reference's CPU-runnable configuration): dim 288, 6 layers,
+6 query heads, 6 KV heads, head_dim 48, FFN hidden 768, vocab 32000,
+max seq 256, RoPE theta 10000, RMSNorm eps 1e-5. Every weight is F32 drawn
+N(0, 0.02) from numpy's Philox generator with the given seed.
+
+The file layout follows the GGUF v3 writer in lee-muriithi-kingori/
+lestramanika tools/make_tiny_gguf.py:56-165 (header, metadata KVs, tensor
+infos, 32-byte aligned data), with two deliberate differences:
+  * dims are written in GGUF order (ne[0] = the contiguous input dim), and
+  * llama.vocab_size is written explicitly, because pickle_arch_detect
+    otherwise falls back to the last dim of token_embd
+    (src/pickle.c:1010-1021).
+The data of a [out][in] weight is row-major with `in` contiguous, which is
+how pickle_fast_matmul_f32 reads it.
+
+Also returns the 16-token prompt (ids uniform in [3, 32000) from the seed).
+"""
+import struct
+import sys
+
+import numpy as np
+
+HIDDEN, N_LAYERS, N_HEADS, N_KV_HEADS, HEAD_DIM = 288, 6, 6, 6, 48
+FFN, VOCAB, CTX, THETA, EPS = 768, 32000, 256, 10000.0, 1e-5
+ALIGN = 32
+GGUF_U32, GGUF_F32, GGUF_BOOL, GGUF_STR = 4, 6, 7, 8
+
+
+def _tensors():
+    t = [("token_embd.weight", (VOCAB, HIDDEN))]
+    for L in range(N_LAYERS):
+        p = f"blk.{L}."
+        t += [
+            (p + "attn_norm.weight", (HIDDEN,)),
+            (p + "attn_q.weight", (N_HEADS * HEAD_DIM, HIDDEN)),
+            (p + "attn_k.weight", (N_KV_HEADS * HEAD_DIM, HIDDEN)),
+            (p + "attn_v.weight", (N_KV_HEADS * HEAD_DIM, HIDDEN)),
+            (p + "attn_output.weight", (HIDDEN, N_HEADS * HEAD_DIM)),
+            (p + "ffn_norm.weight", (HIDDEN,)),
+            (p + "ffn_gate.weight", (FFN, HIDDEN)),
+            (p + "ffn_up.weight", (FFN, HIDDEN)),
+            (p + "ffn_down.weight", (HIDDEN, FFN)),
+        ]
+    t += [("output_norm.weight", (HIDDEN,)), ("output.weight", (VOCAB, HIDDEN))]
+    return t
+
+
+def _s(b):
+    b = b.encode()
+    return struct.pack("<Q", len(b)) + b
+
+
+def write_model(path, seed=0):
+    rng = np.random.Generator(np.random.Philox(seed))
+    meta = [
+        ("general.architecture", GGUF_STR, "llama"),
+        ("general.name", GGUF_STR, "pickle-b200-tiny"),
+        ("llama.block_count", GGUF_U32, N_LAYERS),
+        ("llama.embedding_length", GGUF_U32, HIDDEN),
+        ("llama.feed_forward_length", GGUF_U32, FFN),
+        ("llama.attention.head_count", GGUF_U32, N_HEADS),
+        ("llama.attention.head_count_kv", GGUF_U32, N_KV_HEADS),
+        ("llama.context_length", GGUF_U32, CTX),
+        ("llama.rope.dimension_count", GGUF_U32, HEAD_DIM),
+        ("llama.vocab_size", GGUF_U32, VOCAB),
+        ("llama.attention.layer_norm_rms_epsilon", GGUF_F32, EPS),
+        ("llama.rope.freq_base", GGUF_F32, THETA),
+        ("llama.tie_word_embeddings", GGUF_BOOL, False),
+    ]
+    tensors = _tensors()
+    datas = [rng.standard_normal(int(np.prod(shape)), dtype=np.float32) * np.float32(0.02)
+             for _, shape in tensors]
+    head = bytearray()
+    head += struct.pack("<IIQQ", 0x46554747, 3, len(tensors), len(meta))
+    for key, typ, val in meta:
+        head += _s(key) + struct.pack("<I", typ)
+        if typ == GGUF_STR:
+            head += _s(val)
+        elif typ == GGUF_U32:
+            head += struct.pack("<I", val)
+        elif typ == GGUF_F32:
+            head += struct.pack("<f", val)
+        else:
+            head += struct.pack("<B", 1 if val else 0)
+    off = 0
+    offsets = []
+    for (name, shape), d in zip(tensors, datas):
+        offsets.append(off)
+        off += d.nbytes
+        off += (-off) % ALIGN
+    for (name, shape), o in zip(tensors, offsets):
+        dims = tuple(reversed(shape))          # GGUF: ne[0] is the contiguous dim
+        head += _s(name) + struct.pack("<I", len(dims))
+        head += b"".join(struct.pack("<Q", d) for d in dims)
+        head += struct.pack("<IQ", 0, o)       # GGML_F32, offset
+    head += b"\0" * ((-len(head)) % ALIGN)
+    with open(path, "wb") as f:
+        f.write(head)
+        for d, o in zip(datas, offsets):
+            f.write(d.tobytes())
+            f.write(b"\0" * ((-d.nbytes) % ALIGN))
+    return prompt_ids(seed)
+
+
+def prompt_ids(seed=0, n=16):
+    rng = np.random.Generator(np.random.Philox(seed + 1))
+    return [int(x) for x in rng.integers(3, VOCAB, size=n)]
+
+
+if __name__ == "__main__":
+    out = sys.argv[1] if len(sys.argv) > 1 else "/tmp/pickle_tiny.gguf"
+    print(write_model(out, int(sys.argv[2]) if len(sys.argv) > 2 else 0))

@@ -1,0 +1,92 @@
+"""Batched causal prefill on the GPU against T sequential oracle steps
+(the reference prefills token by token, src/pickle_fast.c:1881)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from gpu_util import BF16_ABS_TOL, assert_rel, normal
+from lestramanika_b200 import PREFILL_BF16, PREFILL_F32, PickleCuda
+
+pytestmark = pytest.mark.gpu
+
+
+def _oracle_prefill(H, HK, D, S, theta, q, k, v, pos0=0, pre=None):
+    o = oracle.OracleAttn(1, H, HK, D, S, theta)
+    if pre is not None:
+        for p, (qq, kk, vv) in enumerate(pre):
+            o.decode(0, p, qq, kk, vv)
+    out = np.stack([o.decode(0, pos0 + t, q[t], k[t], v[t]) for t in range(q.shape[0])])
+    kc, vc = o.cache(0)
+    kc, vc = kc.copy(), vc.copy()
+    o.close()
+    return out, kc, vc
+
+
+@pytest.mark.parametrize("H,HK,D,T", [(6, 6, 48, 37), (8, 2, 128, 70), (32, 8, 128, 129), (16, 2, 64, 33)])
+def test_prefill_f32_host_api(H, HK, D, T):
+    theta = 10000.0
+    q = normal(5, (T, H * D), 1)
+    k = normal(5, (T, HK * D), 2)
+    v = normal(5, (T, HK * D), 3)
+    cu = PickleCuda(1, H, HK, D, T + 8, rope_theta=theta)
+    got = cu.attn_prefill(0, 0, q, k, v, PREFILL_F32)
+    ref, kc, vc = _oracle_prefill(H, HK, D, T + 8, theta, q, k, v)
+    assert_rel(got, ref, what=f"prefill H={H} HK={HK} D={D} T={T}")
+    # decode continues from the cache the prefill wrote
+    qn, kn, vn = normal(6, H * D, 1), normal(6, HK * D, 2), normal(6, HK * D, 3)
+    got_d = cu.attn_decode(0, T, qn, kn, vn)
+    o = oracle.OracleAttn(1, H, HK, D, T + 8, theta)
+    for t in range(T):
+        o.decode(0, t, q[t], k[t], v[t])
+    assert_rel(got_d, o.decode(0, T, qn, kn, vn), what="decode after prefill")
+    o.close()
+    cu.close()
+
+
+def test_prefill_f32_after_history():
+    """Chunked prefill: T tokens at pos0 > 0 attend the earlier cache rows too."""
+    H, HK, D, theta = 8, 2, 128, 10000.0
+    pre = [(normal(8, H * D, p, 1), normal(8, HK * D, p, 2), normal(8, HK * D, p, 3)) for p in range(40)]
+    T = 25
+    q, k, v = normal(9, (T, H * D), 1), normal(9, (T, HK * D), 2), normal(9, (T, HK * D), 3)
+    cu = PickleCuda(1, H, HK, D, 80, rope_theta=theta)
+    for p, (qq, kk, vv) in enumerate(pre):
+        cu.attn_decode(0, p, qq, kk, vv)
+    got = cu.attn_prefill(0, 40, q, k, v, PREFILL_F32)
+    ref, _, _ = _oracle_prefill(H, HK, D, 80, theta, q, k, v, pos0=40, pre=pre)
+    assert_rel(got, ref, what="prefill after 40 rows")
+    cu.close()
+
+
+def test_prefill_batched_dev_writes_cache():
+    B, T, H, HK, D, theta = 3, 50, 8, 8, 128, 10000.0
+    q, k, v = normal(10, (B, T, H, D), 1), normal(10, (B, T, HK, D), 2), normal(10, (B, T, HK, D), 3)
+    cu = PickleCuda(1, H, HK, D, T, rope_theta=theta, n_seqs=B)
+    dev = torch.device("cuda", 0)
+    qd, kd, vd = (torch.from_numpy(x).to(dev) for x in (q, k, v))
+    ao = torch.empty((B, T, H, D), dtype=torch.float32, device=dev)
+    cu.prefill_dev(0, B, 0, T, qd, kd, vd, ao, PREFILL_F32)
+    cu.sync()
+    kt, vt = cu.kv_tensors(0)
+    for b in range(B):
+        ref, kc, vc = _oracle_prefill(H, HK, D, T, theta, q[b].reshape(T, -1), k[b].reshape(T, -1), v[b].reshape(T, -1))
+        assert_rel(ao[b].cpu().numpy().reshape(T, -1), ref, what=f"seq {b}")
+        np.testing.assert_allclose(kt[b].permute(1, 0, 2).cpu().numpy(), kc, atol=1e-5, rtol=0)
+        np.testing.assert_array_equal(vt[b].permute(1, 0, 2).cpu().numpy(), vc)
+    cu.close()
+
+
+@pytest.mark.parametrize("H,HK,T", [(32, 32, 256), (8, 2, 300)])
+def test_prefill_bf16(H, HK, T):
+    """BF16 tensor-core prefill within 2e-2 max-abs of the F32 oracle."""
+    D, theta = 128, 10000.0
+    q = normal(11, (T, H * D), 1)
+    k = normal(11, (T, HK * D), 2)
+    v = normal(11, (T, HK * D), 3)
+    cu = PickleCuda(1, H, HK, D, T, rope_theta=theta)
+    got = cu.attn_prefill(0, 0, q, k, v, PREFILL_BF16)
+    cu.close()
+    ref, _, _ = _oracle_prefill(H, HK, D, T, theta, q, k, v)
+    err = float(np.max(np.abs(got - ref)))
+    assert err <= BF16_ABS_TOL, err
