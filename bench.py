@@ -372,6 +372,23 @@ def run_ours_multi(args, rank, world, local_rank):
     dist.destroy_process_group()
 
 
+ONLY = {"c2b1": (C2_B1, True), "c2b8": (C2_B8, False), "c2b64": (C2_B64, False), "c4": (C4, False),
+        "c5": (C5, False), "c3": (C3, None)}
+
+
+def run_only(args):
+    """One workload, one GPU: the command the ncu summaries under profiles/ were taken with."""
+    torch = _torch()
+    torch.cuda.set_device(0)
+    w, flush = ONLY[args.only]
+    if flush is None:
+        from lestramanika_b200 import PREFILL_BF16
+        line = prefill_line(w, 0, args.steps, args.warmup, PREFILL_BF16)
+    else:
+        line, _ = decode_line(w, 0, args.steps, args.warmup, flush)
+    print(json.dumps({"only": args.only, **line}), flush=True)
+
+
 def run_reference(args, rank):
     if rank != 0:
         return
@@ -427,6 +444,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--only", choices=sorted(ONLY), help="run one workload on one GPU (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -435,6 +453,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.only:
+        run_only(args)
         return
     if world > 1:
         run_ours_multi(args, rank, world, local_rank)

@@ -1,0 +1,246 @@
+"""Multi-GPU decode inside one box: one process per GPU, NCCL over NVLink.
+
+Two sharding strategies for pickle's decode attention (the reference runs on
+one host with OpenMP over heads only, src/pickle_fast.c:1960):
+
+* KV-head-group sharding (HeadShardedDecode). Rank r owns KV heads
+  [r*HK/N, (r+1)*HK/N) and their query heads (kv_head = h*HK/H,
+  src/pickle_fast.c:1963, keeps every query head on the rank of its KV
+  head), i.e. 1/N of the cache. Each rank decodes its heads; the head
+  outputs [B][H/N][D] are all-gathered and laid out as [B][H][D].
+* Sequence-chunk sharding (SeqShardedDecode). Rank r owns cache positions
+  [r*S/N, (r+1)*S/N) of every head; the last rank appends the new token.
+  Each rank computes the unnormalised triple (m, l, acc) of its chunk; the
+  triples are all-gathered and merged by log-sum-exp.
+
+The per-rank compute is a callable so the same orchestration runs with the
+B200 kernels (NCCL, device tensors) and, in the CPU tests, with a CPU
+computation over gloo. All ranks take the same collective steps in the same
+order; process groups are created with a short timeout so a rank that
+stops participating turns into an error on the others instead of a hang.
+"""
+import datetime
+import os
+
+from .workloads import head_shard, seq_shard
+
+
+def init_group(backend, rank, world, timeout_s=60, device=None):
+    """Join the default process group with a bounded collective timeout."""
+    import torch
+    import torch.distributed as dist
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    kw = {"timeout": datetime.timedelta(seconds=timeout_s)}
+    if device is not None:
+        kw["device_id"] = torch.device("cuda", device)
+    dist.init_process_group(backend, rank=rank, world_size=world, **kw)
+
+
+def merge_triples(m, l, acc):
+    """Log-sum-exp merge of gathered partials (torch, any device).
+
+    m, l: [N][rows]; acc: [N][rows][D] ->  out [rows][D] =
+    sum_i e^(m_i - M) acc_i / sum_i e^(m_i - M) l_i,  M = max_i m_i.
+    (The B200 path runs the same formula in lse_merge_kernel.)
+    """
+    import torch
+    M = m.max(dim=0).values
+    w = torch.where(torch.isinf(m) & (m < 0), torch.zeros_like(m), torch.exp(m - M))
+    L = (w * l).sum(dim=0)
+    L = torch.where(L == 0, torch.ones_like(L), L)
+    return (w.unsqueeze(-1) * acc).sum(dim=0) / L.unsqueeze(-1)
+
+
+class HeadShardedDecode:
+    """KV-head-group sharded decode step for one rank.
+
+    compute(q, k, v, out) fills out [B][H/N][D] for this rank's heads;
+    step() returns the all-gathered [B][H][D].
+    """
+
+    def __init__(self, B, H, HK, D, rank, world, compute, device=None, dtype=None):
+        import torch
+        (self.h0, self.h1), (self.k0, self.k1) = head_shard_dims(H, HK, world, rank)
+        self.B, self.H, self.HK, self.D, self.world = B, H, HK, D, world
+        self.compute = compute
+        dev = torch.device("cpu") if device is None else torch.device("cuda", device)
+        dtype = dtype or torch.float32
+        self.local = torch.empty((B, self.h1 - self.h0, D), device=dev, dtype=dtype)
+        # Flat [N*B][H/N][D]: all_gather_into_tensor concatenates along dim 0.
+        self.gathered = torch.empty((world * B, self.h1 - self.h0, D), device=dev, dtype=dtype)
+        self.out = torch.empty((B, H, D), device=dev, dtype=dtype)
+
+    def slice_inputs(self, q, k, v):
+        """This rank's share of full [B][H][D] q and [B][HK][D] k/v."""
+        return (q[:, self.h0:self.h1].contiguous(), k[:, self.k0:self.k1].contiguous(),
+                v[:, self.k0:self.k1].contiguous())
+
+    def step(self, q_local, k_local, v_local):
+        import torch.distributed as dist
+        self.compute(q_local, k_local, v_local, self.local)
+        dist.all_gather_into_tensor(self.gathered, self.local)
+        # [N][B][H/N][D] -> [B][N][H/N][D] = [B][H][D]
+        g = self.gathered.view(self.world, self.B, self.h1 - self.h0, self.D)
+        self.out.view(self.B, self.world, self.h1 - self.h0, self.D).copy_(g.transpose(0, 1))
+        return self.out
+
+
+def head_shard_dims(H, HK, world, rank):
+    if HK % world or H % world:
+        raise ValueError(f"{H} query / {HK} KV heads do not split {world} ways")
+    hk, h = HK // world, H // world
+    return (rank * h, (rank + 1) * h), (rank * hk, (rank + 1) * hk)
+
+
+class SeqShardedDecode:
+    """Sequence-chunk sharded decode step for one rank.
+
+    compute(q, k, v, m, l, acc) fills this rank's partial triple for all B*H
+    rows; merge(m_all, l_all, acc_all, out) merges the gathered [N]-stacked
+    triples (default: merge_triples). step() returns out [B][H][D].
+    """
+
+    def __init__(self, B, H, D, ctx, rank, world, compute, merge=None, device=None):
+        import torch
+        self.p0, self.p1 = seq_shard(ctx, world, rank)
+        self.append = rank == world - 1
+        self.B, self.H, self.D, self.world = B, H, D, world
+        self.compute = compute
+        self.merge = merge
+        dev = torch.device("cpu") if device is None else torch.device("cuda", device)
+        rows = B * H
+        self.m = torch.empty(rows, device=dev)
+        self.l = torch.empty(rows, device=dev)
+        self.acc = torch.empty((rows, D), device=dev)
+        # Flat along dim 0 for all_gather_into_tensor; viewed as [N][rows](...) to merge.
+        self.m_all = torch.empty(world * rows, device=dev)
+        self.l_all = torch.empty(world * rows, device=dev)
+        self.acc_all = torch.empty((world * rows, D), device=dev)
+        self.out = torch.empty((B, H, D), device=dev)
+
+    @property
+    def n_local(self):
+        return self.p1 - self.p0
+
+    def step(self, q, k, v):
+        import torch.distributed as dist
+        self.compute(q, k, v, self.m, self.l, self.acc)
+        dist.all_gather_into_tensor(self.m_all, self.m)
+        dist.all_gather_into_tensor(self.l_all, self.l)
+        dist.all_gather_into_tensor(self.acc_all, self.acc)
+        if self.merge is not None:
+            self.merge(self.m_all, self.l_all, self.acc_all, self.out)
+        else:
+            rows = self.B * self.H
+            self.out.view(-1, self.D).copy_(merge_triples(self.m_all.view(self.world, rows),
+                                                          self.l_all.view(self.world, rows),
+                                                          self.acc_all.view(self.world, rows, self.D)))
+        return self.out
+
+
+# ---------------------------------------------------------------------------
+# B200 benchmarks of the two strategies (called by bench.py under torchrun)
+# ---------------------------------------------------------------------------
+
+def _max_over_ranks(ms, device):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([ms], device=torch.device("cuda", device))
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _timed(fn, steps, warmup, device):
+    import torch
+    import torch.distributed as dist
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    torch.cuda.synchronize(device)
+    st = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        fn()
+    e1.record(st)
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    return _max_over_ranks(e0.elapsed_time(e1) / steps, device)
+
+
+def bench_head_sharded(w, rank, world, device, steps, warmup):
+    import torch
+    from .api import PickleCuda
+    (h0, h1), (k0, k1) = head_shard(w, world, rank)
+    H, HK = h1 - h0, k1 - k0
+    cu = PickleCuda(1, H, HK, w.D, w.ctx + 1, rope_theta=w.theta, n_seqs=w.B, device=device)
+    kt, vt = cu.kv_tensors(0)
+    g = torch.Generator(device=f"cuda:{device}")
+    g.manual_seed(1000 + rank)
+    for b in range(w.B):
+        kt[b, :, :w.ctx].normal_(generator=g)
+        vt[b, :, :w.ctx].normal_(generator=g)
+    dev = torch.device("cuda", device)
+    q = torch.randn((w.B, H, w.D), generator=g, device=dev)
+    k = torch.randn((w.B, HK, w.D), generator=g, device=dev)
+    v = torch.randn((w.B, HK, w.D), generator=g, device=dev)
+    st = torch.cuda.current_stream(device)
+
+    def compute(qq, kk, vv, out):
+        cu.decode_batch_dev(0, w.B, w.ctx, qq, kk, vv, out, st)
+
+    hs = HeadShardedDecode(w.B, w.H, w.HK, w.D, rank, world, compute, device=device)
+    ms = _timed(lambda: hs.step(q, k, v), steps, warmup, device)
+    kernel_ms = _timed(lambda: compute(q, k, v, hs.local), steps, warmup, device)
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    hout = torch.empty(hs.out.shape).pin_memory()
+
+    def e2e_step():
+        q.copy_(hq, non_blocking=True)
+        k.copy_(hk, non_blocking=True)
+        v.copy_(hv, non_blocking=True)
+        hout.copy_(hs.step(q, k, v), non_blocking=True)
+
+    e2e_ms = _timed(e2e_step, steps, warmup, device)
+    cu.sync(st)
+    cu.close()
+    per_gpu = w.kv_bytes / world
+    return {"ms": ms, "kernel_ms": kernel_ms, "kernel_GBps_per_gpu": per_gpu / (kernel_ms * 1e-3) / 1e9,
+            "e2e": {"value": w.kv_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": sum(x.numel() * 4 for x in (hq, hk, hv)),
+                    "d2h_bytes_per_step": hout.numel() * 4, "ms_per_step": e2e_ms}}
+
+
+def bench_seq_sharded(w, rank, world, device, steps, warmup):
+    import torch
+    from .api import PickleCuda, lse_merge_dev
+    p0, p1 = seq_shard(w.ctx, world, rank)
+    n_local = p1 - p0
+    append = rank == world - 1
+    cu = PickleCuda(1, w.H, w.HK, w.D, n_local + 1, rope_theta=w.theta, n_seqs=w.B, rope_len=w.ctx + 1,
+                    device=device)
+    kt, vt = cu.kv_tensors(0)
+    g = torch.Generator(device=f"cuda:{device}")
+    g.manual_seed(2000 + rank)
+    for b in range(w.B):
+        kt[b, :, :n_local].normal_(generator=g)
+        vt[b, :, :n_local].normal_(generator=g)
+    dev = torch.device("cuda", device)
+    g.manual_seed(7)                       # q / new k, v identical on every rank
+    q = torch.randn((w.B, w.H, w.D), generator=g, device=dev)
+    k = torch.randn((w.B, w.HK, w.D), generator=g, device=dev)
+    v = torch.randn((w.B, w.HK, w.D), generator=g, device=dev)
+    st = torch.cuda.current_stream(device)
+
+    def compute(qq, kk, vv, m, l, acc):
+        cu.decode_partial_dev(0, w.B, w.ctx, n_local, append, qq, kk, vv, m, l, acc, st)
+
+    def merge(m_all, l_all, acc_all, out):
+        lse_merge_dev(world, w.B * w.H, w.D, m_all, l_all, acc_all, out, st)
+
+    ss = SeqShardedDecode(w.B, w.H, w.D, w.ctx, rank, world, compute, merge=merge, device=device)
+    ms = _timed(lambda: ss.step(q, k, v), steps, warmup, device)
+    cu.sync(st)
+    cu.close()
+    return {"ms": ms}
