@@ -150,6 +150,26 @@ PICKLE_CUDA_API int  pickle_cuda_lse_merge_dev(int n_parts, int n_rows, int head
                                const float* m_in, const float* l_in, const float* acc_in,
                                float* out, void* stream);
 
+/* Decode without any allocation, for callers that cannot let a library
+ * call cudaMalloc (their device memory comes from their own arena). No
+ * counterpart in the reference. Same computation as
+ * pickle_cuda_decode_batch_dev on caller-owned device buffers: q [n_seqs][H][D],
+ * k/v [n_seqs][HK][D] (pre-RoPE), the head-major cache
+ * k_cache/v_cache [n_seqs][HK][max_seq][D] (row pos is written), RoPE tables
+ * rope_sin/rope_cos [>= pos+1][half] and ao [n_seqs][H][D]; err_flag is an
+ * optional device int that records a bounded wait giving up. Its split-KV
+ * scratch is a fixed 4 MiB device array inside this library, shared by all
+ * calls: calls that overlap on the GPU race, so serialise them on one
+ * stream. n_seqs * n_kv_heads above 4096 is rejected (PICKLE_ERR_RANGE).
+ * Uses the current device; its first call there does a one-time set-up
+ * (looks up the array's address) and should come before any stream capture. */
+PICKLE_CUDA_API int pickle_cuda_decode_noalloc(int n_seqs, int n_heads, int n_kv_heads, int head_dim,
+                                               int half, int max_seq, size_t pos,
+                                               const float* rope_sin, const float* rope_cos,
+                                               const float* q, const float* k, const float* v,
+                                               float* k_cache, float* v_cache, float* ao,
+                                               int* err_flag, void* stream);
+
 /* Copy host K/V rows in pickle's own layout [n_pos][HK][D] (already
  * rotated, as the host cache holds them) into the device cache at
  * positions [pos0, pos0+n_pos) of (layer, seq). Lets a caller import a

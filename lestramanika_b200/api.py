@@ -61,6 +61,8 @@ SIGNATURES = {
     "pickle_cuda_sync": ([_vp, _vp], _i),
     "pickle_cuda_decode_plan": ([_vp, _i, _sz, ctypes.POINTER(_i), ctypes.POINTER(_i)], _i),
     "pickle_cuda_last_error": ([_vp], ctypes.c_char_p),
+    "pickle_cuda_decode_noalloc": ([_i, _i, _i, _i, _i, _i, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                    _vp], _i),
 }
 
 
@@ -225,6 +227,16 @@ def lse_merge_dev(n_parts, n_rows, head_dim, m, l, acc, out, stream=None):
                                          _stream(stream))
     if rc != PICKLE_OK:
         raise PickleError(rc, "pickle_cuda_lse_merge_dev")
+
+
+def decode_noalloc(n_seqs, n_heads, n_kv_heads, head_dim, half, max_seq, pos, rope_sin, rope_cos, q, k, v,
+                   k_cache, v_cache, ao, err_flag=None, stream=None):
+    """pickle_cuda_decode_noalloc on caller-owned device tensors (no allocation inside)."""
+    rc = lib().pickle_cuda_decode_noalloc(n_seqs, n_heads, n_kv_heads, head_dim, half, max_seq, pos,
+                                          _ptr(rope_sin), _ptr(rope_cos), _ptr(q), _ptr(k), _ptr(v),
+                                          _ptr(k_cache), _ptr(v_cache), _ptr(ao), _ptr(err_flag), _stream(stream))
+    if rc != PICKLE_OK:
+        raise PickleError(rc, "pickle_cuda_decode_noalloc")
 
 
 def abi_version():

@@ -38,7 +38,8 @@ def build_lib(force=False, verbose=False):
         return LIB
     cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
            "-Xcompiler", "-fvisibility=hidden", "-I" + os.path.join(ROOT, "include"), "-I" + CSRC,
-           "-DPICKLE_CUDA_BUILD", "-o", LIB + ".tmp", os.path.join(CSRC, "pickle_cuda.cu")]
+           "-DPICKLE_CUDA_BUILD", "-o", LIB + ".tmp", os.path.join(CSRC, "pickle_cuda.cu"),
+           os.path.join(CSRC, "decode_noalloc.cu")]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)
