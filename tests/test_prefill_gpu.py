@@ -90,3 +90,20 @@ def test_prefill_bf16(H, HK, T):
     ref, _, _ = _oracle_prefill(H, HK, D, T, theta, q, k, v)
     err = float(np.max(np.abs(got - ref)))
     assert err <= BF16_ABS_TOL, err
+
+
+def test_prefill_bf16_full_length_subset_of_heads():
+    """Llama-2-7B-shaped prefill length (T=2048, 32 MHA heads) on one sequence:
+    every head runs on the GPU; heads 0, 13 and 31 are checked against the
+    oracle (heads are independent when H == HK)."""
+    H, HK, D, T, theta = 32, 32, 128, 2048, 10000.0
+    q = normal(12, (T, H, D), 1)
+    k = normal(12, (T, HK, D), 2)
+    v = normal(12, (T, HK, D), 3)
+    cu = PickleCuda(1, H, HK, D, T, rope_theta=theta)
+    got = cu.attn_prefill(0, 0, q.reshape(T, -1), k.reshape(T, -1), v.reshape(T, -1), PREFILL_BF16).reshape(T, H, D)
+    cu.close()
+    for h in (0, 13, 31):
+        ref, _, _ = _oracle_prefill(1, 1, D, T, theta, q[:, h], k[:, h], v[:, h])
+        err = float(np.max(np.abs(got[:, h] - ref)))
+        assert err <= BF16_ABS_TOL, (h, err)
