@@ -226,8 +226,11 @@ def decode_line(w, device, steps, warmup, flush_l2):
 
 
 def prefill_line(w, device, steps, warmup, precision):
+    """Causal prefill: the whole pickle_cuda_prefill_dev call (RoPE/cast/KV-cache
+    producer + attention) and, for BF16, the tensor-core attention kernel alone
+    (pickle_cuda_prefill_attn_bf16_dev on BF16 head-major operands)."""
     torch = _torch()
-    from lestramanika_b200 import PickleCuda
+    from lestramanika_b200 import PickleCuda, api
     dev = torch.device("cuda", device)
     cu = PickleCuda(1, w.H, w.HK, w.D, w.T, rope_theta=w.theta, n_seqs=w.B, device=device)
     g = torch.Generator(device=dev)
@@ -237,19 +240,35 @@ def prefill_line(w, device, steps, warmup, precision):
     v = torch.randn((w.B, w.T, w.HK, w.D), generator=g, device=dev)
     ao = torch.empty_like(q)
     st = torch.cuda.current_stream()
-    for _ in range(warmup):
-        cu.prefill_dev(0, w.B, 0, w.T, q, k, v, ao, precision, st)
-    cu.sync(st)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(steps):
-        cu.prefill_dev(0, w.B, 0, w.T, q, k, v, ao, precision, st)
-    e1.record(st)
-    cu.sync(st)
-    ms = e0.elapsed_time(e1) / steps
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        cu.sync(st)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            fn()
+        e1.record(st)
+        cu.sync(st)
+        return e0.elapsed_time(e1) / steps
+
+    ms = timed(lambda: cu.prefill_dev(0, w.B, 0, w.T, q, k, v, ao, precision, st))
+    out = {"workload": w.name, "precision": "bf16-tcgen05" if precision else "f32-cuda-core", "ms": ms,
+           "TFLOPs": w.flops / (ms * 1e-3) / 1e12, "includes": "rope+cast+kv-cache write producer + attention",
+           "flops_per_step": w.flops}
+    if precision:
+        qb = q.transpose(1, 2).contiguous().to(torch.bfloat16)
+        kb = k.transpose(1, 2).contiguous().to(torch.bfloat16)
+        vb = v.transpose(1, 2).contiguous().to(torch.bfloat16)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        ams = timed(lambda: api.prefill_attn_bf16_dev(w.B, w.T, w.H, w.HK, w.D, qb, kb, vb, ao, err, st))
+        out["attn_ms"] = ams
+        out["attn_TFLOPs"] = w.flops / (ams * 1e-3) / 1e12
+        out["producer_ms"] = ms - ams
+        out["producer_GBps"] = w.io_bytes / ((ms - ams) * 1e-3) / 1e9 if ms > ams else None
     cu.close()
-    return {"workload": w.name, "precision": "bf16-tcgen05" if precision else "f32-cuda-core", "ms": ms,
-            "TFLOPs": w.flops / (ms * 1e-3) / 1e12, "includes": "rope+cast+kv-cache write pre-pass"}
+    return out
 
 
 def cpu_baseline(seconds=10.0):
@@ -305,8 +324,9 @@ def run_ours_single(args):
         extras[w.name] = line
     try:
         from lestramanika_b200 import PREFILL_BF16
-        pf = prefill_line(C3, device, max(2, min(args.steps, 5)), max(args.warmup, 3), PREFILL_BF16)
+        pf = prefill_line(C3, device, max(5, min(args.steps, 10)), max(args.warmup, 3), PREFILL_BF16)
         pf["frac_of_measured_bf16"] = pf["TFLOPs"] / bf16
+        pf["attn_frac_of_measured_bf16"] = pf["attn_TFLOPs"] / bf16
         extras["prefill"] = pf
     except Exception as exc:  # reported, not hidden
         extras["prefill"] = {"error": str(exc)[:200]}

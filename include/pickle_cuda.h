@@ -130,6 +130,17 @@ PICKLE_CUDA_API int  pickle_cuda_prefill_dev(pickle_cuda_t* h, int layer, int n_
                              const float* q, const float* k, const float* v,
                              float* ao, int precision, void* stream);
 
+/* Causal attention only, on already rotated BF16 operands in head-major
+ * layout: q [n_seqs][H][T][D], k/v [n_seqs][HK][T][D] (BF16), output
+ * ao [n_seqs][T][H][D] F32; query t attends keys [0, t]. The tensor-core
+ * kernel that pickle_cuda_prefill_dev runs after its RoPE/cast/cache-write
+ * producer, exposed for callers whose activations are already BF16.
+ * head_dim must be 128. err_flag (optional device int) records a device
+ * wait that gave up. */
+PICKLE_CUDA_API int pickle_cuda_prefill_attn_bf16_dev(int n_seqs, int T, int n_heads, int n_kv_heads, int head_dim,
+                                                      const void* q_bf16, const void* k_bf16, const void* v_bf16,
+                                                      float* ao, int* err_flag, void* stream);
+
 /* Partial decode for sequence-chunk sharding: the n_seqs queries at
  * absolute position `pos` (RoPE row) attend over the `n_local` cache rows
  * [0, n_local) this handle holds for each sequence; when append != 0 the

@@ -61,6 +61,7 @@ SIGNATURES = {
     "pickle_cuda_sync": ([_vp, _vp], _i),
     "pickle_cuda_decode_plan": ([_vp, _i, _sz, ctypes.POINTER(_i), ctypes.POINTER(_i)], _i),
     "pickle_cuda_last_error": ([_vp], ctypes.c_char_p),
+    "pickle_cuda_prefill_attn_bf16_dev": ([_i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp], _i),
     "pickle_cuda_decode_noalloc": ([_i, _i, _i, _i, _i, _i, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp], _i),
 }
@@ -227,6 +228,14 @@ def lse_merge_dev(n_parts, n_rows, head_dim, m, l, acc, out, stream=None):
                                          _stream(stream))
     if rc != PICKLE_OK:
         raise PickleError(rc, "pickle_cuda_lse_merge_dev")
+
+
+def prefill_attn_bf16_dev(n_seqs, T, n_heads, n_kv_heads, head_dim, q, k, v, ao, err_flag=None, stream=None):
+    """Causal attention on rotated BF16 head-major q/k/v (tensor cores), F32 output."""
+    rc = lib().pickle_cuda_prefill_attn_bf16_dev(n_seqs, T, n_heads, n_kv_heads, head_dim, _ptr(q), _ptr(k), _ptr(v),
+                                                 _ptr(ao), _ptr(err_flag), _stream(stream))
+    if rc != PICKLE_OK:
+        raise PickleError(rc, "pickle_cuda_prefill_attn_bf16_dev")
 
 
 def decode_noalloc(n_seqs, n_heads, n_kv_heads, head_dim, half, max_seq, pos, rope_sin, rope_cos, q, k, v,

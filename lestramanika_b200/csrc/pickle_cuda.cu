@@ -428,6 +428,21 @@ int pickle_cuda_prefill_dev(pickle_cuda_t* h, int layer, int n_seqs, size_t pos0
     return prefill_launch(h, layer, n_seqs, pos0, T, q, k, v, ao, precision, (cudaStream_t)stream);
 }
 
+int pickle_cuda_prefill_attn_bf16_dev(int n_seqs, int T, int n_heads, int n_kv_heads, int head_dim,
+                                      const void* q_bf16, const void* k_bf16, const void* v_bf16, float* ao,
+                                      int* err_flag, void* stream) {
+    if (n_seqs < 1 || T < 1 || n_heads < 1 || n_kv_heads < 1 || n_heads % n_kv_heads || !q_bf16 || !k_bf16 ||
+        !v_bf16 || !ao)
+        return PICKLE_ERR_ARG;
+    if (!prefill_tc_supported(head_dim, n_heads / n_kv_heads)) return PICKLE_ERR_ARG;
+    char msg[256];
+    int rc = prefill_tc_launch((const __nv_bfloat16*)q_bf16, (const __nv_bfloat16*)k_bf16,
+                               (const __nv_bfloat16*)v_bf16, ao, n_seqs, T, n_heads, n_kv_heads, head_dim,
+                               1.0f / sqrtf((float)head_dim), err_flag, (cudaStream_t)stream, msg, sizeof(msg));
+    if (rc != 0) fprintf(stderr, "pickle_cuda_prefill_attn_bf16_dev: %s\n", msg);
+    return rc == 0 ? PICKLE_OK : (rc == -6 ? PICKLE_ERR_ARG : PICKLE_ERR_DEVICE);
+}
+
 int pickle_cuda_attn_prefill(pickle_cuda_t* h, int layer, size_t pos0, size_t T, const float* q,
                              const float* k, const float* v, float* ao, int precision) {
     int rc = check_layer(h, layer, 1);
@@ -495,6 +510,16 @@ int pickle_cuda_sync(pickle_cuda_t* h, void* stream) {
 
 namespace {
 
+// Vectorised producer when rows split into float4 rotation pairs, scalar otherwise.
+void launch_rope_append(const RopeAppendArgs& ra, int T, int n_seqs, cudaStream_t st) {
+    const bool vec = ra.D % 4 == 0 && ra.half % 4 == 0 &&
+                     ((uintptr_t)ra.q | (uintptr_t)ra.k | (uintptr_t)ra.v) % 16 == 0;
+    if (vec)
+        rope_append_vec_kernel<<<dim3((unsigned)T, (unsigned)n_seqs), 128, 0, st>>>(ra);
+    else
+        rope_append_kernel<<<dim3((unsigned)T, (unsigned)n_seqs), 256, 0, st>>>(ra);
+}
+
 int prefill_launch(pickle_cuda* h, int layer, int n_seqs, size_t pos0, size_t T, const float* q,
                    const float* k, const float* v, float* ao, int precision, cudaStream_t st) {
     const size_t nq = (size_t)n_seqs * T * h->H * h->D;
@@ -516,7 +541,7 @@ int prefill_launch(pickle_cuda* h, int layer, int n_seqs, size_t pos0, size_t T,
         int rc = ensure_scratch(h, nq * sizeof(float));
         if (rc != PICKLE_OK) return rc;
         ra.q_rot = (float*)h->scratch;
-        rope_append_kernel<<<dim3((unsigned)T, (unsigned)n_seqs), 256, 0, st>>>(ra);
+        launch_rope_append(ra, (int)T, n_seqs, st);
         PCU_CHECK(h, cudaGetLastError());
         // Causal attention: query t of each sequence attends rows [0, pos0+t].
         DecodeArgs a = base_args(h, layer);
@@ -541,7 +566,7 @@ int prefill_launch(pickle_cuda* h, int layer, int n_seqs, size_t pos0, size_t T,
     ra.q_bf16 = (__nv_bfloat16*)base;
     ra.k_bf16 = (__nv_bfloat16*)(base + bq);
     ra.v_bf16 = (__nv_bfloat16*)(base + bq + bk);
-    rope_append_kernel<<<dim3((unsigned)T, (unsigned)n_seqs), 256, 0, st>>>(ra);
+    launch_rope_append(ra, (int)T, n_seqs, st);
     PCU_CHECK(h, cudaGetLastError());
     return prefill_tc_launch(ra.q_bf16, ra.k_bf16, ra.v_bf16, ao, n_seqs, (int)T, h->H, h->HK, h->D,
                              1.0f / sqrtf((float)h->D), h->err_dev, st, h->last_error, sizeof(h->last_error));

@@ -64,6 +64,83 @@ __global__ void rope_append_kernel(const RopeAppendArgs a) {
     }
 }
 
+PCU_DEV uint2 pack_bf16x4(float4 x, float scale) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(x.x * scale, x.y * scale);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(x.z * scale, x.w * scale);
+    return make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+}
+
+// Same result as rope_append_kernel with 16-byte accesses: one thread takes a
+// rotation pair of float4 chunks (d..d+3, d+half..d+half+3), an unrotated
+// float4 chunk past 2*half, or a float4 chunk of v. Needs D % 4 == 0 and
+// half % 4 == 0 (checked by the host). One CTA per token.
+__global__ void __launch_bounds__(128) rope_append_vec_kernel(const RopeAppendArgs a) {
+    const int t = blockIdx.x, seq = blockIdx.y;
+    const long long pos = a.pos0 + t;
+    const int D = a.D, half = a.half;
+    const int NP = half / 4, NT = (D - 2 * half) / 4, NU = NP + NT, NC = D / 4;
+    const float4* sr = reinterpret_cast<const float4*>(a.sin_tab + (size_t)pos * half);
+    const float4* cr = reinterpret_cast<const float4*>(a.cos_tab + (size_t)pos * half);
+    const size_t tok = (size_t)seq * a.T + t;
+    const int n_q = a.H * NU, n_k = a.HK * NU, n_v = a.HK * NC;
+    for (int u = threadIdx.x; u < n_q + n_k + n_v; u += blockDim.x) {
+        if (u < n_q + n_k) {
+            const bool is_q = u < n_q;
+            const int uu = is_q ? u : u - n_q;
+            const int h = uu / NU, c = uu % NU;
+            const float* row = is_q ? a.q + (tok * a.H + h) * D : a.k + (tok * a.HK + h) * D;
+            float4 lo_out, hi_out;
+            int d_lo, d_hi = -1;
+            if (c < NP) {
+                d_lo = 4 * c;
+                d_hi = d_lo + half;
+                const float4 x0 = *reinterpret_cast<const float4*>(row + d_lo);
+                const float4 x1 = *reinterpret_cast<const float4*>(row + d_hi);
+                const float4 sv = sr[c], cv = cr[c];
+                // src/pickle_fast.c:1917-1924: x' = c*x0 - s*x1, x'' = s*x0 + c*x1
+                lo_out = make_float4(cv.x * x0.x - sv.x * x1.x, cv.y * x0.y - sv.y * x1.y,
+                                     cv.z * x0.z - sv.z * x1.z, cv.w * x0.w - sv.w * x1.w);
+                hi_out = make_float4(sv.x * x0.x + cv.x * x1.x, sv.y * x0.y + cv.y * x1.y,
+                                     sv.z * x0.z + cv.z * x1.z, sv.w * x0.w + cv.w * x1.w);
+            } else {
+                d_lo = 2 * half + 4 * (c - NP);
+                lo_out = *reinterpret_cast<const float4*>(row + d_lo);
+            }
+            if (is_q) {
+                if (a.q_rot) {
+                    float* dst = a.q_rot + (tok * a.H + h) * D;
+                    *reinterpret_cast<float4*>(dst + d_lo) = lo_out;
+                    if (d_hi >= 0) *reinterpret_cast<float4*>(dst + d_hi) = hi_out;
+                }
+                if (a.q_bf16) {
+                    __nv_bfloat16* dst = a.q_bf16 + (((size_t)seq * a.H + h) * a.T + t) * D;
+                    *reinterpret_cast<uint2*>(dst + d_lo) = pack_bf16x4(lo_out, a.q_prescale);
+                    if (d_hi >= 0) *reinterpret_cast<uint2*>(dst + d_hi) = pack_bf16x4(hi_out, a.q_prescale);
+                }
+            } else {
+                float* dst = a.kc + (size_t)seq * a.seq_stride + (size_t)h * a.head_stride + (size_t)pos * D;
+                *reinterpret_cast<float4*>(dst + d_lo) = lo_out;
+                if (d_hi >= 0) *reinterpret_cast<float4*>(dst + d_hi) = hi_out;
+                if (a.k_bf16) {
+                    __nv_bfloat16* bd = a.k_bf16 + (((size_t)seq * a.HK + h) * a.T + t) * D;
+                    *reinterpret_cast<uint2*>(bd + d_lo) = pack_bf16x4(lo_out, 1.0f);
+                    if (d_hi >= 0) *reinterpret_cast<uint2*>(bd + d_hi) = pack_bf16x4(hi_out, 1.0f);
+                }
+            }
+        } else {
+            const int uu = u - n_q - n_k;
+            const int h = uu / NC, c = uu % NC;
+            const float4 x = *reinterpret_cast<const float4*>(a.v + (tok * a.HK + h) * D + 4 * c);
+            float* dst = a.vc + (size_t)seq * a.seq_stride + (size_t)h * a.head_stride + (size_t)pos * D;
+            *reinterpret_cast<float4*>(dst + 4 * c) = x;
+            if (a.v_bf16) {
+                __nv_bfloat16* bd = a.v_bf16 + (((size_t)seq * a.HK + h) * a.T + t) * D;
+                *reinterpret_cast<uint2*>(bd + 4 * c) = pack_bf16x4(x, 1.0f);
+            }
+        }
+    }
+}
+
 // o = sum_i e^(m_i - M) acc_i / sum_i e^(m_i - M) l_i over n_parts partial
 // triples of n_rows rows; one CTA per row, one thread per element.
 __global__ void lse_merge_kernel(int n_parts, int n_rows, int D, const float* __restrict__ m,

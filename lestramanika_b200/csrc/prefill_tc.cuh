@@ -8,21 +8,27 @@
 // (written by rope_append_kernel), accumulation is F32 in tensor memory,
 // the output is F32.
 //
-// One CTA owns a 128-row query tile of one (sequence, head):
-//   warp 4      one lane loads Q once and K/V tiles (128 keys) into a
+// One CTA owns two 128-row query tiles (A = rows q0..q0+127, B = the next
+// 128) of one (sequence, head); both share every K/V tile.
+//   warp 8      one lane loads Q_A, Q_B once and K/V tiles (128 keys) into a
 //               2-stage ring with 3-D TMA tensor copies (128-byte swizzle,
 //               no multicast);
-//   warp 5      allocates 512 TMEM columns and one lane issues tcgen05.mma:
-//               S_j = Q K_j^T into one of two S buffers (M=N=128, K=D), then
-//               O += P_{j-1} V_{j-1} (A = P from shared memory, B = V read
-//               MN-major), committing to mbarriers;
-//   warps 0-3   the softmax warpgroup: thread r owns query row r, reads its
-//               S row from TMEM (tcgen05.ld), applies the causal mask, keeps
-//               the running max in the log2 domain (rescaling O in TMEM only
-//               when the max grows by more than 2^8), writes P as BF16 into
-//               the swizzled K-major layout the MMA reads, and at the end
-//               normalises its O row and stores it.
-// S_{j+1} is computed by the tensor cores while the softmax works on S_j.
+//   warp 9      allocates 512 TMEM columns - S_A, S_B, O_A, O_B, 128 each -
+//               and one lane issues tcgen05.mma in the order
+//               PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): S_X = Q_X K^T (both
+//               operands in shared memory), O_X += P_X V (P_X read from
+//               TMEM, V read MN-major from shared memory);
+//   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B: thread r
+//               owns query row r (TMEM lane r). It loads its S row
+//               (tcgen05.ld), masks, keeps the running max in the log2
+//               domain (rescaling its O row in TMEM only when the max grows by
+//               more than 2^8), writes P as packed BF16 over the first 64
+//               columns of its S row (tcgen05.st) and at the end normalises
+//               and stores its O row.
+// MMAs issued by one thread execute in order, so S_FULL_X(j) also means
+// PV_X(j-1) is complete (O_X may be rescaled), and S_X(j+1) cannot overwrite
+// P_X(j) before PV_X(j) has read it. While one tile's softmax runs, the
+// tensor core works on the other tile's MMAs.
 // Every mbarrier wait is bounded; a timeout sets the error word, drains the
 // copies and MMAs in flight, frees TMEM and exits.
 #pragma once
@@ -35,25 +41,25 @@
 
 namespace tc {
 
-constexpr int BM = 128;                    // query rows per CTA
+constexpr int BM = 128;                    // query rows per tile (two tiles per CTA)
 constexpr int BN = 128;                    // keys per tile
 constexpr int HD = 128;                    // head dim handled here
 constexpr int HALF_BYTES = 128 * 128;      // one 64-column half of a 128-row tile (bf16)
 constexpr int TILE_BYTES = 2 * HALF_BYTES; // 128 x 128 bf16
 constexpr int STAGES = 2;
-constexpr int SMEM_Q = 0;
-constexpr int SMEM_KV = SMEM_Q + TILE_BYTES;                 // stage s: K at +2s*TILE, V at +(2s+1)*TILE
-constexpr int SMEM_P = SMEM_KV + STAGES * 2 * TILE_BYTES;
-constexpr int SMEM_BAR = SMEM_P + TILE_BYTES;
+constexpr int SMEM_Q = 0;                                    // Q_A, Q_B
+constexpr int SMEM_KV = SMEM_Q + 2 * TILE_BYTES;             // stage s: K at +2s*TILE, V at +(2s+1)*TILE
+constexpr int SMEM_BAR = SMEM_KV + STAGES * 2 * TILE_BYTES;
 constexpr int N_BARS = 16;
 constexpr int SMEM_BYTES = SMEM_BAR + N_BARS * 8 + 16 + 1024; // + TMEM address slot + alignment slack
-constexpr int THREADS = 192;
+constexpr int WARP_TMA = 8, WARP_MMA = 9;
+constexpr int THREADS = 320;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
 // Barrier slots.
-enum { B_Q = 0, B_KV_FULL = 1, B_KV_EMPTY = 3, B_S_FULL = 5, B_S_FREE = 7, B_P_FULL = 9, B_PV_DONE = 10,
-       B_DRAIN = 11 };
+enum { B_Q = 0, B_KV_FULL = 1, B_KV_EMPTY = 3, B_S_FULL = 5 /* +tile */, B_P_FULL = 7 /* +tile */, B_O_DONE = 9,
+       B_DRAIN = 10 };
 
 // tcgen05 instruction descriptor, kind::f16: F32 accumulate, BF16 A and B,
 // M = 128, N = 128, A K-major, B K-major (b_mn = 0) or MN-major (b_mn = 1).
@@ -95,6 +101,15 @@ PCU_DEV void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// D (TMEM) += A (TMEM, K-major, two BF16 per column) x B (shared memory).
+PCU_DEV void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -144,7 +159,41 @@ PCU_DEV void tmem_st32(uint32_t taddr, const float (&v)[32]) {
         : "memory");
 }
 
+// TMEM lane loads/stores of 128 and 64 32-bit columns (generated).
+PCU_DEV void tmem_ld128(uint32_t taddr, float (&v)[128]) {
+    uint32_t r[128];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]), "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]), "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]), "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]), "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]), "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+        : "r"(taddr)
+        : "memory");
+    #pragma unroll
+    for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+PCU_DEV void tmem_st64(uint32_t taddr, const uint32_t (&v)[64]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64};"
+        :: "r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]), "r"(v[32]), "r"(v[33]), "r"(v[34]), "r"(v[35]), "r"(v[36]), "r"(v[37]), "r"(v[38]), "r"(v[39]), "r"(v[40]), "r"(v[41]), "r"(v[42]), "r"(v[43]), "r"(v[44]), "r"(v[45]), "r"(v[46]), "r"(v[47]), "r"(v[48]), "r"(v[49]), "r"(v[50]), "r"(v[51]), "r"(v[52]), "r"(v[53]), "r"(v[54]), "r"(v[55]), "r"(v[56]), "r"(v[57]), "r"(v[58]), "r"(v[59]), "r"(v[60]), "r"(v[61]), "r"(v[62]), "r"(v[63])
+        : "memory");
+}
+
+PCU_DEV void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        :: "r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+
 PCU_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 2^x with one MUFU instruction (relative error ~2^-22, far below BF16 P).
+PCU_DEV float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 PCU_DEV uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
@@ -153,10 +202,29 @@ PCU_DEV uint32_t pack_bf16x2(float lo, float hi) {
 
 struct PrefillTcArgs {
     float* ao;            // [n_seqs][T][H][D] F32
-    int T, H, HK, n_qt;
+    int T, H, HK, n_qb;   // n_qb = query blocks of 2 * BM rows
     float scale_log2;     // log2(e) / sqrtf(D)
     int* err;
 };
+
+// S_X = Q_X K_j^T: M=128, N=128, K=HD in steps of 16 (32 bytes of a 128-byte swizzle row).
+PCU_DEV void issue_qk(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr) {
+    const uint32_t id = idesc_bf16(BN, 0);
+    #pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+        const uint32_t off = (ks / 4) * HALF_BYTES + (ks % 4) * 32;
+        mma_bf16(d_tmem, smem_desc(q_addr + off, 16, 1024), smem_desc(k_addr + off, 16, 1024), id, ks > 0);
+    }
+}
+
+// O_X += P_X V_j: A = P_X in TMEM (16 keys = 8 columns per step), B = V_j MN-major.
+PCU_DEV void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, bool first) {
+    const uint32_t id = idesc_bf16(HD, 1);
+    #pragma unroll
+    for (int ks = 0; ks < BN / 16; ++ks)
+        mma_bf16_ts(o_tmem, p_tmem + ks * 8, smem_desc(v_addr + ks * 16 * 128, HALF_BYTES, 1024), id,
+                    (!first || ks > 0));
+}
 
 __global__ void __launch_bounds__(THREADS, 1)
 prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -171,11 +239,15 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     __shared__ int s_abort, s_issued;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int h = blockIdx.x, seq = blockIdx.y;
-    const int qt = a.n_qt - 1 - (int)blockIdx.z;           // heaviest query tiles first
-    const int q0 = qt * BM;
+    // Consecutive CTAs share (sequence, head), so a head's K/V tiles stay in
+    // L2 while its query blocks run; heaviest (latest) query blocks first.
+    const int qb = a.n_qb - 1 - (int)blockIdx.x;
+    const int h = blockIdx.y, seq = blockIdx.z;
+    const int q0 = qb * 2 * BM;
     const int kvh = h * a.HK / a.H;                         // src/pickle_fast.c:1963
-    const int n_kv = min((q0 + BM + BN - 1) / BN, (a.T + BN - 1) / BN);
+    const int kv_tiles_T = (a.T + BN - 1) / BN;
+    const int n_kv_A = min(q0 / BN + 1, kv_tiles_T);
+    const int n_kv_B = min((q0 + BM) / BN + 1, kv_tiles_T);
 
     if (tid == 0) {
         mbar_init(&bars[B_Q], 1);
@@ -183,32 +255,32 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
             mbar_init(&bars[B_KV_FULL + s], 1);
             mbar_init(&bars[B_KV_EMPTY + s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&bars[B_S_FULL + b], 1);
-            mbar_init(&bars[B_S_FREE + b], 4);
+        for (int x = 0; x < 2; ++x) {
+            mbar_init(&bars[B_S_FULL + x], 1);
+            mbar_init(&bars[B_P_FULL + x], 4);
         }
-        mbar_init(&bars[B_P_FULL], 4);
-        mbar_init(&bars[B_PV_DONE], 1);
+        mbar_init(&bars[B_O_DONE], 1);
         mbar_init(&bars[B_DRAIN], 1);
         mbar_fence_init();
         s_abort = 0;
         s_issued = 0;
     }
-    if (warp == 5) tmem_alloc(tmem_slot, TMEM_COLS);
+    if (warp == WARP_MMA) tmem_alloc(tmem_slot, TMEM_COLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tmem_S0 = tmem, tmem_O = tmem + 256;
 
-    if (warp == 4) {
+    if (warp == WARP_TMA) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             const int zq = seq * a.H + h, zk = seq * a.HK + kvh;
-            mbar_arrive_expect_tx(&bars[B_Q], TILE_BYTES);
-            tma_load_3d(base_u32 + SMEM_Q, &tm_q, 0, q0, zq, &bars[B_Q]);
-            tma_load_3d(base_u32 + SMEM_Q + HALF_BYTES, &tm_q, 64, q0, zq, &bars[B_Q]);
-            for (int j = 0; j < n_kv; ++j) {
+            mbar_arrive_expect_tx(&bars[B_Q], 2 * TILE_BYTES);
+            for (int x = 0; x < 2; ++x) {
+                tma_load_3d(base_u32 + SMEM_Q + x * TILE_BYTES, &tm_q, 0, q0 + x * BM, zq, &bars[B_Q]);
+                tma_load_3d(base_u32 + SMEM_Q + x * TILE_BYTES + HALF_BYTES, &tm_q, 64, q0 + x * BM, zq, &bars[B_Q]);
+            }
+            for (int j = 0; j < n_kv_B; ++j) {
                 const int s = j % STAGES;
                 if (j >= STAGES && !mbar_wait(&bars[B_KV_EMPTY + s], ((j / STAGES) - 1) & 1)) {
                     record_error(a.err, PCU_DEVERR_EMPTY_WAIT);
@@ -226,45 +298,55 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
                 s_issued = j + 1;
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == WARP_MMA) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            const uint32_t id_qk = idesc_bf16(BN, 0);
-            const uint32_t id_pv = idesc_bf16(HD, 1);
+            const uint32_t qA = base_u32 + SMEM_Q, qB = qA + TILE_BYTES;
+            const uint32_t sA = tmem, sB = tmem + 128, oA = tmem + 256, oB = tmem + 384;
+            int kv_ready = -1;
             bool ok = mbar_wait(&bars[B_Q], 0);
-            tc_fence_after();
-            for (int j = 0; ok && j <= n_kv; ++j) {
-                if (j < n_kv) {
-                    const int s = j % STAGES, b = j & 1;
-                    ok = mbar_wait(&bars[B_KV_FULL + s], (j / STAGES) & 1);
-                    if (ok && j >= 2) ok = mbar_wait(&bars[B_S_FREE + b], ((j / 2) - 1) & 1);
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint32_t kaddr = base_u32 + SMEM_KV + (2 * s) * TILE_BYTES;
-                    #pragma unroll
-                    for (int ks = 0; ks < HD / 16; ++ks) {
-                        const uint32_t off = (ks / 4) * HALF_BYTES + (ks % 4) * 32;
-                        mma_bf16(tmem_S0 + b * 128, smem_desc(base_u32 + SMEM_Q + off, 16, 1024),
-                                 smem_desc(kaddr + off, 16, 1024), id_qk, ks > 0);
-                    }
-                    mma_commit(&bars[B_S_FULL + b]);
+            auto wait_kv = [&](int j) {
+                if (ok && j > kv_ready) {
+                    ok = mbar_wait(&bars[B_KV_FULL + j % STAGES], (j / STAGES) & 1);
+                    kv_ready = j;
                 }
-                if (j >= 1) {
-                    const int jp = j - 1, s = jp % STAGES;
-                    ok = mbar_wait(&bars[B_P_FULL], jp & 1);
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint32_t vaddr = base_u32 + SMEM_KV + (2 * s + 1) * TILE_BYTES;
-                    #pragma unroll
-                    for (int ks = 0; ks < BN / 16; ++ks) {
-                        const uint32_t poff = (ks / 4) * HALF_BYTES + (ks % 4) * 32;
-                        mma_bf16(tmem_O, smem_desc(base_u32 + SMEM_P + poff, 16, 1024),
-                                 smem_desc(vaddr + ks * 16 * 128, HALF_BYTES, 1024), id_pv, (jp > 0 || ks > 0));
-                    }
-                    mma_commit(&bars[B_PV_DONE]);
-                    mma_commit(&bars[B_KV_EMPTY + s]);
-                }
+                tc_fence_after();
+            };
+            auto k_addr = [&](int j) { return base_u32 + SMEM_KV + (2 * (j % STAGES)) * TILE_BYTES; };
+            wait_kv(0);
+            if (ok) {
+                issue_qk(sA, qA, k_addr(0));
+                mma_commit(&bars[B_S_FULL + 0]);
+                issue_qk(sB, qB, k_addr(0));
+                mma_commit(&bars[B_S_FULL + 1]);
             }
+            for (int j = 0; ok && j < n_kv_B; ++j) {
+                const uint32_t vaddr = k_addr(j) + TILE_BYTES;
+                if (j < n_kv_A) {
+                    ok = mbar_wait(&bars[B_P_FULL + 0], j & 1);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_pv(oA, sA, vaddr, j == 0);
+                    if (j + 1 < n_kv_A) {
+                        wait_kv(j + 1);
+                        if (!ok) break;
+                        issue_qk(sA, qA, k_addr(j + 1));
+                        mma_commit(&bars[B_S_FULL + 0]);
+                    }
+                }
+                ok = mbar_wait(&bars[B_P_FULL + 1], j & 1);
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv(oB, sB, vaddr, j == 0);
+                if (j + 1 < n_kv_B) {
+                    wait_kv(j + 1);
+                    if (!ok) break;
+                    issue_qk(sB, qB, k_addr(j + 1));
+                    mma_commit(&bars[B_S_FULL + 1]);
+                }
+                mma_commit(&bars[B_KV_EMPTY + j % STAGES]);
+            }
+            if (ok) mma_commit(&bars[B_O_DONE]);
             if (!ok) {
                 record_error(a.err, PCU_DEVERR_MMA_WAIT);
                 s_abort = 1;
@@ -274,88 +356,74 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
             if (!mbar_wait(&bars[B_DRAIN], 0)) record_error(a.err, PCU_DEVERR_DRAIN_WAIT);
         }
     } else {
-        // ---------------- softmax warpgroup: thread = query row ----------------
-        const int row = tid;                                  // 0..127 (TMEM lane)
-        const int q = q0 + row;
-        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-        unsigned char* pbase = base + SMEM_P;
+        // ---------------- softmax: one thread per query row of tile X ----------------
+        const int x = warp >> 2;                                  // 0 = tile A, 1 = tile B
+        const int row = (warp & 3) * 32 + lane;                   // TMEM lane = row in tile
+        const int qx0 = q0 + x * BM;
+        const int q = qx0 + row;
+        const int n_kv = x ? n_kv_B : n_kv_A;
+        const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t s_tm = tmem + x * 128 + lane_off, o_tm = tmem + 256 + x * 128 + lane_off;
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
         for (int j = 0; j < n_kv; ++j) {
-            const int b = j & 1;
-            ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_S_FULL + b], (j / 2) & 1));
+            ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_S_FULL + x], j & 1));
             if (!ok) break;
             tc_fence_after();
             float s[BN];
-            #pragma unroll
-            for (int c = 0; c < BN / 32; ++c) {
-                float v[32];
-                tmem_ld32(tmem_S0 + b * 128 + lane_off + c * 32, v);
-                #pragma unroll
-                for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars[B_S_FREE + b]);
-            // causal mask (and keys past T on a ragged last tile)
+            tmem_ld128(s_tm, s);
             const int k0 = j * BN;
-            if (k0 + BN - 1 > q0 || k0 + BN > a.T) {
+            if (k0 + BN - 1 > qx0 || k0 + BN > a.T) {
                 #pragma unroll
                 for (int c = 0; c < BN; ++c)
                     if (k0 + c > q || k0 + c >= a.T) s[c] = -INFINITY;
             }
-            float mx = -INFINITY;
+            float mx[8];
             #pragma unroll
-            for (int c = 0; c < BN; ++c) mx = fmaxf(mx, s[c]);
-            const float m_tile = mx * a.scale_log2;
+            for (int i = 0; i < 8; ++i) mx[i] = s[i];
+            #pragma unroll
+            for (int c = 8; c < BN; ++c) mx[c & 7] = fmaxf(mx[c & 7], s[c]);
+            const float m_all = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                      fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            const float m_tile = m_all * a.scale_log2;
             float alpha = 1.0f;
             const bool grow = m_tile > m_run + RESCALE_THRESHOLD || m_run == -INFINITY;
             if (grow) {
-                alpha = exp2f(m_run - m_tile);
+                alpha = fast_exp2(m_run - m_tile);
                 m_run = m_tile;
             }
-            float sum = 0.f;
-            #pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                s[c] = exp2f(fmaf(s[c], a.scale_log2, -m_run));
-                sum += s[c];
-            }
-            // P buffer and O are owned by PV_{j-1} until it completes.
-            if (j >= 1) {
-                ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_PV_DONE], (j - 1) & 1));
-                if (!ok) break;
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, grow)) {
+            // S_FULL_X(j) implies PV_X(j-1) finished: O_X is stable here.
+            if (j > 0 && __any_sync(0xffffffffu, grow)) {
+                #pragma unroll
+                for (int c = 0; c < HD / 32; ++c) {
+                    float o[32];
+                    tmem_ld32(o_tm + c * 32, o);
+                    uint32_t ou[32];
                     #pragma unroll
-                    for (int c = 0; c < HD / 32; ++c) {
-                        float o[32];
-                        tmem_ld32(tmem_O + lane_off + c * 32, o);
-                        #pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                        tmem_st32(tmem_O + lane_off + c * 32, o);
-                    }
-                    tmem_st_wait();
+                    for (int i = 0; i < 32; ++i) ou[i] = __float_as_uint(o[i] * alpha);
+                    tmem_st32u(o_tm + c * 32, ou);
                 }
             }
-            l_run = l_run * alpha + sum;
-            // P row -> 128-byte-swizzled K-major tile (two 64-key halves).
+            float sm[8];
             #pragma unroll
-            for (int ch = 0; ch < BN / 8; ++ch) {
-                const int half = ch / 8, chunk = ch % 8;
-                uint4 w;
-                w.x = pack_bf16x2(s[ch * 8 + 0], s[ch * 8 + 1]);
-                w.y = pack_bf16x2(s[ch * 8 + 2], s[ch * 8 + 3]);
-                w.z = pack_bf16x2(s[ch * 8 + 4], s[ch * 8 + 5]);
-                w.w = pack_bf16x2(s[ch * 8 + 6], s[ch * 8 + 7]);
-                const int off = half * HALF_BYTES + (row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4);
-                *reinterpret_cast<uint4*>(pbase + off) = w;
+            for (int i = 0; i < 8; ++i) sm[i] = 0.f;
+            uint32_t pk[BN / 2];
+            #pragma unroll
+            for (int c = 0; c < BN; c += 2) {
+                const float p0 = fast_exp2(fmaf(s[c], a.scale_log2, -m_run));
+                const float p1 = fast_exp2(fmaf(s[c + 1], a.scale_log2, -m_run));
+                sm[(c >> 1) & 7] += p0 + p1;
+                pk[c >> 1] = pack_bf16x2(p0, p1);
             }
-            fence_async_smem();
+            const float sum = ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
+            l_run = l_run * alpha + sum;
+            tmem_st64(s_tm, pk);                                  // P_X over S_X columns [0, 64)
+            tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars[B_P_FULL]);
+            if (lane == 0) mbar_arrive(&bars[B_P_FULL + x]);
         }
-        if (ok && n_kv > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_PV_DONE], (n_kv - 1) & 1));
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_O_DONE], 0));
         if (!ok) {
             if (lane == 0) { record_error(a.err, PCU_DEVERR_FULL_WAIT); s_abort = 1; }
         } else {
@@ -365,7 +433,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
             #pragma unroll
             for (int c = 0; c < HD / 32; ++c) {
                 float o[32];
-                tmem_ld32(tmem_O + lane_off + c * 32, o);
+                tmem_ld32(o_tm + c * 32, o);
                 if (q < a.T) {
                     #pragma unroll
                     for (int i = 0; i < 32; i += 4)
@@ -377,7 +445,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 4 && lane == 0 && s_abort) {
+    if (warp == WARP_TMA && lane == 0 && s_abort) {
         // Copies issued but never consumed must land before shared memory goes away:
         // the last STAGES tiles issued cover every copy that can still be in flight.
         const int issued = s_issued;
@@ -385,7 +453,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
             if (!mbar_wait(&bars[B_KV_FULL + j % STAGES], (j / STAGES) & 1)) record_error(a.err, PCU_DEVERR_DRAIN_WAIT);
         if (!mbar_wait(&bars[B_Q], 0)) record_error(a.err, PCU_DEVERR_DRAIN_WAIT);
     }
-    if (warp == 5) {
+    if (warp == WARP_MMA) {
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);
     }
@@ -448,10 +516,10 @@ inline int prefill_tc_launch(const __nv_bfloat16* q, const __nv_bfloat16* k, con
     a.T = T;
     a.H = H;
     a.HK = HK;
-    a.n_qt = (T + tc::BM - 1) / tc::BM;
+    a.n_qb = (T + 2 * tc::BM - 1) / (2 * tc::BM);
     a.scale_log2 = scale * 1.4426950408889634f;
     a.err = err;
-    dim3 grid((unsigned)H, (unsigned)n_seqs, (unsigned)a.n_qt);
+    dim3 grid((unsigned)a.n_qb, (unsigned)H, (unsigned)n_seqs);
     tc::prefill_tc_kernel<<<grid, tc::THREADS, tc::SMEM_BYTES, st>>>(tq, tk, tv, a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {

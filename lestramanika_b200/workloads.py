@@ -45,8 +45,9 @@ class Prefill:
 
     @property
     def io_bytes(self):
-        # F32 q/k/v in, F32 KV-cache rows out, F32 output
-        return 4 * self.B * self.T * self.D * (self.H + 2 * self.HK + 2 * self.HK + self.H)
+        """Bytes the producer moves: F32 q/k/v in, F32 KV-cache rows out, BF16 q/k/v out."""
+        per_tok = self.D * (4 * (self.H + 2 * self.HK) + 4 * 2 * self.HK + 2 * (self.H + 2 * self.HK))
+        return self.B * self.T * per_tok
 
 
 C2_B1 = Decode("llama3-8b decode B=1 ctx=4096", 1, 32, 8, 128, 4096, 500000.0)

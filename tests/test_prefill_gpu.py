@@ -107,3 +107,29 @@ def test_prefill_bf16_full_length_subset_of_heads():
         ref, _, _ = _oracle_prefill(1, 1, D, T, theta, q[:, h], k[:, h], v[:, h])
         err = float(np.max(np.abs(got[:, h] - ref)))
         assert err <= BF16_ABS_TOL, (h, err)
+
+
+@pytest.mark.parametrize("B,T,H,HK", [(2, 384, 4, 2), (1, 200, 8, 8)])
+def test_prefill_attn_bf16_entry_matches_torch_fp32(B, T, H, HK):
+    """pickle_cuda_prefill_attn_bf16_dev against a plain PyTorch fp32 causal
+    attention of the same BF16 operands."""
+    from lestramanika_b200 import api
+    D = 128
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(21)
+    q = torch.randn((B, H, T, D), generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn((B, HK, T, D), generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn((B, HK, T, D), generator=g, device=dev).to(torch.bfloat16)
+    ao = torch.empty((B, T, H, D), device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    api.prefill_attn_bf16_dev(B, T, H, HK, D, q, k, v, ao, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    kk = k.float().repeat_interleave(H // HK, dim=1)
+    vv = v.float().repeat_interleave(H // HK, dim=1)
+    s = (q.float() @ kk.transpose(-1, -2)) / np.sqrt(np.float32(D))
+    mask = torch.triu(torch.ones(T, T, dtype=torch.bool, device=dev), diagonal=1)
+    ref = torch.softmax(s.masked_fill(mask, float("-inf")), dim=-1) @ vv        # [B][H][T][D]
+    err_abs = float((ao.permute(0, 2, 1, 3) - ref).abs().max())
+    assert err_abs <= 1e-2, err_abs
