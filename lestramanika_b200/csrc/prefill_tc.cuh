@@ -86,6 +86,16 @@ PCU_DEV void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int
         : "memory");
 }
 
+// Shared -> global tensor store (no multicast), bulk-group completion.
+PCU_DEV void tma_store_4d(const CUtensorMap* map, uint32_t src, int x, int y, int z, int w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+        ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(x), "r"(y), "r"(z), "r"(w)
+        : "memory");
+}
+PCU_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+PCU_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 PCU_DEV void tmem_alloc(uint32_t* slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
                  : "memory");
@@ -228,7 +238,8 @@ PCU_DEV void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, bool fi
 
 __global__ void __launch_bounds__(THREADS, 1)
 prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const PrefillTcArgs a) {
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                  const PrefillTcArgs a) {
     extern __shared__ unsigned char smem_raw[];
     // 1024-byte aligned base (128-byte swizzle atoms).
     const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -427,19 +438,33 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         if (!ok) {
             if (lane == 0) { record_error(a.err, PCU_DEVERR_FULL_WAIT); s_abort = 1; }
         } else {
+            // Epilogue: O_DONE means every MMA and every K/V copy is finished, so
+            // the K/V ring is free. Each warp stages its 32 rows x 128 columns,
+            // normalised, as four 128-byte-swizzled [32 rows][32 floats] boxes
+            // (conflict-free: row r writes 16-byte chunk i at i ^ (r & 7)) and
+            // one lane writes them with TMA tensor stores, which clip rows >= T.
             tc_fence_after();
             const float inv = 1.0f / (l_run == 0.0f ? 1.0f : l_run);
-            float* orow = a.ao + (((size_t)seq * a.T + q) * a.H + h) * HD;
+            unsigned char* stage = base + SMEM_KV + warp * 16384;
             #pragma unroll
             for (int c = 0; c < HD / 32; ++c) {
                 float o[32];
                 tmem_ld32(o_tm + c * 32, o);
-                if (q < a.T) {
-                    #pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<float4*>(orow + c * 32 + i) =
-                            make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
-                }
+                unsigned char* box = stage + c * 4096 + lane * 128;
+                #pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    *reinterpret_cast<float4*>(box + ((i ^ (lane & 7)) << 4)) =
+                        make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+            }
+            fence_async_smem();
+            __syncwarp();
+            const int row0 = qx0 + (warp & 3) * 32;
+            if (lane == 0 && row0 < a.T) {
+                #pragma unroll
+                for (int c = 0; c < HD / 32; ++c)
+                    tma_store_4d(&tm_o, base_u32 + SMEM_KV + warp * 16384 + c * 4096, c * 32, h, row0, seq);
+                bulk_commit();
+                bulk_wait_read0();
             }
         }
     }
@@ -489,6 +514,33 @@ inline int make_tmap(CUtensorMap* map, const void* ptr, int T, int n_heads, char
     return 0;
 }
 
+// 4-D tensor map over the F32 output ao [n_seqs][T][H][D]: box 32 floats x 1 head
+// x 32 rows x 1 sequence, 128-byte swizzle (the epilogue's staging layout).
+inline int make_out_tmap(CUtensorMap* map, float* ao, int n_seqs, int T, int H, char* msg, size_t msg_len) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn) {
+            snprintf(msg, msg_len, "cuTensorMapEncodeTiled not available");
+            return -9;
+        }
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const cuuint64_t dims[4] = {(cuuint64_t)tc::HD, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)n_seqs};
+    const cuuint64_t strides[3] = {(cuuint64_t)tc::HD * 4, (cuuint64_t)H * tc::HD * 4, (cuuint64_t)T * H * tc::HD * 4};
+    const cuuint32_t box[4] = {32, 1, 32, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ao, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        snprintf(msg, msg_len, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+        return -9;
+    }
+    return 0;
+}
+
 // q: [n_seqs][H][T][D], k/v: [n_seqs][HK][T][D] BF16 (rotated); ao: [n_seqs][T][H][D] F32.
 inline int prefill_tc_launch(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, float* ao,
                              int n_seqs, int T, int H, int HK, int D, float scale, int* err, cudaStream_t st,
@@ -497,9 +549,13 @@ inline int prefill_tc_launch(const __nv_bfloat16* q, const __nv_bfloat16* k, con
         snprintf(msg, msg_len, "tensor-core prefill needs head_dim %d", tc::HD);
         return -6;
     }
-    alignas(64) CUtensorMap tq, tk, tv;
+    alignas(64) CUtensorMap tq, tk, tv, to;
+    if (reinterpret_cast<uintptr_t>(ao) % 16 != 0) {
+        snprintf(msg, msg_len, "output must be 16-byte aligned");
+        return -6;
+    }
     if (make_tmap(&tq, q, T, n_seqs * H, msg, msg_len) || make_tmap(&tk, k, T, n_seqs * HK, msg, msg_len) ||
-        make_tmap(&tv, v, T, n_seqs * HK, msg, msg_len))
+        make_tmap(&tv, v, T, n_seqs * HK, msg, msg_len) || make_out_tmap(&to, ao, n_seqs, T, H, msg, msg_len))
         return -9;
     static bool attr_set = false;
     if (!attr_set) {
@@ -520,7 +576,7 @@ inline int prefill_tc_launch(const __nv_bfloat16* q, const __nv_bfloat16* k, con
     a.scale_log2 = scale * 1.4426950408889634f;
     a.err = err;
     dim3 grid((unsigned)a.n_qb, (unsigned)H, (unsigned)n_seqs);
-    tc::prefill_tc_kernel<<<grid, tc::THREADS, tc::SMEM_BYTES, st>>>(tq, tk, tv, a);
+    tc::prefill_tc_kernel<<<grid, tc::THREADS, tc::SMEM_BYTES, st>>>(tq, tk, tv, to, a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         snprintf(msg, msg_len, "prefill_tc launch: %s", cudaGetErrorString(e));
