@@ -363,12 +363,15 @@ def run_ours_multi(args, rank, world, local_rank):
                             device_id=torch.device("cuda", local_rank))
     from lestramanika_b200 import dist as pdist
     hbm, _, _, src = peaks()
-    res = pdist.bench_head_sharded(C4, rank, world, local_rank, args.steps, args.warmup)
+    clk = ClockSampler(local_rank) if rank == 0 else None
+    if clk:
+        clk.__enter__()
+    try:
+        res = pdist.bench_head_sharded(C4, rank, world, local_rank, args.steps, args.warmup)
+    finally:
+        if clk:
+            clk.__exit__(None, None, None)
     res_seq = pdist.bench_seq_sharded(C5, rank, world, local_rank, args.steps, args.warmup)
-    clk = None
-    if rank == 0:
-        with ClockSampler(local_rank) as clk:
-            pass
     if rank == 0:
         gbps = C4.kv_bytes / (res["ms"] * 1e-3) / 1e9
         out = {
@@ -383,7 +386,7 @@ def run_ours_multi(args, rank, world, local_rank):
                          "traffic": None, "note": "per-GPU decode kernel, collective excluded"},
             "e2e": res["e2e"],
             "gpu_launches": args.steps,
-            "clocks": res.get("clocks") or {"sm_mhz": None, "reasons": ["unsampled"]},
+            "clocks": clk.summary() if clk else {"sm_mhz": None, "reasons": ["unsampled"]},
             "extras": {"seq_sharded": {"workload": C5.name, "ms": res_seq["ms"],
                                        "GBps": C5.kv_bytes / (res_seq["ms"] * 1e-3) / 1e9}},
         }

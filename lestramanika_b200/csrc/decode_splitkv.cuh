@@ -68,8 +68,10 @@ constexpr int kMaxSplits = 256;
 
 template <int D, int G>
 struct DecodeCfg {
-    static constexpr int NW = G;                  // consumer warps
-    static constexpr int RPW = 32 / G;            // rows per warp per tile
+    static constexpr int GS = G > 4 ? 4 : G;      // query heads per warp
+    static constexpr int NHG = G / GS;            // head groups (warps of a group split the tile's rows)
+    static constexpr int NW = G;                  // consumer warps = NHG groups x GS warps
+    static constexpr int RPW = 32 / GS;           // rows per warp per tile
     static constexpr int TP = 32;                 // rows per tile
     static constexpr int NCH = D / 4;             // float4 chunks per row
     static constexpr int CPL = (NCH + 31) / 32;   // chunks per lane
@@ -79,13 +81,14 @@ struct DecodeCfg {
     static constexpr int STAGES_RAW = 98304 / STAGE_BYTES;
     static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
     static constexpr int THREADS = (NW + 1) * 32;
+    static constexpr int MIN_CTAS = 2;            // two CTAs per SM
     static constexpr size_t RING_BYTES = (size_t)STAGES * STAGE_BYTES;
     static constexpr size_t NEWROW_OFF = RING_BYTES;
     static constexpr size_t PBUF_OFF = NEWROW_OFF + 2 * ROW_BYTES;
     static constexpr size_t BAR_OFF = (PBUF_OFF + NW * 32 * 4 + 15) / 16 * 16;
     static constexpr size_t SMEM = BAR_OFF + 2 * STAGES * 8;
-    // Epilogue scratch (reuses the ring): per-warp acc, m, l, then split weights.
-    static constexpr size_t EPI_BYTES = (size_t)NW * G * D * 4 + 2 * NW * G * 4 + 2 * G * 4 +
+    // Epilogue scratch (reuses the ring): per-warp acc, m, l, then weights.
+    static constexpr size_t EPI_BYTES = (size_t)NW * GS * D * 4 + 2 * NW * GS * 4 + 2 * G * 4 +
                                         (size_t)G * kMaxSplits * 4;
     static_assert(D % 4 == 0, "rows must be 16-byte multiples");
     static_assert(32 % G == 0 && G <= 8, "G in {1, 2, 4, 8}");
@@ -209,7 +212,7 @@ PCU_DEV void attend_rows(const float* __restrict__ Kw, const float* __restrict__
 }
 
 template <int D, int G>
-__global__ void __launch_bounds__(DecodeCfg<D, G>::THREADS)
+__global__ void __launch_bounds__(DecodeCfg<D, G>::THREADS, DecodeCfg<D, G>::MIN_CTAS)
 decode_splitkv_kernel(const DecodeArgs a) {
     using C = DecodeCfg<D, G>;
     extern __shared__ __align__(128) unsigned char smem[];
@@ -264,7 +267,7 @@ decode_splitkv_kernel(const DecodeArgs a) {
     }
     __syncthreads();
 
-    float4 acc[G][C::CPL];
+    float4 acc[C::GS][C::CPL];
     float m_run = -INFINITY, l_run = 0.f;
 
     if (warp == C::NW) {
@@ -291,11 +294,14 @@ decode_splitkv_kernel(const DecodeArgs a) {
             s_issued = issued;
         }
     } else {
-        // Consumers: rotated query slices of this KV head's G query heads.
-        float4 qr[G][C::CPL];
-        const float* qh0 = a.q + ((size_t)z * a.H + (size_t)kvh * G) * D;
+        // Consumers: warp w serves head group hg = w / GS (GS query heads of this
+        // KV head) and rows [wi * RPW, (wi + 1) * RPW) of every tile.
+        constexpr int GS = C::GS;
+        const int hg = warp / GS, wi = warp % GS;
+        float4 qr[GS][C::CPL];
+        const float* qh0 = a.q + ((size_t)z * a.H + (size_t)kvh * G + hg * GS) * D;
         #pragma unroll
-        for (int g = 0; g < G; ++g) {
+        for (int g = 0; g < GS; ++g) {
             const float* qh = qh0 + (size_t)g * D;
             #pragma unroll
             for (int i = 0; i < C::CPL; ++i) {
@@ -324,17 +330,17 @@ decode_splitkv_kernel(const DecodeArgs a) {
                 break;
             }
             const int rows = min(C::TP, n_rows - it * C::TP);
-            const int nvalid = min(max(rows - warp * C::RPW, 0), C::RPW);
+            const int nvalid = min(max(rows - wi * C::RPW, 0), C::RPW);
             const float* ks = ring + (size_t)s * (C::STAGE_BYTES / 4);
             const float* vs = ks + C::TILE_BYTES / 4;
             if (nvalid > 0)
-                attend_rows<D, G>(ks + warp * C::RPW * D, vs + warp * C::RPW * D, nvalid, qr, acc,
-                                  m_run, l_run, pw, a.scale, lane);
+                attend_rows<D, GS>(ks + wi * C::RPW * D, vs + wi * C::RPW * D, nvalid, qr, acc,
+                                   m_run, l_run, pw, a.scale, lane);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
-        if (do_append && warp == 0 && !*(volatile int*)&s_abort)
-            attend_rows<D, G>(newK, newV, 1, qr, acc, m_run, l_run, pw, a.scale, lane);
+        if (do_append && wi == 0 && !*(volatile int*)&s_abort)
+            attend_rows<D, GS>(newK, newV, 1, qr, acc, m_run, l_run, pw, a.scale, lane);
     }
     __syncthreads();
 
@@ -349,36 +355,38 @@ decode_splitkv_kernel(const DecodeArgs a) {
         return;
     }
 
-    // ---- merge the NW warps of this CTA (scratch reuses the ring) ----
-    float* sm_acc = ring;                               // [NW][G][D]
-    float* sm_m = sm_acc + C::NW * G * D;               // [NW][G]
-    float* sm_l = sm_m + C::NW * G;                     // [NW][G]
-    float* sm_M = sm_l + C::NW * G;                     // [G]
+    // ---- merge the warps of each head group (scratch reuses the ring) ----
+    constexpr int GS = C::GS;
+    float* sm_acc = ring;                               // [NW][GS][D]
+    float* sm_m = sm_acc + C::NW * GS * D;              // [NW][GS]
+    float* sm_l = sm_m + C::NW * GS;                    // [NW][GS]
+    float* sm_M = sm_l + C::NW * GS;                    // [G]
     float* sm_L = sm_M + G;                             // [G]
-    float* sm_w = sm_L + G;                             // [G][kMaxSplits]
+    float* sm_w = sm_L + G;                             // [G][GS] warp weights, later [G][kMaxSplits]
     if (warp < C::NW) {
-        if (lane < G) {
-            sm_m[warp * G + lane] = m_run;
-            sm_l[warp * G + lane] = l_run;
+        if (lane < GS) {
+            sm_m[warp * GS + lane] = m_run;
+            sm_l[warp * GS + lane] = l_run;
         }
         #pragma unroll
-        for (int g = 0; g < G; ++g)
+        for (int g = 0; g < GS; ++g)
             #pragma unroll
             for (int i = 0; i < C::CPL; ++i) {
                 const int c = lane + 32 * i;
-                if (c < C::NCH) reinterpret_cast<float4*>(sm_acc + (warp * G + g) * D)[c] = acc[g][i];
+                if (c < C::NCH) reinterpret_cast<float4*>(sm_acc + (warp * GS + g) * D)[c] = acc[g][i];
             }
     }
     __syncthreads();
-    if (tid < G) {
+    if (tid < G) {                                      // head tid: warps hg*GS .. hg*GS+GS-1, local head gl
+        const int hg = tid / GS, gl = tid % GS;
         float M = -INFINITY;
-        for (int w = 0; w < C::NW; ++w) M = fmaxf(M, sm_m[w * G + tid]);
+        for (int i = 0; i < GS; ++i) M = fmaxf(M, sm_m[(hg * GS + i) * GS + gl]);
         float L = 0.f;
-        for (int w = 0; w < C::NW; ++w) {
-            const float mw = sm_m[w * G + tid];
+        for (int i = 0; i < GS; ++i) {
+            const float mw = sm_m[(hg * GS + i) * GS + gl];
             const float e = (mw == -INFINITY) ? 0.f : expf(mw - M);
-            sm_w[tid * C::NW + w] = e;
-            L += sm_l[w * G + tid] * e;
+            sm_w[tid * GS + i] = e;
+            L += sm_l[(hg * GS + i) * GS + gl] * e;
         }
         sm_M[tid] = M;
         sm_L[tid] = L;
@@ -386,16 +394,22 @@ decode_splitkv_kernel(const DecodeArgs a) {
     __syncthreads();
 
     const size_t gidx = (size_t)z * a.HK + kvh;
+    // A (unnormalised) for head g, float4 chunk c, merged over its group's warps.
+    auto warp_merge = [&](int g, int c) {
+        const int hg = g / GS, gl = g % GS;
+        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i = 0; i < GS; ++i) {
+            const float e = sm_w[g * GS + i];
+            const float4 x = reinterpret_cast<const float4*>(sm_acc + ((hg * GS + i) * GS + gl) * D)[c];
+            A.x = fmaf(e, x.x, A.x); A.y = fmaf(e, x.y, A.y);
+            A.z = fmaf(e, x.z, A.z); A.w = fmaf(e, x.w, A.w);
+        }
+        return A;
+    };
     if (a.n_splits == 1) {
         for (int idx = tid; idx < G * C::NCH; idx += C::THREADS) {
             const int g = idx / C::NCH, c = idx % C::NCH;
-            float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int w = 0; w < C::NW; ++w) {
-                const float e = sm_w[g * C::NW + w];
-                const float4 x = reinterpret_cast<const float4*>(sm_acc + (w * G + g) * D)[c];
-                A.x = fmaf(e, x.x, A.x); A.y = fmaf(e, x.y, A.y);
-                A.z = fmaf(e, x.z, A.z); A.w = fmaf(e, x.w, A.w);
-            }
+            const float4 A = warp_merge(g, c);
             const size_t row = (size_t)z * a.H + (size_t)kvh * G + g;
             float4* dst = reinterpret_cast<float4*>(a.ao + row * D) + c;
             if (a.out_mode == 0) {
@@ -413,13 +427,7 @@ decode_splitkv_kernel(const DecodeArgs a) {
     // ---- several splits: publish this CTA's partial, last CTA merges ----
     for (int idx = tid; idx < G * C::NCH; idx += C::THREADS) {
         const int g = idx / C::NCH, c = idx % C::NCH;
-        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int w = 0; w < C::NW; ++w) {
-            const float e = sm_w[g * C::NW + w];
-            const float4 x = reinterpret_cast<const float4*>(sm_acc + (w * G + g) * D)[c];
-            A.x = fmaf(e, x.x, A.x); A.y = fmaf(e, x.y, A.y);
-            A.z = fmaf(e, x.z, A.z); A.w = fmaf(e, x.w, A.w);
-        }
+        const float4 A = warp_merge(g, c);
         const size_t prow = (gidx * G + g) * a.n_splits + split;
         reinterpret_cast<float4*>(a.ws_acc + prow * D)[c] = A;
         if (c == 0) { a.ws_m[prow] = sm_M[g]; a.ws_l[prow] = sm_L[g]; }
