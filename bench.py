@@ -29,7 +29,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from lestramanika_b200.workloads import C2_B1, C2_B8, C2_B64, C3, C4, C5, head_shard, seq_shard  # noqa: E402
+from lestramanika_b200.workloads import C2_B1, C2_B8, C2_B64, C3, C4, C5, Decode  # noqa: E402
 
 MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS = 6650.0, 1590.0
@@ -395,8 +395,9 @@ def run_ours_multi(args, rank, world, local_rank):
     dist.destroy_process_group()
 
 
+C4_SMALL = Decode("llama3-70b decode B=2 ctx=32768 (profiling size)", 2, 64, 8, 128, 32768, 500000.0)
 ONLY = {"c2b1": (C2_B1, True), "c2b8": (C2_B8, False), "c2b64": (C2_B64, False), "c4": (C4, False),
-        "c5": (C5, False), "c3": (C3, None)}
+        "c4s": (C4_SMALL, False), "c5": (C5, False), "c3": (C3, None)}
 
 
 def run_only(args):
