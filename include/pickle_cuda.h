@@ -181,6 +181,15 @@ PICKLE_CUDA_API int pickle_cuda_decode_noalloc(int n_seqs, int n_heads, int n_kv
                                                float* k_cache, float* v_cache, float* ao,
                                                int* err_flag, void* stream);
 
+/* The same merge over parts packed back to back, as one all-gather of
+ * per-rank buffers leaves them: part i starts at parts + i * part_stride
+ * (floats, >= n_rows * (head_dim + 2)) and holds acc [n_rows][head_dim],
+ * then m [n_rows], then l [n_rows]. A rank fills its part by passing
+ * acc_out = part, m_out = part + n_rows * head_dim, l_out = m_out + n_rows
+ * to pickle_cuda_decode_partial_dev. */
+PICKLE_CUDA_API int pickle_cuda_lse_merge_packed_dev(int n_parts, int n_rows, int head_dim, const float* parts,
+                                                     size_t part_stride, float* out, void* stream);
+
 /* Copy host K/V rows in pickle's own layout [n_pos][HK][D] (already
  * rotated, as the host cache holds them) into the device cache at
  * positions [pos0, pos0+n_pos) of (layer, seq). Lets a caller import a

@@ -4,4 +4,5 @@ The product is libpickle_cuda.so (C ABI: include/pickle_cuda.h) built from
 lestramanika_b200/csrc for sm_100a; this package loads it (api), shards it
 across GPUs (dist) and holds the pickle_fast.c integration hook (hook/).
 """
-from .api import PickleCuda, PickleError, lse_merge_dev, abi_version, lib, PREFILL_F32, PREFILL_BF16  # noqa: F401
+from .api import (PickleCuda, PickleError, lse_merge_dev, lse_merge_packed_dev, abi_version, lib,  # noqa: F401
+                  PREFILL_F32, PREFILL_BF16)

@@ -55,6 +55,7 @@ SIGNATURES = {
     "pickle_cuda_prefill_dev": ([_vp, _i, _i, _sz, _sz, _vp, _vp, _vp, _vp, _i, _vp], _i),
     "pickle_cuda_decode_partial_dev": ([_vp, _i, _i, _sz, _sz, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp], _i),
     "pickle_cuda_lse_merge_dev": ([_i, _i, _i, _vp, _vp, _vp, _vp, _vp], _i),
+    "pickle_cuda_lse_merge_packed_dev": ([_i, _i, _i, _vp, _sz, _vp, _vp], _i),
     "pickle_cuda_kv_write": ([_vp, _i, _i, _sz, _sz, _fp, _fp], _i),
     "pickle_cuda_kv_layout": ([_vp, _i, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
                                ctypes.POINTER(_sz), ctypes.POINTER(_sz)], _i),
@@ -246,6 +247,13 @@ def decode_noalloc(n_seqs, n_heads, n_kv_heads, head_dim, half, max_seq, pos, ro
                                           _ptr(k_cache), _ptr(v_cache), _ptr(ao), _ptr(err_flag), _stream(stream))
     if rc != PICKLE_OK:
         raise PickleError(rc, "pickle_cuda_decode_noalloc")
+
+
+def lse_merge_packed_dev(n_parts, n_rows, head_dim, parts, part_stride, out, stream=None):
+    rc = lib().pickle_cuda_lse_merge_packed_dev(n_parts, n_rows, head_dim, _ptr(parts), part_stride, _ptr(out),
+                                                _stream(stream))
+    if rc != PICKLE_OK:
+        raise PickleError(rc, "pickle_cuda_lse_merge_packed_dev")
 
 
 def abi_version():

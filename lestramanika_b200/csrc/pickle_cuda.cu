@@ -387,7 +387,20 @@ int pickle_cuda_lse_merge_dev(int n_parts, int n_rows, int head_dim, const float
                               const float* acc_in, float* out, void* stream) {
     if (n_parts < 1 || n_rows < 1 || head_dim < 1 || !m_in || !l_in || !acc_in || !out) return PICKLE_ERR_ARG;
     lse_merge_kernel<<<n_rows, head_dim < 128 ? 64 : 128, 0, (cudaStream_t)stream>>>(
-        n_parts, n_rows, head_dim, m_in, l_in, acc_in, out);
+        n_parts, n_rows, head_dim, n_rows, (long long)n_rows * head_dim, m_in, l_in, acc_in, out);
+    return cudaGetLastError() == cudaSuccess ? PICKLE_OK : PICKLE_ERR_DEVICE;
+}
+
+int pickle_cuda_lse_merge_packed_dev(int n_parts, int n_rows, int head_dim, const float* parts,
+                                     size_t part_stride, float* out, void* stream) {
+    if (n_parts < 1 || n_rows < 1 || head_dim < 1 || !parts || !out ||
+        part_stride < (size_t)n_rows * (head_dim + 2))
+        return PICKLE_ERR_ARG;
+    const float* acc = parts;
+    const float* m = parts + (size_t)n_rows * head_dim;
+    const float* l = m + n_rows;
+    lse_merge_kernel<<<n_rows, head_dim < 128 ? 64 : 128, 0, (cudaStream_t)stream>>>(
+        n_parts, n_rows, head_dim, (long long)part_stride, (long long)part_stride, m, l, acc, out);
     return cudaGetLastError() == cudaSuccess ? PICKLE_OK : PICKLE_ERR_DEVICE;
 }
 

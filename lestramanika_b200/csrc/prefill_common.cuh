@@ -142,24 +142,28 @@ __global__ void __launch_bounds__(128) rope_append_vec_kernel(const RopeAppendAr
 }
 
 // o = sum_i e^(m_i - M) acc_i / sum_i e^(m_i - M) l_i over n_parts partial
-// triples of n_rows rows; one CTA per row, one thread per element.
-__global__ void lse_merge_kernel(int n_parts, int n_rows, int D, const float* __restrict__ m,
+// triples of n_rows rows; one CTA per row, one thread per element. Part i's
+// m, l and acc start at m + i*part_stride, l + i*part_stride and
+// acc + i*part_stride (floats), with row stride 1 (m, l) and D (acc).
+__global__ void lse_merge_kernel(int n_parts, int n_rows, int D, long long part_stride_m,
+                                 long long part_stride_acc, const float* __restrict__ m,
                                  const float* __restrict__ l, const float* __restrict__ acc,
                                  float* __restrict__ out) {
     const int row = blockIdx.x;
     float M = -INFINITY;
-    for (int i = 0; i < n_parts; ++i) M = fmaxf(M, m[(size_t)i * n_rows + row]);
+    for (int i = 0; i < n_parts; ++i) M = fmaxf(M, m[(size_t)i * part_stride_m + row]);
     float L = 0.f;
     for (int i = 0; i < n_parts; ++i) {
-        const float mi = m[(size_t)i * n_rows + row];
-        L += (mi == -INFINITY) ? 0.f : l[(size_t)i * n_rows + row] * expf(mi - M);
+        const float mi = m[(size_t)i * part_stride_m + row];
+        L += (mi == -INFINITY) ? 0.f : l[(size_t)i * part_stride_m + row] * expf(mi - M);
     }
     const float inv = 1.0f / (L == 0.0f ? 1.0f : L);
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         float A = 0.f;
         for (int i = 0; i < n_parts; ++i) {
-            const float mi = m[(size_t)i * n_rows + row];
-            if (mi != -INFINITY) A = fmaf(expf(mi - M), acc[((size_t)i * n_rows + row) * D + d], A);
+            const float mi = m[(size_t)i * part_stride_m + row];
+            if (mi != -INFINITY)
+                A = fmaf(expf(mi - M), acc[(size_t)i * part_stride_acc + (size_t)row * D + d], A);
         }
         out[(size_t)row * D + d] = A * inv;
     }

@@ -95,9 +95,11 @@ def head_shard_dims(H, HK, world, rank):
 class SeqShardedDecode:
     """Sequence-chunk sharded decode step for one rank.
 
-    compute(q, k, v, m, l, acc) fills this rank's partial triple for all B*H
-    rows; merge(m_all, l_all, acc_all, out) merges the gathered [N]-stacked
-    triples (default: merge_triples). step() returns out [B][H][D].
+    Each rank's partial triple lives in one packed buffer
+    part = [acc (rows x D) | m (rows) | l (rows)], rows = B*H, so a step is
+    one all-gather. compute(q, k, v, m, l, acc) fills this rank's views;
+    merge(parts, part_stride, out) merges the gathered [N] parts (default:
+    merge_triples on views). step() returns out [B][H][D].
     """
 
     def __init__(self, B, H, D, ctx, rank, world, compute, merge=None, device=None):
@@ -108,14 +110,13 @@ class SeqShardedDecode:
         self.compute = compute
         self.merge = merge
         dev = torch.device("cpu") if device is None else torch.device("cuda", device)
-        rows = B * H
-        self.m = torch.empty(rows, device=dev)
-        self.l = torch.empty(rows, device=dev)
-        self.acc = torch.empty((rows, D), device=dev)
-        # Flat along dim 0 for all_gather_into_tensor; viewed as [N][rows](...) to merge.
-        self.m_all = torch.empty(world * rows, device=dev)
-        self.l_all = torch.empty(world * rows, device=dev)
-        self.acc_all = torch.empty((world * rows, D), device=dev)
+        self.rows = rows = B * H
+        self.stride = rows * (D + 2)
+        self.part = torch.empty(self.stride, device=dev)
+        self.acc = self.part[:rows * D].view(rows, D)
+        self.m = self.part[rows * D:rows * (D + 1)]
+        self.l = self.part[rows * (D + 1):]
+        self.parts = torch.empty(world * self.stride, device=dev)
         self.out = torch.empty((B, H, D), device=dev)
 
     @property
@@ -125,16 +126,14 @@ class SeqShardedDecode:
     def step(self, q, k, v):
         import torch.distributed as dist
         self.compute(q, k, v, self.m, self.l, self.acc)
-        dist.all_gather_into_tensor(self.m_all, self.m)
-        dist.all_gather_into_tensor(self.l_all, self.l)
-        dist.all_gather_into_tensor(self.acc_all, self.acc)
+        dist.all_gather_into_tensor(self.parts, self.part)
         if self.merge is not None:
-            self.merge(self.m_all, self.l_all, self.acc_all, self.out)
+            self.merge(self.parts, self.stride, self.out)
         else:
-            rows = self.B * self.H
-            self.out.view(-1, self.D).copy_(merge_triples(self.m_all.view(self.world, rows),
-                                                          self.l_all.view(self.world, rows),
-                                                          self.acc_all.view(self.world, rows, self.D)))
+            rows, D = self.rows, self.D
+            p = self.parts.view(self.world, self.stride)
+            self.out.view(-1, D).copy_(merge_triples(p[:, rows * D:rows * (D + 1)], p[:, rows * (D + 1):],
+                                                     p[:, :rows * D].reshape(self.world, rows, D)))
         return self.out
 
 
@@ -214,7 +213,7 @@ def bench_head_sharded(w, rank, world, device, steps, warmup):
 
 def bench_seq_sharded(w, rank, world, device, steps, warmup):
     import torch
-    from .api import PickleCuda, lse_merge_dev
+    from .api import PickleCuda, lse_merge_packed_dev
     p0, p1 = seq_shard(w.ctx, world, rank)
     n_local = p1 - p0
     append = rank == world - 1
@@ -236,8 +235,8 @@ def bench_seq_sharded(w, rank, world, device, steps, warmup):
     def compute(qq, kk, vv, m, l, acc):
         cu.decode_partial_dev(0, w.B, w.ctx, n_local, append, qq, kk, vv, m, l, acc, st)
 
-    def merge(m_all, l_all, acc_all, out):
-        lse_merge_dev(world, w.B * w.H, w.D, m_all, l_all, acc_all, out, st)
+    def merge(parts, stride, out):
+        lse_merge_packed_dev(world, w.B * w.H, w.D, parts, stride, out, st)
 
     ss = SeqShardedDecode(w.B, w.H, w.D, w.ctx, rank, world, compute, merge=merge, device=device)
     ms = _timed(lambda: ss.step(q, k, v), steps, warmup, device)
