@@ -109,6 +109,28 @@ PCU_DEV float rope_elem(const float* x, int d, int half, const float* sr, const 
     return x[d];
 }
 
+// Two FP32 fused multiply-adds in one sm_100 instruction (fma.rn.f32x2):
+// exactly the same rounding as two fmaf calls.
+PCU_DEV float2 fma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+PCU_DEV float2 mul2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
 // One reduce-scatter level: lanes exchange the half of their W+W values
 // they do not keep; afterwards v[0..W) hold sums over lane pairs (l, l^W).
 template <int W>
@@ -152,15 +174,13 @@ PCU_DEV void attend_rows(const float* __restrict__ Kw, const float* __restrict__
         }
         #pragma unroll
         for (int g = 0; g < G; ++g) {
-            float s = 0.f;
+            float2 s2 = make_float2(0.f, 0.f);
             #pragma unroll
             for (int i = 0; i < C::CPL; ++i) {
-                s = fmaf(qr[g][i].x, kr[i].x, s);
-                s = fmaf(qr[g][i].y, kr[i].y, s);
-                s = fmaf(qr[g][i].z, kr[i].z, s);
-                s = fmaf(qr[g][i].w, kr[i].w, s);
+                s2 = fma2(make_float2(qr[g][i].x, qr[g][i].y), make_float2(kr[i].x, kr[i].y), s2);
+                s2 = fma2(make_float2(qr[g][i].z, qr[g][i].w), make_float2(kr[i].z, kr[i].w), s2);
             }
-            vals[r * G + g] = s;
+            vals[r * G + g] = s2.x + s2.y;
         }
     }
     float s = reduce_scatter32(vals, lane);          // lane l: row l / G, head l % G
@@ -179,9 +199,12 @@ PCU_DEV void attend_rows(const float* __restrict__ Kw, const float* __restrict__
     #pragma unroll
     for (int g = 0; g < G; ++g) {
         const float ag = __shfl_sync(0xffffffffu, alpha, g);
+        const float2 a2 = make_float2(ag, ag);
         #pragma unroll
         for (int i = 0; i < C::CPL; ++i) {
-            acc[g][i].x *= ag; acc[g][i].y *= ag; acc[g][i].z *= ag; acc[g][i].w *= ag;
+            const float2 lo = mul2(make_float2(acc[g][i].x, acc[g][i].y), a2);
+            const float2 hi = mul2(make_float2(acc[g][i].z, acc[g][i].w), a2);
+            acc[g][i] = make_float4(lo.x, lo.y, hi.x, hi.y);
         }
     }
     pw[lane] = p;
@@ -199,10 +222,10 @@ PCU_DEV void attend_rows(const float* __restrict__ Kw, const float* __restrict__
                     const float4 vv = reinterpret_cast<const float4*>(Vw + r * D)[c];
                     #pragma unroll
                     for (int g = 0; g < G; ++g) {
-                        acc[g][i].x = fmaf(pr[g], vv.x, acc[g][i].x);
-                        acc[g][i].y = fmaf(pr[g], vv.y, acc[g][i].y);
-                        acc[g][i].z = fmaf(pr[g], vv.z, acc[g][i].z);
-                        acc[g][i].w = fmaf(pr[g], vv.w, acc[g][i].w);
+                        const float2 pp = make_float2(pr[g], pr[g]);
+                        const float2 lo = fma2(pp, make_float2(vv.x, vv.y), make_float2(acc[g][i].x, acc[g][i].y));
+                        const float2 hi = fma2(pp, make_float2(vv.z, vv.w), make_float2(acc[g][i].z, acc[g][i].w));
+                        acc[g][i] = make_float4(lo.x, lo.y, hi.x, hi.y);
                     }
                 }
             }
