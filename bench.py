@@ -4,9 +4,11 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 N = 1: headline = Llama-3-8B-shaped decode, B=64, ctx 4096 (KV cache
-       2.15 GB > L2, so no flush between steps), plus B=1 / B=8 (L2 flushed
-       between steps), the 70B-shaped and long-context decodes on one GPU,
-       and causal prefill (TFLOP/s) as extras.
+       2.15 GB > L2, so no flush between steps), plus B=1 / B=8, the
+       70B-shaped and long-context decodes on one GPU, and causal prefill
+       (TFLOP/s) as extras. A workload whose cache fits in L2 (B=1: 34 MB)
+       steps through enough layer caches that the set is twice L2, as a
+       model's decode step does; its L2-write-flushed time is reported too.
 N > 1: headline = Llama-3-70B-shaped decode sharded by KV-head group
        (B=16, ctx 32768), head outputs all-gathered over NVLink (NCCL);
        extra = long-context decode sharded by sequence chunk (ctx 131072),
@@ -34,6 +36,7 @@ from lestramanika_b200.workloads import C2_B1, C2_B8, C2_B64, C3, C4, C5, Decode
 MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS = 6650.0, 1590.0
 L2_FLUSH_BYTES = 512 << 20
+L2_BYTES = 126 << 20
 
 
 def peaks():
@@ -126,21 +129,23 @@ def _torch():
     return torch
 
 
-def make_decode_state(w, device, H=None, HK=None, B=None, ctx_rows=None, seed=0):
-    """Handle with a seeded N(0,1) device cache for workload w (or a shard of it)."""
+def make_decode_state(w, device, H=None, HK=None, B=None, ctx_rows=None, seed=0, n_layers=1):
+    """Handle with seeded N(0,1) device caches (n_layers layers) for workload w (or a shard of it)."""
     torch = _torch()
     from lestramanika_b200 import PickleCuda
     H = H or w.H
     HK = HK or w.HK
     B = B or w.B
     rows = w.ctx if ctx_rows is None else ctx_rows
-    cu = PickleCuda(1, H, HK, w.D, rows + 1, rope_theta=w.theta, n_seqs=B, rope_len=w.ctx + 1, device=device)
-    kt, vt = cu.kv_tensors(0)
+    cu = PickleCuda(n_layers, H, HK, w.D, rows + 1, rope_theta=w.theta, n_seqs=B, rope_len=w.ctx + 1,
+                    device=device)
     g = torch.Generator(device=f"cuda:{device}")
     g.manual_seed(seed)
-    for b in range(B):
-        kt[b, :, :rows].normal_(generator=g)
-        vt[b, :, :rows].normal_(generator=g)
+    for layer in range(n_layers):
+        kt, vt = cu.kv_tensors(layer)
+        for b in range(B):
+            kt[b, :, :rows].normal_(generator=g)
+            vt[b, :, :rows].normal_(generator=g)
     dev = torch.device("cuda", device)
     q = torch.randn((B, H, w.D), generator=g, device=dev)
     k = torch.randn((B, HK, w.D), generator=g, device=dev)
@@ -150,18 +155,19 @@ def make_decode_state(w, device, H=None, HK=None, B=None, ctx_rows=None, seed=0)
     return cu, q, k, v, ao
 
 
-def time_decode(cu, w, q, k, v, ao, steps, warmup, flush=None):
-    """Device time of `steps` decode launches (ms list), CUDA events on the launching stream."""
+def time_decode(cu, w, q, k, v, ao, steps, warmup, flush=None, n_layers=1):
+    """Device time of `steps` decode launches (ms list), CUDA events on the launching stream.
+    Step i attends layer i % n_layers."""
     torch = _torch()
     st = torch.cuda.current_stream()
-    for _ in range(warmup):
-        cu.decode_batch_dev(0, q.shape[0], w.ctx, q, k, v, ao, st)
+    for i in range(warmup):
+        cu.decode_batch_dev(i % n_layers, q.shape[0], w.ctx, q, k, v, ao, st)
     cu.sync(st)
     if flush is None:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
-        for _ in range(steps):
-            cu.decode_batch_dev(0, q.shape[0], w.ctx, q, k, v, ao, st)
+        for i in range(steps):
+            cu.decode_batch_dev(i % n_layers, q.shape[0], w.ctx, q, k, v, ao, st)
         e1.record(st)
         cu.sync(st)
         return [e0.elapsed_time(e1) / steps] * steps
@@ -207,20 +213,30 @@ def time_decode_e2e(cu, w, q, k, v, ao, steps, warmup):
     return ms, h2d, hao.numel() * 4
 
 
-def decode_line(w, device, steps, warmup, flush_l2):
+def decode_line(w, device, steps, warmup, small):
+    """small: the cache fits in L2, so steps rotate over layer caches totalling
+    twice L2 (the headline for the line), and the same decode is also timed
+    on one layer with L2 flushed by a 512 MB write before every step."""
     torch = _torch()
-    cu, q, k, v, ao = make_decode_state(w, device)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, device=f"cuda:{device}") if flush_l2 else None
-    times = time_decode(cu, w, q, k, v, ao, steps, warmup, flush)
+    n_layers = -(-2 * L2_BYTES // w.kv_bytes) if small else 1
+    cu, q, k, v, ao = make_decode_state(w, device, n_layers=n_layers)
+    times = time_decode(cu, w, q, k, v, ao, steps, warmup, None, n_layers)
     splits = cu.decode_plan(w.B, w.ctx)[0]
     ms = sum(times) / len(times)
     out = {"workload": w.name, "ms": ms, "GBps": w.kv_bytes / (ms * 1e-3) / 1e9, "splits": splits,
-           "l2": "flushed between steps" if flush_l2 else "inputs larger than L2"}
+           "l2": (f"{n_layers} layer caches rotated ({n_layers * w.kv_bytes / 1e6:.0f} MB > L2)" if small
+                  else "inputs larger than L2")}
     e2e = None
-    if not flush_l2:
+    if small:
+        flush = torch.empty(L2_FLUSH_BYTES // 4, device=f"cuda:{device}")
+        ft = time_decode(cu, w, q, k, v, ao, steps, warmup, flush)
+        fms = sum(ft) / len(ft)
+        out["l2_write_flushed"] = {"ms": fms, "GBps": w.kv_bytes / (fms * 1e-3) / 1e9}
+        del flush
+    else:
         e2e = time_decode_e2e(cu, w, q, k, v, ao, steps, warmup)
     cu.close()
-    del q, k, v, ao, flush
+    del q, k, v, ao
     torch.cuda.empty_cache()
     return out, e2e
 
@@ -316,10 +332,10 @@ def run_ours_single(args):
     torch.cuda.set_device(device)
     hbm, bf16, bf16_sus, src = peaks()
     with ClockSampler(device) as clk:
-        head, e2e = decode_line(C2_B64, device, args.steps, args.warmup, flush_l2=False)
+        head, e2e = decode_line(C2_B64, device, args.steps, args.warmup, small=False)
     extras = {}
-    for w, flush in ((C2_B1, True), (C2_B8, False), (C4, False), (C5, False)):
-        line, _ = decode_line(w, device, max(args.steps, 5), args.warmup, flush)
+    for w, small in ((C2_B1, True), (C2_B8, False), (C4, False), (C5, False)):
+        line, _ = decode_line(w, device, max(args.steps, 5), args.warmup, small)
         line["frac_of_measured_hbm"] = line["GBps"] / hbm
         extras[w.name] = line
     try:

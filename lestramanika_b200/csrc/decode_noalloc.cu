@@ -24,6 +24,7 @@
 #include "pickle_cuda.h"
 
 #include <cmath>
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -117,6 +118,10 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_decode_noalloc(
         half < 0 || 2 * half > head_dim || max_seq < 1 || !rope_sin || !rope_cos || !q || !k || !v ||
         !k_cache || !v_cache || !ao)
         return PICKLE_ERR_ARG;
+    // Rows move as 16-byte vectors and bulk copies: every row pointer must be 16-byte aligned.
+    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)k_cache | (uintptr_t)v_cache |
+         (uintptr_t)ao) % 16)
+        return PICKLE_ERR_ARG;
     if (pos >= (size_t)max_seq) return PICKLE_ERR_RANGE;
     const int G = n_heads / n_kv_heads;
     NoAllocKernel kern;
@@ -188,6 +193,7 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_decode_noalloc(
     a.n_q = 1;
     a.q_pos0 = (long long)pos;
     a.rope = 1;
+    a.vec = half % 4 == 0 && ((uintptr_t)rope_sin | (uintptr_t)rope_cos) % 16 == 0;
     a.append = 1;
     a.append_idx = (long long)pos;
     a.hist_len0 = hist;

@@ -46,6 +46,7 @@ struct DecodeArgs {
     int n_q;                 // queries per sequence in this launch
     long long q_pos0;        // absolute position of query t = 0 (RoPE row)
     int rope;                // rotate q and k_new with the table row at the query position
+    int vec;                 // half % 4 == 0 and 16-byte aligned tables: float4 RoPE loads
     int append;              // store + attend the new k/v row
     long long append_idx;    // cache row of the new token
     long long hist_len0;     // cached rows [0, hist) attended by query t = 0
@@ -107,6 +108,35 @@ PCU_DEV float rope_elem(const float* x, int d, int half, const float* sr, const 
         return sr[i] * lo + cr[i] * hi;
     }
     return x[d];
+}
+
+PCU_DEV float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+// Elements 4c..4c+3 of a rotated head row with 16-byte loads: the same
+// products and sums as rope_elem (needs half % 4 == 0 and aligned rows).
+PCU_DEV float4 rope_vec4(const float* x, int c, int half, const float* sr, const float* cr) {
+    const int d = 4 * c;
+    if (d < half) {
+        const float4 lo = ld4(x + d), hi = ld4(x + d + half), sn = ld4(sr + d), cs = ld4(cr + d);
+        return make_float4(cs.x * lo.x - sn.x * hi.x, cs.y * lo.y - sn.y * hi.y,
+                           cs.z * lo.z - sn.z * hi.z, cs.w * lo.w - sn.w * hi.w);
+    }
+    if (d < 2 * half) {
+        const int i = d - half;
+        const float4 lo = ld4(x + i), hi = ld4(x + d), sn = ld4(sr + i), cs = ld4(cr + i);
+        return make_float4(sn.x * lo.x + cs.x * hi.x, sn.y * lo.y + cs.y * hi.y,
+                           sn.z * lo.z + cs.z * hi.z, sn.w * lo.w + cs.w * hi.w);
+    }
+    return ld4(x + d);
+}
+
+// Chunk c of a head row, rotated (rope) or not.
+PCU_DEV float4 load_row4(const float* x, int c, int rope, int vec, int half, const float* sr,
+                         const float* cr) {
+    if (!rope) return ld4(x + 4 * c);
+    if (vec) return rope_vec4(x, c, half, sr, cr);
+    return make_float4(rope_elem(x, 4 * c + 0, half, sr, cr), rope_elem(x, 4 * c + 1, half, sr, cr),
+                       rope_elem(x, 4 * c + 2, half, sr, cr), rope_elem(x, 4 * c + 3, half, sr, cr));
 }
 
 // Two FP32 fused multiply-adds in one sm_100 instruction (fma.rn.f32x2):
@@ -264,40 +294,70 @@ decode_splitkv_kernel(const DecodeArgs a) {
     const float* sr = a.sin_tab + (size_t)qpos * a.half;
     const float* cr = a.cos_tab + (size_t)qpos * a.half;
 
-    if (tid == 0) {
-        for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], C::NW);
+    float4 acc[C::GS][C::CPL];
+    float4 qr[C::GS][C::CPL];
+    float m_run = -INFINITY, l_run = 0.f;
+    int first_issued = 0;
+
+    // Prologue. The producer lane sets up the ring and puts the first
+    // STAGES tile copies in flight at once; meanwhile the consumer warps
+    // rotate and store the new row (last split) and load their query heads.
+    if (warp == C::NW) {
+        if (lane == 0) {
+            for (int s = 0; s < C::STAGES; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], C::NW);
+            }
+            mbar_fence_init();
+            s_abort = 0;
+            s_last = 0;
+            s_issued = 0;
+            first_issued = n_tiles < C::STAGES ? n_tiles : C::STAGES;
+            for (int it = 0; it < first_issued; ++it) {
+                const int rows = min(C::TP, n_rows - it * C::TP);
+                const uint32_t bytes = (uint32_t)rows * C::ROW_BYTES;
+                float* ks = ring + (size_t)it * (C::STAGE_BYTES / 4);
+                mbar_arrive_expect_tx(&full[it], 2u * bytes);
+                bulk_g2s(ks, kbase + (size_t)it * C::TP * D, bytes, &full[it]);
+                bulk_g2s(ks + C::TILE_BYTES / 4, vbase + (size_t)it * C::TP * D, bytes, &full[it]);
+            }
         }
-        mbar_fence_init();
-        s_abort = 0;
-        s_last = 0;
-        s_issued = 0;
-    }
-    if (do_append) {
-        const float* kn = a.k_new + ((size_t)seq * a.HK + kvh) * D;
-        const float* vn = a.v_new + ((size_t)seq * a.HK + kvh) * D;
-        float* kdst = a.kc + head_off + (size_t)a.append_idx * D;
-        float* vdst = a.vc + head_off + (size_t)a.append_idx * D;
-        for (int d = tid; d < D; d += C::THREADS) {
-            const float kk = a.rope ? rope_elem(kn, d, a.half, sr, cr) : kn[d];
-            const float vv = vn[d];
-            newK[d] = kk;
-            newV[d] = vv;
-            kdst[d] = kk;
-            vdst[d] = vv;
+    } else {
+        if (do_append) {
+            const float* kn = a.k_new + ((size_t)seq * a.HK + kvh) * D;
+            const float* vn = a.v_new + ((size_t)seq * a.HK + kvh) * D;
+            float4* kdst = reinterpret_cast<float4*>(a.kc + head_off + (size_t)a.append_idx * D);
+            float4* vdst = reinterpret_cast<float4*>(a.vc + head_off + (size_t)a.append_idx * D);
+            for (int c = tid; c < C::NCH; c += C::NW * 32) {
+                const float4 kk = load_row4(kn, c, a.rope, a.vec, a.half, sr, cr);
+                const float4 vv = ld4(vn + 4 * c);
+                reinterpret_cast<float4*>(newK)[c] = kk;
+                reinterpret_cast<float4*>(newV)[c] = vv;
+                kdst[c] = kk;
+                vdst[c] = vv;
+            }
+        }
+        // Warp w serves head group hg = w / GS: GS query heads of this KV head.
+        const int hg = warp / C::GS;
+        const float* qh0 = a.q + ((size_t)z * a.H + (size_t)kvh * G + hg * C::GS) * D;
+        #pragma unroll
+        for (int g = 0; g < C::GS; ++g) {
+            #pragma unroll
+            for (int i = 0; i < C::CPL; ++i) {
+                const int c = lane + 32 * i;
+                qr[g][i] = c < C::NCH ? load_row4(qh0 + (size_t)g * D, c, a.rope, a.vec, a.half, sr, cr)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+                acc[g][i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
         }
     }
     __syncthreads();
 
-    float4 acc[C::GS][C::CPL];
-    float m_run = -INFINITY, l_run = 0.f;
-
     if (warp == C::NW) {
         // Producer: one lane streams the K/V tiles of this split.
         if (lane == 0) {
-            int issued = 0;
-            for (int it = 0; it < n_tiles; ++it) {
+            int issued = first_issued;
+            for (int it = first_issued; it < n_tiles; ++it) {
                 const int s = it % C::STAGES;
                 if (it >= C::STAGES && !mbar_wait(&empty[s], ((it / C::STAGES) - 1) & 1)) {
                     record_error(a.err, PCU_DEVERR_EMPTY_WAIT);
@@ -320,30 +380,7 @@ decode_splitkv_kernel(const DecodeArgs a) {
         // Consumers: warp w serves head group hg = w / GS (GS query heads of this
         // KV head) and rows [wi * RPW, (wi + 1) * RPW) of every tile.
         constexpr int GS = C::GS;
-        const int hg = warp / GS, wi = warp % GS;
-        float4 qr[GS][C::CPL];
-        const float* qh0 = a.q + ((size_t)z * a.H + (size_t)kvh * G + hg * GS) * D;
-        #pragma unroll
-        for (int g = 0; g < GS; ++g) {
-            const float* qh = qh0 + (size_t)g * D;
-            #pragma unroll
-            for (int i = 0; i < C::CPL; ++i) {
-                const int c = lane + 32 * i;
-                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (c < C::NCH) {
-                    if (a.rope) {
-                        x.x = rope_elem(qh, 4 * c + 0, a.half, sr, cr);
-                        x.y = rope_elem(qh, 4 * c + 1, a.half, sr, cr);
-                        x.z = rope_elem(qh, 4 * c + 2, a.half, sr, cr);
-                        x.w = rope_elem(qh, 4 * c + 3, a.half, sr, cr);
-                    } else {
-                        x = reinterpret_cast<const float4*>(qh)[c];
-                    }
-                }
-                qr[g][i] = x;
-                acc[g][i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        }
+        const int wi = warp % GS;
         float* pw = pbuf + warp * 32;
         for (int it = 0; it < n_tiles; ++it) {
             const int s = it % C::STAGES;
@@ -465,36 +502,59 @@ decode_splitkv_kernel(const DecodeArgs a) {
     if (!s_last) return;
     __threadfence();
 
-    // Split weights: warp g handles head g.
+    // Split weights: warp g handles head g; all of its (m, l) loads are in
+    // flight at once (lane j holds splits j, j + 32, ...).
     if (warp < G) {
         const int g = warp;
         const size_t base = (gidx * G + g) * a.n_splits;
+        constexpr int MS = kMaxSplits / 32;
+        float mv[MS], lv[MS];
+        #pragma unroll
+        for (int j = 0; j < MS; ++j) {
+            const int s = lane + 32 * j;
+            const bool in = s < a.n_splits;
+            mv[j] = in ? __ldcg(a.ws_m + base + s) : -INFINITY;
+            lv[j] = in ? __ldcg(a.ws_l + base + s) : 0.f;
+        }
         float M = -INFINITY;
-        for (int s = lane; s < a.n_splits; s += 32) M = fmaxf(M, __ldcg(a.ws_m + base + s));
+        #pragma unroll
+        for (int j = 0; j < MS; ++j) M = fmaxf(M, mv[j]);
         #pragma unroll
         for (int m = 16; m > 0; m >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, m));
         float L = 0.f;
-        for (int s = lane; s < a.n_splits; s += 32) {
-            const float ms = __ldcg(a.ws_m + base + s);
-            const float e = (ms == -INFINITY) ? 0.f : expf(ms - M);
-            sm_w[g * kMaxSplits + s] = e;
-            L += __ldcg(a.ws_l + base + s) * e;
+        #pragma unroll
+        for (int j = 0; j < MS; ++j) {
+            const int s = lane + 32 * j;
+            const float e = (mv[j] == -INFINITY) ? 0.f : expf(mv[j] - M);
+            if (s < a.n_splits) sm_w[g * kMaxSplits + s] = e;
+            L += lv[j] * e;
         }
         #pragma unroll
         for (int m = 16; m > 0; m >>= 1) L += __shfl_xor_sync(0xffffffffu, L, m);
         if (lane == 0) { sm_M[g] = M; sm_L[g] = L; }
     }
     __syncthreads();
+    // Weighted sum of the partial accumulators; loads go out MB at a time so
+    // a few L2 round trips cover all splits.
+    constexpr int MB = 8;
     for (int idx = tid; idx < G * C::NCH; idx += C::THREADS) {
         const int g = idx / C::NCH, c = idx % C::NCH;
         const float4* src = reinterpret_cast<const float4*>(a.ws_acc + (gidx * G + g) * a.n_splits * D) + c;
+        const float* wg = sm_w + g * kMaxSplits;
         float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-        #pragma unroll 4
-        for (int s = 0; s < a.n_splits; ++s) {
-            const float e = sm_w[g * kMaxSplits + s];
-            const float4 x = __ldcg(src + (size_t)s * C::NCH);
-            A.x = fmaf(e, x.x, A.x); A.y = fmaf(e, x.y, A.y);
-            A.z = fmaf(e, x.z, A.z); A.w = fmaf(e, x.w, A.w);
+        for (int s0 = 0; s0 < a.n_splits; s0 += MB) {
+            float4 x[MB];
+            #pragma unroll
+            for (int j = 0; j < MB; ++j)
+                x[j] = s0 + j < a.n_splits ? __ldcg(src + (size_t)(s0 + j) * C::NCH) : make_float4(0.f, 0.f, 0.f, 0.f);
+            #pragma unroll
+            for (int j = 0; j < MB; ++j) {
+                if (s0 + j < a.n_splits) {
+                    const float e = wg[s0 + j];
+                    A.x = fmaf(e, x[j].x, A.x); A.y = fmaf(e, x[j].y, A.y);
+                    A.z = fmaf(e, x[j].z, A.z); A.w = fmaf(e, x[j].w, A.w);
+                }
+            }
         }
         const size_t row = (size_t)z * a.H + (size_t)kvh * G + g;
         float4* dst = reinterpret_cast<float4*>(a.ao + row * D) + c;

@@ -5,6 +5,7 @@
 #include "pickle_cuda.h"
 
 #include <cmath>
+#include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -159,6 +160,7 @@ DecodeArgs base_args(pickle_cuda* h, int layer) {
     a.H = h->H;
     a.HK = h->HK;
     a.half = h->half;
+    a.vec = h->half % 4 == 0;                 // table rows then start on 16-byte boundaries
     a.n_q = 1;
     a.scale = 1.0f / sqrtf((float)h->D);      // src/pickle_fast.c:1959
     a.ws_m = h->ws_m;
@@ -187,6 +189,11 @@ int decode_common(pickle_cuda* h, int layer, int n_seqs, size_t pos, long long h
     if (rc != PICKLE_OK) return rc;
     const long long groups = (long long)n_seqs * h->HK;
     if ((size_t)groups > h->n_counters) return PICKLE_ERR_ARG;
+    // Query, new rows and outputs move as 16-byte vectors.
+    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)ao) % 16) {
+        snprintf(h->last_error, sizeof(h->last_error), "q, k, v and output rows must be 16-byte aligned");
+        return PICKLE_ERR_ARG;
+    }
     DecodeArgs a = base_args(h, layer);
     a.q = q;
     a.k_new = k;
@@ -537,6 +544,10 @@ int prefill_launch(pickle_cuda* h, int layer, int n_seqs, size_t pos0, size_t T,
                    const float* k, const float* v, float* ao, int precision, cudaStream_t st) {
     const size_t nq = (size_t)n_seqs * T * h->H * h->D;
     const size_t nk = (size_t)n_seqs * T * h->HK * h->D;
+    if ((uintptr_t)ao % 16) {
+        snprintf(h->last_error, sizeof(h->last_error), "output rows must be 16-byte aligned");
+        return PICKLE_ERR_ARG;
+    }
     RopeAppendArgs ra;
     memset(&ra, 0, sizeof(ra));
     ra.q = q; ra.k = k; ra.v = v;

@@ -159,3 +159,66 @@ def test_sequential_steps_reuse_device_cache():
                        what=f"pos={pos} layer={layer}")
     cu.close()
     o.close()
+
+
+def _rope_np(x, half, sn, cs):
+    """NeoX rotation of the first 2*half elements (src/pickle_fast.c:1917-1924), float64."""
+    y = x.astype(np.float64).copy()
+    lo, hi = x[..., :half].astype(np.float64), x[..., half:2 * half].astype(np.float64)
+    y[..., :half] = cs * lo - sn * hi
+    y[..., half:2 * half] = sn * lo + cs * hi
+    return y
+
+
+def test_partial_rotary_half_not_multiple_of_four():
+    """An explicit rotary width of 30 pairs (not a multiple of four) takes the
+    element-wise RoPE loads; checked against a float64 restatement."""
+    B, H, HK, D, ctx, half, theta = 2, 8, 2, 64, 300, 30, 10000.0
+    dev = torch.device("cuda", 0)
+    cu = PickleCuda(1, H, HK, D, ctx + 1, half=half, rope_theta=theta, n_seqs=B)
+    kc = normal(5, (B, HK, ctx, D), 1)
+    vc = normal(5, (B, HK, ctx, D), 2)
+    kt, vt = cu.kv_tensors(0)
+    kt[:, :, :ctx] = torch.from_numpy(kc).to(dev)
+    vt[:, :, :ctx] = torch.from_numpy(vc).to(dev)
+    q, k, v = normal(5, (B, H, D), 3), normal(5, (B, HK, D), 4), normal(5, (B, HK, D), 5)
+    ao = torch.empty((B, H, D), device=dev)
+    cu.decode_batch_dev(0, B, ctx, *(torch.from_numpy(x).to(dev) for x in (q, k, v)), ao)
+    cu.sync()
+    got = ao.cpu().numpy()
+    cu.close()
+    inv = (1.0 / np.power(np.float32(theta), np.arange(half, dtype=np.float32) * 2 / np.float32(D))).astype(np.float32)
+    ang = (inv * np.float32(ctx)).astype(np.float64)
+    sn, cs = np.sin(ang), np.cos(ang)
+    qr, kr = _rope_np(q, half, sn, cs), _rope_np(k, half, sn, cs)
+    G = H // HK
+    ref = np.empty((B, H, D))
+    for b in range(B):
+        for h in range(H):
+            kv = h // G
+            keys = np.concatenate([kc[b, kv].astype(np.float64), kr[b, kv][None]])
+            vals = np.concatenate([vc[b, kv].astype(np.float64), v[b, kv].astype(np.float64)[None]])
+            sc = keys @ qr[b, h] / np.sqrt(D)
+            w = np.exp(sc - sc.max())
+            ref[b, h] = (w / w.sum()) @ vals
+    assert_rel(got, ref, what="half=30")
+
+
+def test_decode_rejects_unaligned_rows():
+    """q / k / v / output rows move as 16-byte vectors: a pointer off a
+    16-byte boundary is an argument error, not a device fault."""
+    dev = torch.device("cuda", 0)
+    B, H, HK, D = 1, 8, 2, 64
+    cu = PickleCuda(1, H, HK, D, 16, n_seqs=B)
+    buf = torch.zeros(B * H * D + 1, device=dev)
+    q_bad = buf[1:].view(B, H, D)
+    k = torch.zeros((B, HK, D), device=dev)
+    ao = torch.empty((B, H, D), device=dev)
+    with pytest.raises(PickleError) as e:
+        cu.decode_batch_dev(0, B, 3, q_bad, k, k, ao)
+    assert e.value.code == -6
+    out_bad = torch.empty(B * H * D + 1, device=dev)[1:].view(B, H, D)
+    with pytest.raises(PickleError) as e:
+        cu.decode_batch_dev(0, B, 3, torch.zeros((B, H, D), device=dev), k, k, out_bad)
+    assert e.value.code == -6
+    cu.close()
