@@ -8,15 +8,15 @@
 // buffers it already owns, but it cannot let a library call cudaMalloc
 // behind its back. pickle_cuda_decode_noalloc therefore takes every input
 // and output from the caller (q, k, v, the KV cache, the RoPE tables, ao)
-// and keeps its only scratch - the split-KV partial results and the
-// per-(sequence, KV head) split counters - in one fixed array below.
+// and keeps its only scratch - the split-KV partial results - in one
+// fixed array below.
 //
 // The array is a file-scope __device__ object of kNoAllocScratchBytes
 // (4 MiB); every GPU that loads this library holds it until the process
-// exits. All calls share it and it keeps the last call's contents, so:
-//   * each call clears the counter slots it will use before its launch;
-//   * calls whose kernels overlap on the GPU (other streams, other host
-//     threads) race on the array - serialise them on one stream.
+// exits. All calls share it, so calls whose kernels overlap on the GPU
+// (other streams, other host threads) race on the array - serialise them
+// on one stream. A call is two launches (split kernel, then the merge
+// kernel as its programmatic dependent) when it plans several splits.
 // The first call on each device looks up the array's device address with
 // cudaGetSymbolAddress (host code may not use the symbol itself as a
 // device pointer) and sets the kernel's shared-memory limit; make that
@@ -37,7 +37,7 @@ constexpr size_t kNoAllocScratchBytes = 4u << 20;          // 4 MiB
 constexpr int kNoAllocMaxGroups = 4096;                     // n_seqs * n_kv_heads
 constexpr int kNoAllocMaxDevices = 64;
 
-// Layout: [counters: kNoAllocMaxGroups u32][partials: m, l, acc rows].
+// Layout: [partials: m rows, l rows, acc rows].
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 struct NoAllocDevice {
@@ -144,9 +144,8 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_decode_noalloc(
     if (e != cudaSuccess || occ < 1) { report("occupancy", e); return PICKLE_ERR_DEVICE; }
 
     // Split plan: fill the SMs, but never more partial rows than the array holds.
-    const size_t counter_bytes = (size_t)kNoAllocMaxGroups * sizeof(unsigned);
     const size_t row_bytes = (size_t)(head_dim + 2) * sizeof(float);
-    const long long row_cap = (long long)((kNoAllocScratchBytes - counter_bytes - 64) / row_bytes);
+    const long long row_cap = (long long)((kNoAllocScratchBytes - 64) / row_bytes);
     const long long hist = (long long)pos;
     int n_splits = 1;
     if (hist > 0) {
@@ -168,13 +167,10 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_decode_noalloc(
 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     unsigned char* base = dev->scratch;
-    unsigned* counters = reinterpret_cast<unsigned*>(base);
     const size_t part_rows4 = (part_rows + 3) & ~size_t(3);   // keeps ws_acc 16-byte aligned
-    float* ws_m = reinterpret_cast<float*>(base + counter_bytes);
+    float* ws_m = reinterpret_cast<float*>(base);
     float* ws_l = ws_m + part_rows4;
     float* ws_acc = ws_l + part_rows4;
-    e = cudaMemsetAsync(counters, 0, (size_t)groups * sizeof(unsigned), st);
-    if (e != cudaSuccess) { report("cudaMemsetAsync", e); return PICKLE_ERR_DEVICE; }
 
     DecodeArgs a;
     memset(&a, 0, sizeof(a));
@@ -206,11 +202,22 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_decode_noalloc(
     a.ws_m = ws_m;
     a.ws_l = ws_l;
     a.ws_acc = ws_acc;
-    a.counters = counters;
     a.err = err_flag;
     void* params[] = {&a};
     dim3 grid((unsigned)n_splits, (unsigned)n_kv_heads, (unsigned)n_seqs);
     e = cudaLaunchKernel(kern.fn, grid, dim3(kern.threads), params, kern.smem, st);
     if (e != cudaSuccess) { report("cudaLaunchKernel", e); return PICKLE_ERR_DEVICE; }
+    if (n_splits > 1) {
+        MergeArgs m;
+        memset(&m, 0, sizeof(m));
+        m.ws_m = ws_m;
+        m.ws_l = ws_l;
+        m.ws_acc = ws_acc;
+        m.n_splits = n_splits;
+        m.out_mode = 0;
+        m.out = ao;
+        e = launch_decode_merge(head_dim, m, n_seqs * n_heads, st);
+        if (e != cudaSuccess) { report("merge launch", e); return PICKLE_ERR_DEVICE; }
+    }
     return PICKLE_OK;
 }

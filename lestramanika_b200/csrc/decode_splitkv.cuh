@@ -24,9 +24,13 @@
 //
 // The new token's row (RoPE'd k, v) is stored to the cache and attended
 // from shared memory by the CTA of the last split, so no CTA ever reads a
-// row another CTA of the same launch writes. Splits are merged by the last
-// CTA of each (kv_head, z) to finish (atomic ticket on a per-group
-// counter, reset by that CTA), so a decode step is one launch.
+// row another CTA of the same launch writes. With one split a CTA writes
+// the normalised output itself. With several, each CTA publishes its
+// unnormalised partial (m, l, acc) and decode_merge_kernel combines them:
+// it is launched as a programmatic dependent of the split kernel, so its
+// CTAs are resident before the split kernel retires and start merging as
+// soon as the partials are visible. Spreading the merge over one CTA per
+// output row keeps it off a single SM's L2 bandwidth.
 #pragma once
 #include <cfloat>
 #include <cmath>
@@ -61,7 +65,6 @@ struct DecodeArgs {
     float* ws_m;             // [n_groups][G][n_splits]
     float* ws_l;
     float* ws_acc;           // [n_groups][G][n_splits][D]
-    unsigned* counters;      // [n_groups], zero between launches
     int* err;
 };
 
@@ -71,7 +74,7 @@ template <int D, int G>
 struct DecodeCfg {
     static constexpr int GS = G > 4 ? 4 : G;      // query heads per warp
     static constexpr int NHG = G / GS;            // head groups (warps of a group split the tile's rows)
-    static constexpr int NW = G;                  // consumer warps = NHG groups x GS warps
+    static constexpr int NW = G;                  // warps of a consumer set = NHG groups x GS warps
     static constexpr int RPW = 32 / GS;           // rows per warp per tile
     static constexpr int TP = 32;                 // rows per tile
     static constexpr int NCH = D / 4;             // float4 chunks per row
@@ -81,19 +84,31 @@ struct DecodeCfg {
     static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
     static constexpr int STAGES_RAW = 98304 / STAGE_BYTES;
     static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
-    static constexpr int THREADS = (NW + 1) * 32;
+    // Consumer sets: set k takes tiles k, k + NSET, ... with its own online
+    // softmax state, so up to eight consumer warps (four for D > 128, whose
+    // query and accumulator slices take twice the registers) share one
+    // CTA's ring, never more sets than tiles in flight.
+    static constexpr int NSET_RAW = (D > 128 ? 4 : 8) / G;
+    static constexpr int NSET = NSET_RAW < 1 ? 1 : (NSET_RAW > STAGES ? STAGES : NSET_RAW);
+    static constexpr int NCW = NSET * NW;         // consumer warps
+    static constexpr int WPH = NSET * GS;         // warps holding partial state of one query head
+    static constexpr int THREADS = (NCW + 1) * 32;
     static constexpr int MIN_CTAS = 2;            // two CTAs per SM
     static constexpr size_t RING_BYTES = (size_t)STAGES * STAGE_BYTES;
     static constexpr size_t NEWROW_OFF = RING_BYTES;
     static constexpr size_t PBUF_OFF = NEWROW_OFF + 2 * ROW_BYTES;
-    static constexpr size_t BAR_OFF = (PBUF_OFF + NW * 32 * 4 + 15) / 16 * 16;
+    static constexpr size_t BAR_OFF = (PBUF_OFF + NCW * 32 * 4 + 15) / 16 * 16;
     static constexpr size_t SMEM = BAR_OFF + 2 * STAGES * 8;
-    // Epilogue scratch (reuses the ring): per-warp acc, m, l, then weights.
-    static constexpr size_t EPI_BYTES = (size_t)NW * GS * D * 4 + 2 * NW * GS * 4 + 2 * G * 4 +
-                                        (size_t)G * kMaxSplits * 4;
+    // Epilogue scratch reuses the ring: own (M, L) [G] each, warp weights
+    // [G][8], then the per-warp (acc, m, l) of the intra-CTA merge.
+    static constexpr int RING_FLOATS = (int)(RING_BYTES / 4);
+    static constexpr int FRONT = (2 * G + 8 * G + 31) / 32 * 32;
+    static constexpr int INTRA = NCW * GS * D + 2 * NCW * GS;
     static_assert(D % 4 == 0, "rows must be 16-byte multiples");
     static_assert(32 % G == 0 && G <= 8, "G in {1, 2, 4, 8}");
-    static_assert(EPI_BYTES <= RING_BYTES, "epilogue scratch must fit in the ring");
+    static_assert(FRONT + INTRA <= RING_FLOATS, "epilogue scratch must fit in the ring");
+    static_assert(NSET >= 1 && THREADS <= 288, "at most eight consumer warps");
+    static_assert(WPH <= 8, "warp weights: eight per head");
 };
 
 // NeoX rotation of element d of a head row x (src/pickle_fast.c:1917-1924).
@@ -275,7 +290,7 @@ decode_splitkv_kernel(const DecodeArgs a) {
     float* pbuf = reinterpret_cast<float*>(smem + C::PBUF_OFF);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
     uint64_t* empty = full + C::STAGES;
-    __shared__ int s_abort, s_last, s_issued;
+    __shared__ int s_abort, s_issued;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, kvh = blockIdx.y, z = blockIdx.z;
@@ -299,10 +314,12 @@ decode_splitkv_kernel(const DecodeArgs a) {
     float m_run = -INFINITY, l_run = 0.f;
     int first_issued = 0;
 
+    griddep_launch_dependents();                        // the merge kernel may take free SM slots now
+
     // Prologue. The producer lane sets up the ring and puts the first
     // STAGES tile copies in flight at once; meanwhile the consumer warps
     // rotate and store the new row (last split) and load their query heads.
-    if (warp == C::NW) {
+    if (warp == C::NCW) {
         if (lane == 0) {
             for (int s = 0; s < C::STAGES; ++s) {
                 mbar_init(&full[s], 1);
@@ -310,7 +327,6 @@ decode_splitkv_kernel(const DecodeArgs a) {
             }
             mbar_fence_init();
             s_abort = 0;
-            s_last = 0;
             s_issued = 0;
             first_issued = n_tiles < C::STAGES ? n_tiles : C::STAGES;
             for (int it = 0; it < first_issued; ++it) {
@@ -328,7 +344,7 @@ decode_splitkv_kernel(const DecodeArgs a) {
             const float* vn = a.v_new + ((size_t)seq * a.HK + kvh) * D;
             float4* kdst = reinterpret_cast<float4*>(a.kc + head_off + (size_t)a.append_idx * D);
             float4* vdst = reinterpret_cast<float4*>(a.vc + head_off + (size_t)a.append_idx * D);
-            for (int c = tid; c < C::NCH; c += C::NW * 32) {
+            for (int c = tid; c < C::NCH; c += C::NCW * 32) {
                 const float4 kk = load_row4(kn, c, a.rope, a.vec, a.half, sr, cr);
                 const float4 vv = ld4(vn + 4 * c);
                 reinterpret_cast<float4*>(newK)[c] = kk;
@@ -337,8 +353,8 @@ decode_splitkv_kernel(const DecodeArgs a) {
                 vdst[c] = vv;
             }
         }
-        // Warp w serves head group hg = w / GS: GS query heads of this KV head.
-        const int hg = warp / C::GS;
+        // Warp w serves head group hg = (w % NW) / GS: GS query heads of this KV head.
+        const int hg = (warp % C::NW) / C::GS;
         const float* qh0 = a.q + ((size_t)z * a.H + (size_t)kvh * G + hg * C::GS) * D;
         #pragma unroll
         for (int g = 0; g < C::GS; ++g) {
@@ -353,7 +369,7 @@ decode_splitkv_kernel(const DecodeArgs a) {
     }
     __syncthreads();
 
-    if (warp == C::NW) {
+    if (warp == C::NCW) {
         // Producer: one lane streams the K/V tiles of this split.
         if (lane == 0) {
             int issued = first_issued;
@@ -377,13 +393,25 @@ decode_splitkv_kernel(const DecodeArgs a) {
             s_issued = issued;
         }
     } else {
-        // Consumers: warp w serves head group hg = w / GS (GS query heads of this
-        // KV head) and rows [wi * RPW, (wi + 1) * RPW) of every tile.
+        // Consumers: warp w belongs to set w / NW, which takes tiles set,
+        // set + NSET, ...; within the set it serves head group (w % NW) / GS
+        // and rows [wi * RPW, (wi + 1) * RPW) of each of its tiles.
         constexpr int GS = C::GS;
-        const int wi = warp % GS;
+        const int set = warp / C::NW, wi = (warp % C::NW) % GS;
         float* pw = pbuf + warp * 32;
-        for (int it = 0; it < n_tiles; ++it) {
+        for (int it = set; it < n_tiles; it += C::NSET) {
             const int s = it % C::STAGES;
+            if (C::NSET > 1 && it >= C::STAGES) {
+                // Consecutive uses of a stage may belong to different sets. Wait
+                // for the release of the previous use (tile it - STAGES) first:
+                // then the stage's full barrier is at most one phase away and
+                // its parity wait cannot match the phase two uses back.
+                const bool rel = __all_sync(0xffffffffu, mbar_wait(&empty[s], ((it / C::STAGES) - 1) & 1));
+                if (!rel) {
+                    if (lane == 0) { record_error(a.err, PCU_DEVERR_EMPTY_WAIT); s_abort = 1; }
+                    break;
+                }
+            }
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (it / C::STAGES) & 1));
             if (!ok) {
                 if (lane == 0) { record_error(a.err, PCU_DEVERR_FULL_WAIT); s_abort = 1; }
@@ -399,7 +427,7 @@ decode_splitkv_kernel(const DecodeArgs a) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
-        if (do_append && wi == 0 && !*(volatile int*)&s_abort)
+        if (do_append && set == n_tiles % C::NSET && wi == 0 && !*(volatile int*)&s_abort)
             attend_rows<D, GS>(newK, newV, 1, qr, acc, m_run, l_run, pw, a.scale, lane);
     }
     __syncthreads();
@@ -415,15 +443,19 @@ decode_splitkv_kernel(const DecodeArgs a) {
         return;
     }
 
-    // ---- merge the warps of each head group (scratch reuses the ring) ----
+    // ---- epilogue: merge the warps holding each query head's state ----
     constexpr int GS = C::GS;
-    float* sm_acc = ring;                               // [NW][GS][D]
-    float* sm_m = sm_acc + C::NW * GS * D;              // [NW][GS]
-    float* sm_l = sm_m + C::NW * GS;                    // [NW][GS]
-    float* sm_M = sm_l + C::NW * GS;                    // [G]
-    float* sm_L = sm_M + G;                             // [G]
-    float* sm_w = sm_L + G;                             // [G][GS] warp weights, later [G][kMaxSplits]
-    if (warp < C::NW) {
+    const size_t gidx = (size_t)z * a.HK + kvh;
+    float* own_M = ring;                                // [G]
+    float* own_L = own_M + G;                           // [G]
+    float* sm_ww = own_L + G;                           // [G][8] weights of the warps of a head
+    float* sm_acc = ring + C::FRONT;                    // [NCW][GS][D]
+    float* sm_m = sm_acc + C::NCW * GS * D;             // [NCW][GS]
+    float* sm_l = sm_m + C::NCW * GS;                   // [NCW][GS]
+    // Warp j (0 <= j < WPH) holding state of local head gl of head group hg.
+    auto head_warp = [&](int hg, int j) { return (j / GS) * C::NW + hg * GS + j % GS; };
+
+    if (warp < C::NCW) {
         if (lane < GS) {
             sm_m[warp * GS + lane] = m_run;
             sm_l[warp * GS + lane] = l_run;
@@ -437,135 +469,184 @@ decode_splitkv_kernel(const DecodeArgs a) {
             }
     }
     __syncthreads();
-    if (tid < G) {                                      // head tid: warps hg*GS .. hg*GS+GS-1, local head gl
-        const int hg = tid / GS, gl = tid % GS;
-        float M = -INFINITY;
-        for (int i = 0; i < GS; ++i) M = fmaxf(M, sm_m[(hg * GS + i) * GS + gl]);
-        float L = 0.f;
-        for (int i = 0; i < GS; ++i) {
-            const float mw = sm_m[(hg * GS + i) * GS + gl];
-            const float e = (mw == -INFINITY) ? 0.f : expf(mw - M);
-            sm_w[tid * GS + i] = e;
-            L += sm_l[(hg * GS + i) * GS + gl] * e;
-        }
-        sm_M[tid] = M;
-        sm_L[tid] = L;
+    if (warp < G) {                                     // warp g: weights of the WPH warps of head g
+        const int g = warp, hg = g / GS, gl = g % GS;
+        const float mw = lane < C::WPH ? sm_m[head_warp(hg, lane) * GS + gl] : -INFINITY;
+        const float lw = lane < C::WPH ? sm_l[head_warp(hg, lane) * GS + gl] : 0.f;
+        float M = mw;
+        #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float e = (mw == -INFINITY) ? 0.f : expf(mw - M);
+        float L = lw * e;
+        #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        if (lane < C::WPH) sm_ww[g * 8 + lane] = e;
+        if (lane == 0) { own_M[g] = M; own_L[g] = L; }
     }
     __syncthreads();
 
-    const size_t gidx = (size_t)z * a.HK + kvh;
-    // A (unnormalised) for head g, float4 chunk c, merged over its group's warps.
-    auto warp_merge = [&](int g, int c) {
-        const int hg = g / GS, gl = g % GS;
+    for (int idx = tid; idx < G * C::NCH; idx += C::THREADS) {
+        const int g = idx / C::NCH, c = idx % C::NCH, hg = g / GS, gl = g % GS;
         float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int i = 0; i < GS; ++i) {
-            const float e = sm_w[g * GS + i];
-            const float4 x = reinterpret_cast<const float4*>(sm_acc + ((hg * GS + i) * GS + gl) * D)[c];
+        for (int j = 0; j < C::WPH; ++j) {
+            const float e = sm_ww[g * 8 + j];
+            const float4 x = reinterpret_cast<const float4*>(sm_acc + (head_warp(hg, j) * GS + gl) * D)[c];
             A.x = fmaf(e, x.x, A.x); A.y = fmaf(e, x.y, A.y);
             A.z = fmaf(e, x.z, A.z); A.w = fmaf(e, x.w, A.w);
         }
-        return A;
-    };
-    if (a.n_splits == 1) {
-        for (int idx = tid; idx < G * C::NCH; idx += C::THREADS) {
-            const int g = idx / C::NCH, c = idx % C::NCH;
-            const float4 A = warp_merge(g, c);
-            const size_t row = (size_t)z * a.H + (size_t)kvh * G + g;
-            float4* dst = reinterpret_cast<float4*>(a.ao + row * D) + c;
-            if (a.out_mode == 0) {
-                const float L = sm_L[g];
-                const float inv = 1.0f / (L == 0.0f ? 1.0f : L);
-                *dst = make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv);
-            } else {
-                *dst = A;
-                if (c == 0) { a.out_m[row] = sm_M[g]; a.out_l[row] = sm_L[g]; }
-            }
+        if (a.n_splits > 1) {
+            // Partial of this split; decode_merge_kernel combines the splits.
+            const size_t prow = (gidx * G + g) * a.n_splits + split;
+            reinterpret_cast<float4*>(a.ws_acc + prow * D)[c] = A;
+            if (c == 0) { a.ws_m[prow] = own_M[g]; a.ws_l[prow] = own_L[g]; }
+            continue;
         }
-        return;
+        const size_t row = (size_t)z * a.H + (size_t)kvh * G + g;
+        float4* dst = reinterpret_cast<float4*>(a.ao + row * D) + c;
+        if (a.out_mode == 0) {
+            const float L = own_L[g];
+            const float inv = 1.0f / (L == 0.0f ? 1.0f : L);
+            *dst = make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv);
+        } else {
+            *dst = A;
+            if (c == 0) { a.out_m[row] = own_M[g]; a.out_l[row] = own_L[g]; }
+        }
     }
+}
 
-    // ---- several splits: publish this CTA's partial, last CTA merges ----
-    for (int idx = tid; idx < G * C::NCH; idx += C::THREADS) {
-        const int g = idx / C::NCH, c = idx % C::NCH;
-        const float4 A = warp_merge(g, c);
-        const size_t prow = (gidx * G + g) * a.n_splits + split;
-        reinterpret_cast<float4*>(a.ws_acc + prow * D)[c] = A;
-        if (c == 0) { a.ws_m[prow] = sm_M[g]; a.ws_l[prow] = sm_L[g]; }
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const unsigned prev = atomicAdd(&a.counters[gidx], 1u);
-        s_last = (prev == (unsigned)a.n_splits - 1u);
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
+// Combine the n_splits partials of every output row r (= z * H + h, which
+// is also the partial row group (z * HK + kv_head) * G + local head):
+//   M = max_s m_s, w_s = e^(m_s - M), L = sum_s w_s l_s,
+//   out = sum_s w_s acc_s / L      (out_mode 1: sum_s w_s acc_s, M, L)
+// i.e. the reference's softmax over all cached rows (src/pickle_fast.c
+// :2034-2091) assembled from per-split maxima and sums. One CTA per row;
+// thread (sg, c) takes float4 chunk c of splits sg, sg + SG, ... with all
+// of its loads in flight, and the SG partial sums meet in shared memory.
+struct MergeArgs {
+    const float* ws_m;       // [n_rows][n_splits]
+    const float* ws_l;
+    const float* ws_acc;     // [n_rows][n_splits][D]
+    int n_splits;
+    int out_mode;
+    float* out;              // [n_rows][D]
+    float* out_m;            // [n_rows] (out_mode 1)
+    float* out_l;
+};
 
-    // Split weights: warp g handles head g; all of its (m, l) loads are in
-    // flight at once (lane j holds splits j, j + 32, ...).
-    if (warp < G) {
-        const int g = warp;
-        const size_t base = (gidx * G + g) * a.n_splits;
+constexpr int kMergeThreads = 256;
+
+template <int D>
+__global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const MergeArgs a) {
+    constexpr int NCH = D / 4;
+    constexpr int SG = kMergeThreads / NCH;             // split groups
+    constexpr int BATCH = 8;                            // loads in flight per thread per round
+    __shared__ float s_w[kMaxSplits];
+    __shared__ float s_M, s_L;
+    __shared__ float4 s_red[SG][NCH];
+    const int tid = threadIdx.x, row = blockIdx.x;
+    const int sg = tid / NCH, c = tid % NCH;
+    const int S = a.n_splits;
+    griddep_wait();                                     // the split kernel's partials are visible
+
+    if (tid < 32) {
         constexpr int MS = kMaxSplits / 32;
         float mv[MS], lv[MS];
         #pragma unroll
         for (int j = 0; j < MS; ++j) {
-            const int s = lane + 32 * j;
-            const bool in = s < a.n_splits;
-            mv[j] = in ? __ldcg(a.ws_m + base + s) : -INFINITY;
-            lv[j] = in ? __ldcg(a.ws_l + base + s) : 0.f;
+            const int s = tid + 32 * j;
+            mv[j] = s < S ? a.ws_m[(size_t)row * S + s] : -INFINITY;
+            lv[j] = s < S ? a.ws_l[(size_t)row * S + s] : 0.f;
         }
         float M = -INFINITY;
         #pragma unroll
         for (int j = 0; j < MS; ++j) M = fmaxf(M, mv[j]);
         #pragma unroll
-        for (int m = 16; m > 0; m >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, m));
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         float L = 0.f;
         #pragma unroll
         for (int j = 0; j < MS; ++j) {
-            const int s = lane + 32 * j;
+            const int s = tid + 32 * j;
             const float e = (mv[j] == -INFINITY) ? 0.f : expf(mv[j] - M);
-            if (s < a.n_splits) sm_w[g * kMaxSplits + s] = e;
+            if (s < S) s_w[s] = e;
             L += lv[j] * e;
         }
         #pragma unroll
-        for (int m = 16; m > 0; m >>= 1) L += __shfl_xor_sync(0xffffffffu, L, m);
-        if (lane == 0) { sm_M[g] = M; sm_L[g] = L; }
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        if (tid == 0) { s_M = M; s_L = L; }
+    }
+    // Every thread's first batch of partial rows is loaded before the weights are needed.
+    float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4* src = reinterpret_cast<const float4*>(a.ws_acc + (size_t)row * S * D) + c;
+    float4 x[BATCH];
+    if (sg < SG) {
+        #pragma unroll
+        for (int j = 0; j < BATCH; ++j) {
+            const int s = sg + SG * j;
+            x[j] = s < S ? src[(size_t)s * NCH] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
     }
     __syncthreads();
-    // Weighted sum of the partial accumulators; loads go out MB at a time so
-    // a few L2 round trips cover all splits.
-    constexpr int MB = 8;
-    for (int idx = tid; idx < G * C::NCH; idx += C::THREADS) {
-        const int g = idx / C::NCH, c = idx % C::NCH;
-        const float4* src = reinterpret_cast<const float4*>(a.ws_acc + (gidx * G + g) * a.n_splits * D) + c;
-        const float* wg = sm_w + g * kMaxSplits;
-        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int s0 = 0; s0 < a.n_splits; s0 += MB) {
-            float4 x[MB];
+    if (sg < SG) {
+        for (int s0 = sg; s0 < S; s0 += SG * BATCH) {
+            if (s0 != sg) {
+                #pragma unroll
+                for (int j = 0; j < BATCH; ++j) {
+                    const int s = s0 + SG * j;
+                    x[j] = s < S ? src[(size_t)s * NCH] : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
             #pragma unroll
-            for (int j = 0; j < MB; ++j)
-                x[j] = s0 + j < a.n_splits ? __ldcg(src + (size_t)(s0 + j) * C::NCH) : make_float4(0.f, 0.f, 0.f, 0.f);
-            #pragma unroll
-            for (int j = 0; j < MB; ++j) {
-                if (s0 + j < a.n_splits) {
-                    const float e = wg[s0 + j];
+            for (int j = 0; j < BATCH; ++j) {
+                const int s = s0 + SG * j;
+                if (s < S) {
+                    const float e = s_w[s];
                     A.x = fmaf(e, x[j].x, A.x); A.y = fmaf(e, x[j].y, A.y);
                     A.z = fmaf(e, x[j].z, A.z); A.w = fmaf(e, x[j].w, A.w);
                 }
             }
         }
-        const size_t row = (size_t)z * a.H + (size_t)kvh * G + g;
-        float4* dst = reinterpret_cast<float4*>(a.ao + row * D) + c;
+        s_red[sg][c] = A;
+    }
+    __syncthreads();
+    if (tid < NCH) {
+        float4 T = s_red[0][tid];
+        #pragma unroll
+        for (int k = 1; k < SG; ++k) {
+            const float4 y = s_red[k][tid];
+            T.x += y.x; T.y += y.y; T.z += y.z; T.w += y.w;
+        }
+        float4* dst = reinterpret_cast<float4*>(a.out + (size_t)row * D) + tid;
         if (a.out_mode == 0) {
-            const float L = sm_L[g];
-            const float inv = 1.0f / (L == 0.0f ? 1.0f : L);
-            *dst = make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv);
+            const float inv = 1.0f / (s_L == 0.0f ? 1.0f : s_L);
+            *dst = make_float4(T.x * inv, T.y * inv, T.z * inv, T.w * inv);
         } else {
-            *dst = A;
-            if (c == 0) { a.out_m[row] = sm_M[g]; a.out_l[row] = sm_L[g]; }
+            *dst = T;
+            if (tid == 0) { a.out_m[row] = s_M; a.out_l[row] = s_L; }
         }
     }
-    if (tid == 0) a.counters[gidx] = 0u;
+}
+
+// Host: the merge launch, as a programmatic dependent of the split kernel
+// just queued on `st` (its CTAs may become resident before the split
+// kernel ends; griddepcontrol.wait holds them until the partials are
+// visible). n_rows = queries x query heads.
+inline cudaError_t launch_decode_merge(int D, const MergeArgs& m, int n_rows, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)n_rows);
+    cfg.blockDim = dim3(kMergeThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    switch (D) {
+        case 48: return cudaLaunchKernelEx(&cfg, decode_merge_kernel<48>, m);
+        case 64: return cudaLaunchKernelEx(&cfg, decode_merge_kernel<64>, m);
+        case 96: return cudaLaunchKernelEx(&cfg, decode_merge_kernel<96>, m);
+        case 128: return cudaLaunchKernelEx(&cfg, decode_merge_kernel<128>, m);
+        case 256: return cudaLaunchKernelEx(&cfg, decode_merge_kernel<256>, m);
+        default: return cudaErrorInvalidValue;
+    }
 }

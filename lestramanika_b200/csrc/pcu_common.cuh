@@ -83,6 +83,12 @@ PCU_DEV void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint
         : "memory");
 }
 
+// Programmatic dependent launch: a dependent grid waits here until its
+// prerequisite grid has completed and that grid's writes are visible; the
+// prerequisite lets the dependent be scheduled once all its CTAs ran this.
+PCU_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+PCU_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 PCU_DEV void record_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
 }

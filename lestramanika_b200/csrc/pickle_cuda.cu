@@ -40,8 +40,6 @@ struct pickle_cuda {
     float* ws_l = nullptr;
     float* ws_acc = nullptr;
     size_t ws_rows = 0;        // capacity in (group * G * split) rows
-    unsigned* counters = nullptr;
-    size_t n_counters = 0;
     int* err_dev = nullptr;
     cudaStream_t stream = nullptr;
     // Host-buffer entry points: pinned staging and its device mirror.
@@ -166,7 +164,6 @@ DecodeArgs base_args(pickle_cuda* h, int layer) {
     a.ws_m = h->ws_m;
     a.ws_l = h->ws_l;
     a.ws_acc = h->ws_acc;
-    a.counters = h->counters;
     a.err = h->err_dev;
     return a;
 }
@@ -177,6 +174,19 @@ int launch_decode(pickle_cuda* h, DecodeArgs& a, int n_z, cudaStream_t st) {
     dim3 grid((unsigned)a.n_splits, (unsigned)h->HK, (unsigned)n_z);
     void* params[] = {&a};
     PCU_CHECK(h, cudaLaunchKernel(h->decode.fn, grid, dim3(h->decode.threads), params, h->decode.smem, st));
+    if (a.n_splits > 1) {
+        MergeArgs m;
+        memset(&m, 0, sizeof(m));
+        m.ws_m = a.ws_m;
+        m.ws_l = a.ws_l;
+        m.ws_acc = a.ws_acc;
+        m.n_splits = a.n_splits;
+        m.out_mode = a.out_mode;
+        m.out = a.ao;
+        m.out_m = a.out_m;
+        m.out_l = a.out_l;
+        PCU_CHECK(h, launch_decode_merge(h->D, m, n_z * h->H, st));   // one row per (query, head)
+    }
     return PICKLE_OK;
 }
 
@@ -188,7 +198,6 @@ int decode_common(pickle_cuda* h, int layer, int n_seqs, size_t pos, long long h
     int rc = prepare_kernel(h, h->decode);
     if (rc != PICKLE_OK) return rc;
     const long long groups = (long long)n_seqs * h->HK;
-    if ((size_t)groups > h->n_counters) return PICKLE_ERR_ARG;
     // Query, new rows and outputs move as 16-byte vectors.
     if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)ao) % 16) {
         snprintf(h->last_error, sizeof(h->last_error), "q, k, v and output rows must be 16-byte aligned");
@@ -326,13 +335,10 @@ int pickle_cuda_init(const pickle_cuda_params_t* p, int device, pickle_cuda_t** 
 
     // Split-KV workspace: at most 4096 partial rows per KV group member.
     h->ws_rows = (size_t)4096 * h->G;
-    h->n_counters = (size_t)h->n_seqs * h->HK;
     ok = cudaMalloc(&h->ws_m, h->ws_rows * sizeof(float)) == cudaSuccess &&
          cudaMalloc(&h->ws_l, h->ws_rows * sizeof(float)) == cudaSuccess &&
          cudaMalloc(&h->ws_acc, h->ws_rows * h->D * sizeof(float)) == cudaSuccess &&
-         cudaMalloc(&h->counters, h->n_counters * sizeof(unsigned)) == cudaSuccess &&
          cudaMalloc(&h->err_dev, sizeof(int)) == cudaSuccess &&
-         cudaMemset(h->counters, 0, h->n_counters * sizeof(unsigned)) == cudaSuccess &&
          cudaMemset(h->err_dev, 0, sizeof(int)) == cudaSuccess;
     if (!ok) return bail(PICKLE_ERR_MEMORY);
     if (prepare_kernel(h, h->decode) != PICKLE_OK) return bail(PICKLE_ERR_DEVICE);
@@ -348,7 +354,7 @@ void pickle_cuda_free(pickle_cuda_t* h) {
     cudaFree(h->kc); cudaFree(h->vc);
     cudaFree(h->sin_tab); cudaFree(h->cos_tab);
     cudaFree(h->ws_m); cudaFree(h->ws_l); cudaFree(h->ws_acc);
-    cudaFree(h->counters); cudaFree(h->err_dev);
+    cudaFree(h->err_dev);
     cudaFree(h->stage_dev); cudaFree(h->scratch);
     if (h->stage_host) cudaFreeHost(h->stage_host);
     if (h->stream) cudaStreamDestroy(h->stream);
