@@ -99,16 +99,14 @@ struct DecodeCfg {
     static constexpr size_t PBUF_OFF = NEWROW_OFF + 2 * ROW_BYTES;
     static constexpr size_t BAR_OFF = (PBUF_OFF + NCW * 32 * 4 + 15) / 16 * 16;
     static constexpr size_t SMEM = BAR_OFF + 2 * STAGES * 8;
-    // Epilogue scratch reuses the ring: own (M, L) [G] each, warp weights
-    // [G][8], then the per-warp (acc, m, l) of the intra-CTA merge.
+    // Epilogue scratch reuses the ring: the per-warp (acc, m, l) of the
+    // intra-CTA merge.
     static constexpr int RING_FLOATS = (int)(RING_BYTES / 4);
-    static constexpr int FRONT = (2 * G + 8 * G + 31) / 32 * 32;
     static constexpr int INTRA = NCW * GS * D + 2 * NCW * GS;
     static_assert(D % 4 == 0, "rows must be 16-byte multiples");
     static_assert(32 % G == 0 && G <= 8, "G in {1, 2, 4, 8}");
-    static_assert(FRONT + INTRA <= RING_FLOATS, "epilogue scratch must fit in the ring");
+    static_assert(INTRA <= RING_FLOATS, "epilogue scratch must fit in the ring");
     static_assert(NSET >= 1 && THREADS <= 288, "at most eight consumer warps");
-    static_assert(WPH <= 8, "warp weights: eight per head");
 };
 
 // NeoX rotation of element d of a head row x (src/pickle_fast.c:1917-1924).
@@ -306,6 +304,11 @@ decode_splitkv_kernel(const DecodeArgs a) {
     const float* kbase = a.kc + head_off + (size_t)row0 * D;
     const float* vbase = a.vc + head_off + (size_t)row0 * D;
     const int n_tiles = (n_rows + C::TP - 1) / C::TP;
+    // A short split (small batches, where every CTA starts at once) puts only
+    // its first tile in flight and requests the other stages once it lands:
+    // the first tiles then arrive early and compute overlaps the rest of the
+    // stream, instead of every CTA's tiles arriving interleaved at the end.
+    const bool stagger = n_tiles <= 2 * C::STAGES;
     const float* sr = a.sin_tab + (size_t)qpos * a.half;
     const float* cr = a.cos_tab + (size_t)qpos * a.half;
 
@@ -329,6 +332,7 @@ decode_splitkv_kernel(const DecodeArgs a) {
             s_abort = 0;
             s_issued = 0;
             first_issued = n_tiles < C::STAGES ? n_tiles : C::STAGES;
+            if (stagger && first_issued > 1) first_issued = 1;
             for (int it = 0; it < first_issued; ++it) {
                 const int rows = min(C::TP, n_rows - it * C::TP);
                 const uint32_t bytes = (uint32_t)rows * C::ROW_BYTES;
@@ -375,6 +379,11 @@ decode_splitkv_kernel(const DecodeArgs a) {
             int issued = first_issued;
             for (int it = first_issued; it < n_tiles; ++it) {
                 const int s = it % C::STAGES;
+                if (stagger && it == 1 && !mbar_wait(&full[0], 0)) {
+                    record_error(a.err, PCU_DEVERR_EMPTY_WAIT);
+                    s_abort = 1;
+                    break;
+                }
                 if (it >= C::STAGES && !mbar_wait(&empty[s], ((it / C::STAGES) - 1) & 1)) {
                     record_error(a.err, PCU_DEVERR_EMPTY_WAIT);
                     s_abort = 1;
@@ -446,10 +455,7 @@ decode_splitkv_kernel(const DecodeArgs a) {
     // ---- epilogue: merge the warps holding each query head's state ----
     constexpr int GS = C::GS;
     const size_t gidx = (size_t)z * a.HK + kvh;
-    float* own_M = ring;                                // [G]
-    float* own_L = own_M + G;                           // [G]
-    float* sm_ww = own_L + G;                           // [G][8] weights of the warps of a head
-    float* sm_acc = ring + C::FRONT;                    // [NCW][GS][D]
+    float* sm_acc = ring;                               // [NCW][GS][D]
     float* sm_m = sm_acc + C::NCW * GS * D;             // [NCW][GS]
     float* sm_l = sm_m + C::NCW * GS;                   // [NCW][GS]
     // Warp j (0 <= j < WPH) holding state of local head gl of head group hg.
@@ -469,27 +475,25 @@ decode_splitkv_kernel(const DecodeArgs a) {
             }
     }
     __syncthreads();
-    if (warp < G) {                                     // warp g: weights of the WPH warps of head g
-        const int g = warp, hg = g / GS, gl = g % GS;
-        const float mw = lane < C::WPH ? sm_m[head_warp(hg, lane) * GS + gl] : -INFINITY;
-        const float lw = lane < C::WPH ? sm_l[head_warp(hg, lane) * GS + gl] : 0.f;
-        float M = mw;
-        #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        const float e = (mw == -INFINITY) ? 0.f : expf(mw - M);
-        float L = lw * e;
-        #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-        if (lane < C::WPH) sm_ww[g * 8 + lane] = e;
-        if (lane == 0) { own_M[g] = M; own_L[g] = L; }
-    }
-    __syncthreads();
 
+    // Thread (g, c): weights of the WPH warps holding head g, computed by
+    // every thread of the head (no second barrier), then chunk c of the
+    // head's partial.
     for (int idx = tid; idx < G * C::NCH; idx += C::THREADS) {
         const int g = idx / C::NCH, c = idx % C::NCH, hg = g / GS, gl = g % GS;
-        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+        float mw[C::WPH];
+        float M = -INFINITY;
+        #pragma unroll
         for (int j = 0; j < C::WPH; ++j) {
-            const float e = sm_ww[g * 8 + j];
+            mw[j] = sm_m[head_warp(hg, j) * GS + gl];
+            M = fmaxf(M, mw[j]);
+        }
+        float L = 0.f;
+        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+        #pragma unroll
+        for (int j = 0; j < C::WPH; ++j) {
+            const float e = (mw[j] == -INFINITY) ? 0.f : expf(mw[j] - M);
+            L = fmaf(sm_l[head_warp(hg, j) * GS + gl], e, L);
             const float4 x = reinterpret_cast<const float4*>(sm_acc + (head_warp(hg, j) * GS + gl) * D)[c];
             A.x = fmaf(e, x.x, A.x); A.y = fmaf(e, x.y, A.y);
             A.z = fmaf(e, x.z, A.z); A.w = fmaf(e, x.w, A.w);
@@ -498,18 +502,17 @@ decode_splitkv_kernel(const DecodeArgs a) {
             // Partial of this split; decode_merge_kernel combines the splits.
             const size_t prow = (gidx * G + g) * a.n_splits + split;
             reinterpret_cast<float4*>(a.ws_acc + prow * D)[c] = A;
-            if (c == 0) { a.ws_m[prow] = own_M[g]; a.ws_l[prow] = own_L[g]; }
+            if (c == 0) { a.ws_m[prow] = M; a.ws_l[prow] = L; }
             continue;
         }
         const size_t row = (size_t)z * a.H + (size_t)kvh * G + g;
         float4* dst = reinterpret_cast<float4*>(a.ao + row * D) + c;
         if (a.out_mode == 0) {
-            const float L = own_L[g];
             const float inv = 1.0f / (L == 0.0f ? 1.0f : L);
             *dst = make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv);
         } else {
             *dst = A;
-            if (c == 0) { a.out_m[row] = own_M[g]; a.out_l[row] = own_L[g]; }
+            if (c == 0) { a.out_m[row] = M; a.out_l[row] = L; }
         }
     }
 }
@@ -548,6 +551,8 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const Merge
     const int S = a.n_splits;
     griddep_wait();                                     // the split kernel's partials are visible
 
+    // Warp 0: split weights w_s = e^(m_s - M) into shared memory and L; the
+    // other warps put their first batch of partial-row loads in flight.
     if (tid < 32) {
         constexpr int MS = kMaxSplits / 32;
         float mv[MS], lv[MS];
@@ -574,7 +579,6 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const Merge
         for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
         if (tid == 0) { s_M = M; s_L = L; }
     }
-    // Every thread's first batch of partial rows is loaded before the weights are needed.
     float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
     const float4* src = reinterpret_cast<const float4*>(a.ws_acc + (size_t)row * S * D) + c;
     float4 x[BATCH];

@@ -203,9 +203,11 @@ def bench_head_sharded(w, rank, world, device, steps, warmup):
 
     e2e_ms = _timed(e2e_step, steps, warmup, device)
     cu.sync(st)
+    splits = cu.decode_plan(w.B, w.ctx)[0]
     cu.close()
     per_gpu = w.kv_bytes / world
     return {"ms": ms, "kernel_ms": kernel_ms, "kernel_GBps_per_gpu": per_gpu / (kernel_ms * 1e-3) / 1e9,
+            "launches_per_step": 2 if splits > 1 else 1, "splits": splits,
             "e2e": {"value": w.kv_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                     "h2d_bytes_per_step": sum(x.numel() * 4 for x in (hq, hk, hv)),
                     "d2h_bytes_per_step": hout.numel() * 4, "ms_per_step": e2e_ms}}
