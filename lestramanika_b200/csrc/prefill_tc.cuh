@@ -205,6 +205,28 @@ PCU_DEV float fast_exp2(float x) {
     return y;
 }
 
+// Two FP32 operations per instruction (sm_100 f32x2): same rounding as two
+// scalar fmaf / additions.
+PCU_DEV float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+PCU_DEV float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
 PCU_DEV uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -415,18 +437,22 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
                     tmem_st32u(o_tm + c * 32, ou);
                 }
             }
-            float sm[8];
+            // Column pairs: x * scale - m and the row-sum additions as f32x2
+            // (one instruction per pair instead of two).
+            float2 sm2[4];
             #pragma unroll
-            for (int i = 0; i < 8; ++i) sm[i] = 0.f;
+            for (int i = 0; i < 4; ++i) sm2[i] = make_float2(0.f, 0.f);
             uint32_t pk[BN / 2];
+            const float2 sc2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-m_run, -m_run);
             #pragma unroll
             for (int c = 0; c < BN; c += 2) {
-                const float p0 = fast_exp2(fmaf(s[c], a.scale_log2, -m_run));
-                const float p1 = fast_exp2(fmaf(s[c + 1], a.scale_log2, -m_run));
-                sm[(c >> 1) & 7] += p0 + p1;
-                pk[c >> 1] = pack_bf16x2(p0, p1);
+                const float2 x = ffma2(make_float2(s[c], s[c + 1]), sc2, nm2);
+                const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+                sm2[(c >> 1) & 3] = fadd2(sm2[(c >> 1) & 3], p);
+                pk[c >> 1] = pack_bf16x2(p.x, p.y);
             }
-            const float sum = ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
+            const float2 t = fadd2(fadd2(sm2[0], sm2[1]), fadd2(sm2[2], sm2[3]));
+            const float sum = t.x + t.y;
             l_run = l_run * alpha + sum;
             tmem_st64(s_tm, pk);                                  // P_X over S_X columns [0, 64)
             tmem_st_wait();

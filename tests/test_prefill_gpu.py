@@ -133,3 +133,29 @@ def test_prefill_attn_bf16_entry_matches_torch_fp32(B, T, H, HK):
     ref = torch.softmax(s.masked_fill(mask, float("-inf")), dim=-1) @ vv        # [B][H][T][D]
     err_abs = float((ao.permute(0, 2, 1, 3) - ref).abs().max())
     assert err_abs <= 1e-2, err_abs
+
+
+def test_prefill_bf16_batched_long_prompt_matches_f32_path():
+    """A batched full-length GQA prompt (B=2, T=2048, 8 query / 4 KV heads):
+    the KV cache the tensor-core path writes equals the F32 path's bit for
+    bit, and every output row of every head is within the BF16 bar of the
+    F32 path (itself checked against the oracle above)."""
+    B, T, H, HK, D, theta = 2, 2048, 8, 4, 128, 10000.0
+    dev = torch.device("cuda", 0)
+    q, k, v = normal(13, (B, T, H, D), 1), normal(13, (B, T, HK, D), 2), normal(13, (B, T, HK, D), 3)
+    qd, kd, vd = (torch.from_numpy(x).to(dev) for x in (q, k, v))
+    outs, caches = [], []
+    for precision in (PREFILL_F32, PREFILL_BF16):
+        cu = PickleCuda(1, H, HK, D, T, rope_theta=theta, n_seqs=B)
+        ao = torch.full((B, T, H, D), float("nan"), device=dev)
+        cu.prefill_dev(0, B, 0, T, qd, kd, vd, ao, precision)
+        cu.sync()
+        kt, vt = cu.kv_tensors(0)
+        outs.append(ao.cpu().numpy())
+        caches.append((kt.cpu().numpy(), vt.cpu().numpy()))
+        cu.close()
+    np.testing.assert_array_equal(caches[1][0], caches[0][0])
+    np.testing.assert_array_equal(caches[1][1], caches[0][1])
+    assert np.isfinite(outs[1]).all()
+    err = float(np.max(np.abs(outs[1] - outs[0])))
+    assert err <= BF16_ABS_TOL, err
