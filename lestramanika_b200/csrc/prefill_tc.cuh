@@ -272,10 +272,13 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     __shared__ int s_abort, s_issued;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // Consecutive CTAs share (sequence, head), so a head's K/V tiles stay in
-    // L2 while its query blocks run; heaviest (latest) query blocks first.
-    const int qb = a.n_qb - 1 - (int)blockIdx.x;
-    const int h = blockIdx.y, seq = blockIdx.z;
+    // Dispatch order (x fastest): every head's heaviest (latest) query block
+    // of a sequence, then the next-lighter ones, sequence by sequence. The
+    // longest CTAs start first (the light ones fill the tail) and the K/V of
+    // one sequence's heads is what the resident CTAs share in L2.
+    const int h = blockIdx.x;
+    const int qb = a.n_qb - 1 - (int)blockIdx.y;
+    const int seq = blockIdx.z;
     const int q0 = qb * 2 * BM;
     const int kvh = h * a.HK / a.H;                         // src/pickle_fast.c:1963
     const int kv_tiles_T = (a.T + BN - 1) / BN;
@@ -601,7 +604,7 @@ inline int prefill_tc_launch(const __nv_bfloat16* q, const __nv_bfloat16* k, con
     a.n_qb = (T + 2 * tc::BM - 1) / (2 * tc::BM);
     a.scale_log2 = scale * 1.4426950408889634f;
     a.err = err;
-    dim3 grid((unsigned)a.n_qb, (unsigned)H, (unsigned)n_seqs);
+    dim3 grid((unsigned)H, (unsigned)a.n_qb, (unsigned)n_seqs);
     tc::prefill_tc_kernel<<<grid, tc::THREADS, tc::SMEM_BYTES, st>>>(tq, tk, tv, to, a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
