@@ -41,6 +41,7 @@ struct pickle_cuda {
     float* ws_acc = nullptr;
     size_t ws_rows = 0;        // capacity in (group * G * split) rows
     int* err_dev = nullptr;
+    unsigned* prefill_next = nullptr;   // next-item counter of the persistent prefill, zero between launches
     cudaStream_t stream = nullptr;
     // Host-buffer entry points: pinned staging and its device mirror.
     float* stage_host = nullptr;
@@ -253,6 +254,8 @@ int take_device_error(pickle_cuda* h, cudaStream_t st) {
     if (err != 0) {
         snprintf(h->last_error, sizeof(h->last_error), "device wait gave up (code %d)", err);
         PCU_CHECK(h, cudaMemsetAsync(h->err_dev, 0, sizeof(int), st));
+        // A launch that gave up may leave the persistent prefill's item counter part-way.
+        PCU_CHECK(h, cudaMemsetAsync(h->prefill_next, 0, sizeof(unsigned), st));
         PCU_CHECK(h, cudaStreamSynchronize(st));
         return PICKLE_ERR_DEVICE;
     }
@@ -339,6 +342,8 @@ int pickle_cuda_init(const pickle_cuda_params_t* p, int device, pickle_cuda_t** 
          cudaMalloc(&h->ws_l, h->ws_rows * sizeof(float)) == cudaSuccess &&
          cudaMalloc(&h->ws_acc, h->ws_rows * h->D * sizeof(float)) == cudaSuccess &&
          cudaMalloc(&h->err_dev, sizeof(int)) == cudaSuccess &&
+         cudaMalloc(&h->prefill_next, sizeof(unsigned)) == cudaSuccess &&
+         cudaMemset(h->prefill_next, 0, sizeof(unsigned)) == cudaSuccess &&
          cudaMemset(h->err_dev, 0, sizeof(int)) == cudaSuccess;
     if (!ok) return bail(PICKLE_ERR_MEMORY);
     if (prepare_kernel(h, h->decode) != PICKLE_OK) return bail(PICKLE_ERR_DEVICE);
@@ -355,6 +360,7 @@ void pickle_cuda_free(pickle_cuda_t* h) {
     cudaFree(h->sin_tab); cudaFree(h->cos_tab);
     cudaFree(h->ws_m); cudaFree(h->ws_l); cudaFree(h->ws_acc);
     cudaFree(h->err_dev);
+    cudaFree(h->prefill_next);
     cudaFree(h->stage_dev); cudaFree(h->scratch);
     if (h->stage_host) cudaFreeHost(h->stage_host);
     if (h->stream) cudaStreamDestroy(h->stream);
@@ -464,7 +470,8 @@ int pickle_cuda_prefill_attn_bf16_dev(int n_seqs, int T, int n_heads, int n_kv_h
     char msg[256];
     int rc = prefill_tc_launch((const __nv_bfloat16*)q_bf16, (const __nv_bfloat16*)k_bf16,
                                (const __nv_bfloat16*)v_bf16, ao, n_seqs, T, n_heads, n_kv_heads, head_dim,
-                               1.0f / sqrtf((float)head_dim), err_flag, (cudaStream_t)stream, msg, sizeof(msg));
+                               1.0f / sqrtf((float)head_dim), err_flag, nullptr, (cudaStream_t)stream, msg,
+                               sizeof(msg));
     if (rc != 0) fprintf(stderr, "pickle_cuda_prefill_attn_bf16_dev: %s\n", msg);
     return rc == 0 ? PICKLE_OK : (rc == -6 ? PICKLE_ERR_ARG : PICKLE_ERR_DEVICE);
 }
@@ -599,7 +606,8 @@ int prefill_launch(pickle_cuda* h, int layer, int n_seqs, size_t pos0, size_t T,
     launch_rope_append(ra, (int)T, n_seqs, st);
     PCU_CHECK(h, cudaGetLastError());
     return prefill_tc_launch(ra.q_bf16, ra.k_bf16, ra.v_bf16, ao, n_seqs, (int)T, h->H, h->HK, h->D,
-                             1.0f / sqrtf((float)h->D), h->err_dev, st, h->last_error, sizeof(h->last_error));
+                             1.0f / sqrtf((float)h->D), h->err_dev, h->prefill_next, st, h->last_error,
+                             sizeof(h->last_error));
 }
 
 }  // namespace

@@ -8,23 +8,28 @@
 // (written by rope_append_kernel), accumulation is F32 in tensor memory,
 // the output is F32.
 //
-// One CTA owns two 128-row query tiles (A = rows q0..q0+127, B = the next
-// 128) of one (sequence, head); both share every K/V tile.
-//   warp 8      one lane loads Q_A, Q_B once and K/V tiles (128 keys) into a
-//               2-stage ring with 3-D TMA tensor copies (128-byte swizzle,
-//               no multicast);
-//   warp 9      allocates 512 TMEM columns - S_A, S_B, O_A, O_B, 128 each -
-//               and one lane issues tcgen05.mma in the order
+// Work item: two 128-row query tiles (A = rows q0..q0+127, B = the next
+// 128) of one (sequence, head); both share every K/V tile. The kernel is
+// persistent: one CTA per SM takes items from a shared counter (heaviest
+// first: every head's latest query block of a sequence, then the next
+// lighter ones), and one item's tail overlaps the next item's start.
+//   warp 8      one lane takes the next item, loads Q_A, Q_B (once the last
+//               QK^T MMA of the previous item has read them) and streams K/V
+//               tiles (128 keys) through a 2-stage ring with 3-D TMA tensor
+//               copies (128-byte swizzle, no multicast);
+//   warp 9      allocates 512 TMEM columns once - S_A, S_B, O_A, O_B, 128
+//               each - and one lane issues tcgen05.mma in the order
 //               PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): S_X = Q_X K^T (both
-//               operands in shared memory), O_X += P_X V (P_X read from
-//               TMEM, V read MN-major from shared memory);
+//               operands in shared memory), O_X += P_X V (P_X read from TMEM,
+//               V read MN-major from shared memory). An item's first PV_X
+//               waits until the previous item's O_X has been read out;
 //   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B: thread r
 //               owns query row r (TMEM lane r). It loads its S row
 //               (tcgen05.ld), masks, keeps the running max in the log2
 //               domain (rescaling its O row in TMEM only when the max grows by
 //               more than 2^8), writes P as packed BF16 over the first 64
-//               columns of its S row (tcgen05.st) and at the end normalises
-//               and stores its O row.
+//               columns of its S row (tcgen05.st). At the item's end it reads
+//               its O row, releases O_X and stores the normalised row.
 // MMAs issued by one thread execute in order, so S_FULL_X(j) also means
 // PV_X(j-1) is complete (O_X may be rescaled), and S_X(j+1) cannot overwrite
 // P_X(j) before PV_X(j) has read it. While one tile's softmax runs, the
@@ -49,17 +54,21 @@ constexpr int TILE_BYTES = 2 * HALF_BYTES; // 128 x 128 bf16
 constexpr int STAGES = 2;
 constexpr int SMEM_Q = 0;                                    // Q_A, Q_B
 constexpr int SMEM_KV = SMEM_Q + 2 * TILE_BYTES;             // stage s: K at +2s*TILE, V at +(2s+1)*TILE
-constexpr int SMEM_BAR = SMEM_KV + STAGES * 2 * TILE_BYTES;
-constexpr int N_BARS = 16;
+constexpr int SMEM_OUT = SMEM_KV + STAGES * 2 * TILE_BYTES;  // per softmax warp: 32 rows x 32 floats
+constexpr int OUT_STAGE_BYTES = 32 * 32 * 4;
+constexpr int SMEM_BAR = SMEM_OUT + 8 * OUT_STAGE_BYTES;
+constexpr int N_BARS = 20;
 constexpr int SMEM_BYTES = SMEM_BAR + N_BARS * 8 + 16 + 1024; // + TMEM address slot + alignment slack
+static_assert(SMEM_BYTES <= 232448, "dynamic shared memory of one CTA on sm_100");
 constexpr int WARP_TMA = 8, WARP_MMA = 9;
 constexpr int THREADS = 320;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
-// Barrier slots.
-enum { B_Q = 0, B_KV_FULL = 1, B_KV_EMPTY = 3, B_S_FULL = 5 /* +tile */, B_P_FULL = 7 /* +tile */, B_O_DONE = 9,
-       B_DRAIN = 10 };
+// Barrier slots (+x: tile A / B, +s: ring stage, +i: item slot).
+enum { B_Q_FULL = 0, B_Q_FREE = 1, B_KV_FULL = 2, B_KV_EMPTY = 4, B_S_FULL = 6, B_P_FULL = 8, B_O_DONE = 10,
+       B_O_FREE = 12, B_ITEM_FULL = 14, B_ITEM_EMPTY = 16, B_DRAIN = 18 };
+constexpr int SOFTMAX_WARPS = 8;
 
 // tcgen05 instruction descriptor, kind::f16: F32 accumulate, BF16 A and B,
 // M = 128, N = 128, A K-major, B K-major (b_mn = 0) or MN-major (b_mn = 1).
@@ -85,16 +94,6 @@ PCU_DEV void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
         : "memory");
 }
-
-// Shared -> global tensor store (no multicast), bulk-group completion.
-PCU_DEV void tma_store_4d(const CUtensorMap* map, uint32_t src, int x, int y, int z, int w) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
-        ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(x), "r"(y), "r"(z), "r"(w)
-        : "memory");
-}
-PCU_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-PCU_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
 PCU_DEV void tmem_alloc(uint32_t* slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
@@ -130,7 +129,6 @@ PCU_DEV void mma_commit(uint64_t* bar) {
 
 PCU_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 PCU_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-PCU_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // 32 consecutive 32-bit columns of this thread's TMEM lane. The wait is in
 // the same asm statement, so no use of the outputs can be scheduled before
@@ -235,9 +233,30 @@ PCU_DEV uint32_t pack_bf16x2(float lo, float hi) {
 struct PrefillTcArgs {
     float* ao;            // [n_seqs][T][H][D] F32
     int T, H, HK, n_qb;   // n_qb = query blocks of 2 * BM rows
+    int n_seqs;
+    int n_items;          // n_seqs * n_qb * H
     float scale_log2;     // log2(e) / sqrtf(D)
+    unsigned* next_item;  // zero between launches; the last CTA to take from it resets it
     int* err;
 };
+
+struct PrefillItem {
+    int h, seq, q0, n_kv_A, n_kv_B;
+};
+
+// Item i: head fastest, then query blocks latest (heaviest) first, then sequences.
+PCU_DEV PrefillItem prefill_item(int i, const PrefillTcArgs& a) {
+    PrefillItem it;
+    it.h = i % a.H;
+    const int r = i / a.H;
+    const int qb = a.n_qb - 1 - r % a.n_qb;
+    it.seq = r / a.n_qb;
+    it.q0 = qb * 2 * BM;
+    const int kv_tiles_T = (a.T + BN - 1) / BN;
+    it.n_kv_A = min(it.q0 / BN + 1, kv_tiles_T);
+    it.n_kv_B = min((it.q0 + BM) / BN + 1, kv_tiles_T);
+    return it;
+}
 
 // S_X = Q_X K_j^T: M=128, N=128, K=HD in steps of 16 (32 bytes of a 128-byte swizzle row).
 PCU_DEV void issue_qk(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr) {
@@ -260,8 +279,7 @@ PCU_DEV void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, bool fi
 
 __global__ void __launch_bounds__(THREADS, 1)
 prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                  const PrefillTcArgs a) {
+                  const __grid_constant__ CUtensorMap tm_v, const PrefillTcArgs a) {
     extern __shared__ unsigned char smem_raw[];
     // 1024-byte aligned base (128-byte swizzle atoms).
     const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -269,69 +287,80 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     unsigned char* base = smem_raw + (base_u32 - raw_u32);
     uint64_t* bars = reinterpret_cast<uint64_t*>(base + SMEM_BAR);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + SMEM_BAR + N_BARS * 8);
-    __shared__ int s_abort, s_issued;
+    __shared__ int s_abort, s_kv_issued, s_q_issued;
+    __shared__ int s_item[2];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // Dispatch order (x fastest): every head's heaviest (latest) query block
-    // of a sequence, then the next-lighter ones, sequence by sequence. The
-    // longest CTAs start first (the light ones fill the tail) and the K/V of
-    // one sequence's heads is what the resident CTAs share in L2.
-    const int h = blockIdx.x;
-    const int qb = a.n_qb - 1 - (int)blockIdx.y;
-    const int seq = blockIdx.z;
-    const int q0 = qb * 2 * BM;
-    const int kvh = h * a.HK / a.H;                         // src/pickle_fast.c:1963
-    const int kv_tiles_T = (a.T + BN - 1) / BN;
-    const int n_kv_A = min(q0 / BN + 1, kv_tiles_T);
-    const int n_kv_B = min((q0 + BM) / BN + 1, kv_tiles_T);
-
     if (tid == 0) {
-        mbar_init(&bars[B_Q], 1);
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&bars[B_KV_FULL + s], 1);
-            mbar_init(&bars[B_KV_EMPTY + s], 1);
-        }
+        mbar_init(&bars[B_Q_FULL], 1);
+        mbar_init(&bars[B_Q_FREE], 1);
         for (int x = 0; x < 2; ++x) {
+            mbar_init(&bars[B_KV_FULL + x], 1);
+            mbar_init(&bars[B_KV_EMPTY + x], 1);
             mbar_init(&bars[B_S_FULL + x], 1);
             mbar_init(&bars[B_P_FULL + x], 4);
+            mbar_init(&bars[B_O_DONE + x], 1);
+            mbar_init(&bars[B_O_FREE + x], 4);
+            mbar_init(&bars[B_ITEM_FULL + x], 1);
+            mbar_init(&bars[B_ITEM_EMPTY + x], 1 + SOFTMAX_WARPS);
         }
-        mbar_init(&bars[B_O_DONE], 1);
         mbar_init(&bars[B_DRAIN], 1);
         mbar_fence_init();
         s_abort = 0;
-        s_issued = 0;
+        s_kv_issued = 0;
+        s_q_issued = 0;
     }
     if (warp == WARP_MMA) tmem_alloc(tmem_slot, TMEM_COLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    auto aborted = [&]() { return *(volatile int*)&s_abort != 0; };
+    auto fail = [&](int code) { record_error(a.err, code); s_abort = 1; };
 
     if (warp == WARP_TMA) {
-        // ---------------- TMA producer ----------------
+        // ---------------- items, Q and the K/V ring ----------------
         if (lane == 0) {
-            const int zq = seq * a.H + h, zk = seq * a.HK + kvh;
-            mbar_arrive_expect_tx(&bars[B_Q], 2 * TILE_BYTES);
-            for (int x = 0; x < 2; ++x) {
-                tma_load_3d(base_u32 + SMEM_Q + x * TILE_BYTES, &tm_q, 0, q0 + x * BM, zq, &bars[B_Q]);
-                tma_load_3d(base_u32 + SMEM_Q + x * TILE_BYTES + HALF_BYTES, &tm_q, 64, q0 + x * BM, zq, &bars[B_Q]);
-            }
-            for (int j = 0; j < n_kv_B; ++j) {
-                const int s = j % STAGES;
-                if (j >= STAGES && !mbar_wait(&bars[B_KV_EMPTY + s], ((j / STAGES) - 1) & 1)) {
-                    record_error(a.err, PCU_DEVERR_EMPTY_WAIT);
-                    s_abort = 1;
-                    break;
+            int g = 0;                                  // K/V tiles issued so far
+            for (int k = 0;; ++k) {
+                const int slot = k & 1;
+                if (k >= 2 && !mbar_wait(&bars[B_ITEM_EMPTY + slot], ((k >> 1) - 1) & 1)) { fail(PCU_DEVERR_EMPTY_WAIT); break; }
+                if (aborted()) break;
+                const unsigned idx = atomicAdd(a.next_item, 1u);
+                // Every CTA takes exactly one index past the end: the last of those resets the counter.
+                if (idx == (unsigned)a.n_items + gridDim.x - 1u) *a.next_item = 0u;
+                s_item[slot] = idx < (unsigned)a.n_items ? (int)idx : -1;
+                mbar_arrive(&bars[B_ITEM_FULL + slot]);
+                if (idx >= (unsigned)a.n_items) break;
+                const PrefillItem it = prefill_item((int)idx, a);
+                const int kvh = it.h * a.HK / a.H;     // src/pickle_fast.c:1963
+                const int zq = it.seq * a.H + it.h, zk = it.seq * a.HK + kvh;
+                // Q_A, Q_B may be overwritten once the previous item's last QK^T MMA has completed.
+                if (k >= 1 && !mbar_wait(&bars[B_Q_FREE], (k - 1) & 1)) { fail(PCU_DEVERR_EMPTY_WAIT); break; }
+                mbar_arrive_expect_tx(&bars[B_Q_FULL], 2 * TILE_BYTES);
+                for (int x = 0; x < 2; ++x) {
+                    tma_load_3d(base_u32 + SMEM_Q + x * TILE_BYTES, &tm_q, 0, it.q0 + x * BM, zq, &bars[B_Q_FULL]);
+                    tma_load_3d(base_u32 + SMEM_Q + x * TILE_BYTES + HALF_BYTES, &tm_q, 64, it.q0 + x * BM, zq,
+                                &bars[B_Q_FULL]);
                 }
-                if (*(volatile int*)&s_abort) break;
-                const uint32_t kdst = base_u32 + SMEM_KV + (2 * s) * TILE_BYTES;
-                const uint32_t vdst = kdst + TILE_BYTES;
-                mbar_arrive_expect_tx(&bars[B_KV_FULL + s], 2 * TILE_BYTES);
-                tma_load_3d(kdst, &tm_k, 0, j * BN, zk, &bars[B_KV_FULL + s]);
-                tma_load_3d(kdst + HALF_BYTES, &tm_k, 64, j * BN, zk, &bars[B_KV_FULL + s]);
-                tma_load_3d(vdst, &tm_v, 0, j * BN, zk, &bars[B_KV_FULL + s]);
-                tma_load_3d(vdst + HALF_BYTES, &tm_v, 64, j * BN, zk, &bars[B_KV_FULL + s]);
-                s_issued = j + 1;
+                s_q_issued = k + 1;
+                for (int j = 0; j < it.n_kv_B; ++j, ++g) {
+                    const int s = g % STAGES;
+                    if (g >= STAGES && !mbar_wait(&bars[B_KV_EMPTY + s], ((g / STAGES) - 1) & 1)) {
+                        fail(PCU_DEVERR_EMPTY_WAIT);
+                        break;
+                    }
+                    if (aborted()) break;
+                    const uint32_t kdst = base_u32 + SMEM_KV + (2 * s) * TILE_BYTES;
+                    const uint32_t vdst = kdst + TILE_BYTES;
+                    mbar_arrive_expect_tx(&bars[B_KV_FULL + s], 2 * TILE_BYTES);
+                    tma_load_3d(kdst, &tm_k, 0, j * BN, zk, &bars[B_KV_FULL + s]);
+                    tma_load_3d(kdst + HALF_BYTES, &tm_k, 64, j * BN, zk, &bars[B_KV_FULL + s]);
+                    tma_load_3d(vdst, &tm_v, 0, j * BN, zk, &bars[B_KV_FULL + s]);
+                    tma_load_3d(vdst + HALF_BYTES, &tm_v, 64, j * BN, zk, &bars[B_KV_FULL + s]);
+                    s_kv_issued = g + 1;
+                }
+                if (aborted()) break;
             }
         }
     } else if (warp == WARP_MMA) {
@@ -339,54 +368,71 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         if (lane == 0) {
             const uint32_t qA = base_u32 + SMEM_Q, qB = qA + TILE_BYTES;
             const uint32_t sA = tmem, sB = tmem + 128, oA = tmem + 256, oB = tmem + 384;
-            int kv_ready = -1;
-            bool ok = mbar_wait(&bars[B_Q], 0);
-            auto wait_kv = [&](int j) {
-                if (ok && j > kv_ready) {
-                    ok = mbar_wait(&bars[B_KV_FULL + j % STAGES], (j / STAGES) & 1);
-                    kv_ready = j;
+            auto k_addr = [&](int g) { return base_u32 + SMEM_KV + (2 * (g % STAGES)) * TILE_BYTES; };
+            bool ok = true;
+            int g0 = 0, kv_ready = -1, pa = 0, pb = 0;
+            auto wait_kv = [&](int g) {
+                if (ok && g > kv_ready) {
+                    ok = mbar_wait(&bars[B_KV_FULL + g % STAGES], (g / STAGES) & 1);
+                    kv_ready = g;
                 }
                 tc_fence_after();
             };
-            auto k_addr = [&](int j) { return base_u32 + SMEM_KV + (2 * (j % STAGES)) * TILE_BYTES; };
-            wait_kv(0);
-            if (ok) {
-                issue_qk(sA, qA, k_addr(0));
+            for (int k = 0; ok; ++k) {
+                const int slot = k & 1;
+                ok = mbar_wait(&bars[B_ITEM_FULL + slot], (k >> 1) & 1);
+                if (!ok) break;
+                const int idx = *(volatile int*)&s_item[slot];
+                mbar_arrive(&bars[B_ITEM_EMPTY + slot]);
+                if (idx < 0) break;
+                const PrefillItem it = prefill_item(idx, a);
+                ok = mbar_wait(&bars[B_Q_FULL], k & 1);
+                wait_kv(g0);
+                if (!ok) break;
+                issue_qk(sA, qA, k_addr(g0));
                 mma_commit(&bars[B_S_FULL + 0]);
-                issue_qk(sB, qB, k_addr(0));
+                issue_qk(sB, qB, k_addr(g0));
                 mma_commit(&bars[B_S_FULL + 1]);
-            }
-            for (int j = 0; ok && j < n_kv_B; ++j) {
-                const uint32_t vaddr = k_addr(j) + TILE_BYTES;
-                if (j < n_kv_A) {
-                    ok = mbar_wait(&bars[B_P_FULL + 0], j & 1);
+                if (it.n_kv_B == 1) mma_commit(&bars[B_Q_FREE]);
+                for (int j = 0; ok && j < it.n_kv_B; ++j) {
+                    const int g = g0 + j;
+                    const uint32_t vaddr = k_addr(g) + TILE_BYTES;
+                    if (j < it.n_kv_A) {
+                        ok = mbar_wait(&bars[B_P_FULL + 0], pa & 1);
+                        ++pa;
+                        // O_A is overwritten by the first PV: the previous item's O_A must be read out.
+                        if (ok && j == 0 && k > 0) ok = mbar_wait(&bars[B_O_FREE + 0], (k - 1) & 1);
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue_pv(oA, sA, vaddr, j == 0);
+                        if (j + 1 == it.n_kv_A) mma_commit(&bars[B_O_DONE + 0]);
+                        if (j + 1 < it.n_kv_A) {
+                            wait_kv(g + 1);
+                            if (!ok) break;
+                            issue_qk(sA, qA, k_addr(g + 1));
+                            mma_commit(&bars[B_S_FULL + 0]);
+                        }
+                    }
+                    ok = mbar_wait(&bars[B_P_FULL + 1], pb & 1);
+                    ++pb;
+                    if (ok && j == 0 && k > 0) ok = mbar_wait(&bars[B_O_FREE + 1], (k - 1) & 1);
                     if (!ok) break;
                     tc_fence_after();
-                    issue_pv(oA, sA, vaddr, j == 0);
-                    if (j + 1 < n_kv_A) {
-                        wait_kv(j + 1);
+                    issue_pv(oB, sB, vaddr, j == 0);
+                    if (j + 1 == it.n_kv_B) mma_commit(&bars[B_O_DONE + 1]);
+                    if (j + 1 < it.n_kv_B) {
+                        wait_kv(g + 1);
                         if (!ok) break;
-                        issue_qk(sA, qA, k_addr(j + 1));
-                        mma_commit(&bars[B_S_FULL + 0]);
+                        issue_qk(sB, qB, k_addr(g + 1));
+                        mma_commit(&bars[B_S_FULL + 1]);
+                        // S_B of the item's last K/V tile is its last read of Q_A / Q_B.
+                        if (j + 2 == it.n_kv_B) mma_commit(&bars[B_Q_FREE]);
                     }
+                    mma_commit(&bars[B_KV_EMPTY + g % STAGES]);
                 }
-                ok = mbar_wait(&bars[B_P_FULL + 1], j & 1);
-                if (!ok) break;
-                tc_fence_after();
-                issue_pv(oB, sB, vaddr, j == 0);
-                if (j + 1 < n_kv_B) {
-                    wait_kv(j + 1);
-                    if (!ok) break;
-                    issue_qk(sB, qB, k_addr(j + 1));
-                    mma_commit(&bars[B_S_FULL + 1]);
-                }
-                mma_commit(&bars[B_KV_EMPTY + j % STAGES]);
+                g0 += it.n_kv_B;
             }
-            if (ok) mma_commit(&bars[B_O_DONE]);
-            if (!ok) {
-                record_error(a.err, PCU_DEVERR_MMA_WAIT);
-                s_abort = 1;
-            }
+            if (!ok) fail(PCU_DEVERR_MMA_WAIT);
             // Let every MMA this thread issued finish before TMEM can be freed.
             mma_commit(&bars[B_DRAIN]);
             if (!mbar_wait(&bars[B_DRAIN], 0)) record_error(a.err, PCU_DEVERR_DRAIN_WAIT);
@@ -395,117 +441,140 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         // ---------------- softmax: one thread per query row of tile X ----------------
         const int x = warp >> 2;                                  // 0 = tile A, 1 = tile B
         const int row = (warp & 3) * 32 + lane;                   // TMEM lane = row in tile
-        const int qx0 = q0 + x * BM;
-        const int q = qx0 + row;
-        const int n_kv = x ? n_kv_B : n_kv_A;
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t s_tm = tmem + x * 128 + lane_off, o_tm = tmem + 256 + x * 128 + lane_off;
-        float m_run = -INFINITY, l_run = 0.f;
+        int sc = 0;                                               // S_FULL_X phases consumed
         bool ok = true;
-        for (int j = 0; j < n_kv; ++j) {
-            ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_S_FULL + x], j & 1));
+        for (int k = 0; ok; ++k) {
+            const int slot = k & 1;
+            ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_ITEM_FULL + slot], (k >> 1) & 1));
+            if (!ok) break;
+            const int idx = *(volatile int*)&s_item[slot];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[B_ITEM_EMPTY + slot]);
+            if (idx < 0) break;
+            const PrefillItem it = prefill_item(idx, a);
+            const int qx0 = it.q0 + x * BM;
+            const int q = qx0 + row;
+            const int n_kv = x ? it.n_kv_B : it.n_kv_A;
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int j = 0; j < n_kv; ++j, ++sc) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_S_FULL + x], sc & 1));
+                if (!ok) break;
+                tc_fence_after();
+                float s[BN];
+                tmem_ld128(s_tm, s);
+                const int k0 = j * BN;
+                if (k0 + BN - 1 > qx0 || k0 + BN > a.T) {
+                    #pragma unroll
+                    for (int c = 0; c < BN; ++c)
+                        if (k0 + c > q || k0 + c >= a.T) s[c] = -INFINITY;
+                }
+                float mx[8];
+                #pragma unroll
+                for (int i = 0; i < 8; ++i) mx[i] = s[i];
+                #pragma unroll
+                for (int c = 8; c < BN; ++c) mx[c & 7] = fmaxf(mx[c & 7], s[c]);
+                const float m_all = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                          fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                const float m_tile = m_all * a.scale_log2;
+                float alpha = 1.0f;
+                const bool grow = m_tile > m_run + RESCALE_THRESHOLD || m_run == -INFINITY;
+                if (grow) {
+                    alpha = fast_exp2(m_run - m_tile);
+                    m_run = m_tile;
+                }
+                // S_FULL_X(j) implies PV_X(j-1) finished: O_X is stable here.
+                if (j > 0 && __any_sync(0xffffffffu, grow)) {
+                    #pragma unroll
+                    for (int c = 0; c < HD / 32; ++c) {
+                        float o[32];
+                        tmem_ld32(o_tm + c * 32, o);
+                        uint32_t ou[32];
+                        #pragma unroll
+                        for (int i = 0; i < 32; ++i) ou[i] = __float_as_uint(o[i] * alpha);
+                        tmem_st32u(o_tm + c * 32, ou);
+                    }
+                }
+                // Column pairs: x * scale - m and the row-sum additions as f32x2
+                // (one instruction per pair instead of two).
+                float2 sm2[4];
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) sm2[i] = make_float2(0.f, 0.f);
+                uint32_t pk[BN / 2];
+                const float2 sc2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-m_run, -m_run);
+                #pragma unroll
+                for (int c = 0; c < BN; c += 2) {
+                    const float2 xx = ffma2(make_float2(s[c], s[c + 1]), sc2, nm2);
+                    const float2 p = make_float2(fast_exp2(xx.x), fast_exp2(xx.y));
+                    sm2[(c >> 1) & 3] = fadd2(sm2[(c >> 1) & 3], p);
+                    pk[c >> 1] = pack_bf16x2(p.x, p.y);
+                }
+                const float2 t = fadd2(fadd2(sm2[0], sm2[1]), fadd2(sm2[2], sm2[3]));
+                l_run = l_run * alpha + (t.x + t.y);
+                tmem_st64(s_tm, pk);                              // P_X over S_X columns [0, 64)
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars[B_P_FULL + x]);
+            }
+            if (!ok) break;
+            // Item epilogue: read the O row out of TMEM and release O_X for
+            // the next item's first PV.
+            ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_O_DONE + x], k & 1));
             if (!ok) break;
             tc_fence_after();
-            float s[BN];
-            tmem_ld128(s_tm, s);
-            const int k0 = j * BN;
-            if (k0 + BN - 1 > qx0 || k0 + BN > a.T) {
-                #pragma unroll
-                for (int c = 0; c < BN; ++c)
-                    if (k0 + c > q || k0 + c >= a.T) s[c] = -INFINITY;
-            }
-            float mx[8];
-            #pragma unroll
-            for (int i = 0; i < 8; ++i) mx[i] = s[i];
-            #pragma unroll
-            for (int c = 8; c < BN; ++c) mx[c & 7] = fmaxf(mx[c & 7], s[c]);
-            const float m_all = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                      fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-            const float m_tile = m_all * a.scale_log2;
-            float alpha = 1.0f;
-            const bool grow = m_tile > m_run + RESCALE_THRESHOLD || m_run == -INFINITY;
-            if (grow) {
-                alpha = fast_exp2(m_run - m_tile);
-                m_run = m_tile;
-            }
-            // S_FULL_X(j) implies PV_X(j-1) finished: O_X is stable here.
-            if (j > 0 && __any_sync(0xffffffffu, grow)) {
-                #pragma unroll
-                for (int c = 0; c < HD / 32; ++c) {
-                    float o[32];
-                    tmem_ld32(o_tm + c * 32, o);
-                    uint32_t ou[32];
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) ou[i] = __float_as_uint(o[i] * alpha);
-                    tmem_st32u(o_tm + c * 32, ou);
-                }
-            }
-            // Column pairs: x * scale - m and the row-sum additions as f32x2
-            // (one instruction per pair instead of two).
-            float2 sm2[4];
-            #pragma unroll
-            for (int i = 0; i < 4; ++i) sm2[i] = make_float2(0.f, 0.f);
-            uint32_t pk[BN / 2];
-            const float2 sc2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-m_run, -m_run);
-            #pragma unroll
-            for (int c = 0; c < BN; c += 2) {
-                const float2 x = ffma2(make_float2(s[c], s[c + 1]), sc2, nm2);
-                const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-                sm2[(c >> 1) & 3] = fadd2(sm2[(c >> 1) & 3], p);
-                pk[c >> 1] = pack_bf16x2(p.x, p.y);
-            }
-            const float2 t = fadd2(fadd2(sm2[0], sm2[1]), fadd2(sm2[2], sm2[3]));
-            const float sum = t.x + t.y;
-            l_run = l_run * alpha + sum;
-            tmem_st64(s_tm, pk);                                  // P_X over S_X columns [0, 64)
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars[B_P_FULL + x]);
-        }
-        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_O_DONE], 0));
-        if (!ok) {
-            if (lane == 0) { record_error(a.err, PCU_DEVERR_FULL_WAIT); s_abort = 1; }
-        } else {
-            // Epilogue: O_DONE means every MMA and every K/V copy is finished, so
-            // the K/V ring is free. Each warp stages its 32 rows x 128 columns,
-            // normalised, as four 128-byte-swizzled [32 rows][32 floats] boxes
-            // (conflict-free: row r writes 16-byte chunk i at i ^ (r & 7)) and
-            // one lane writes them with TMA tensor stores, which clip rows >= T.
-            tc_fence_after();
-            const float inv = 1.0f / (l_run == 0.0f ? 1.0f : l_run);
-            unsigned char* stage = base + SMEM_KV + warp * 16384;
+            float o[HD];
             #pragma unroll
             for (int c = 0; c < HD / 32; ++c) {
-                float o[32];
-                tmem_ld32(o_tm + c * 32, o);
-                unsigned char* box = stage + c * 4096 + lane * 128;
+                float oc[32];
+                tmem_ld32(o_tm + c * 32, oc);
+                #pragma unroll
+                for (int i = 0; i < 32; ++i) o[c * 32 + i] = oc[i];
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[B_O_FREE + x]);
+            // The warp's 32 rows go out 32 columns at a time through a 4 KB
+            // stage: lane r writes row r (16-byte chunk i at i ^ (r & 7), no
+            // bank conflicts), then eight lanes per row read it back so each
+            // store instruction writes four whole 128-byte row segments. Rows
+            // >= T are padding and not stored.
+            const float inv = 1.0f / (l_run == 0.0f ? 1.0f : l_run);
+            unsigned char* stage = base + SMEM_OUT + warp * OUT_STAGE_BYTES;
+            const int row_base = qx0 + (warp & 3) * 32;
+            #pragma unroll
+            for (int c = 0; c < HD / 32; ++c) {
                 #pragma unroll
                 for (int i = 0; i < 8; ++i)
-                    *reinterpret_cast<float4*>(box + ((i ^ (lane & 7)) << 4)) =
-                        make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
-            }
-            fence_async_smem();
-            __syncwarp();
-            const int row0 = qx0 + (warp & 3) * 32;
-            if (lane == 0 && row0 < a.T) {
+                    *reinterpret_cast<float4*>(stage + lane * 128 + ((i ^ (lane & 7)) << 4)) =
+                        make_float4(o[c * 32 + 4 * i] * inv, o[c * 32 + 4 * i + 1] * inv,
+                                    o[c * 32 + 4 * i + 2] * inv, o[c * 32 + 4 * i + 3] * inv);
+                __syncwarp();
                 #pragma unroll
-                for (int c = 0; c < HD / 32; ++c)
-                    tma_store_4d(&tm_o, base_u32 + SMEM_KV + warp * 16384 + c * 4096, c * 32, h, row0, seq);
-                bulk_commit();
-                bulk_wait_read0();
+                for (int r4 = 0; r4 < 8; ++r4) {
+                    const int r = r4 * 4 + (lane >> 3), ch = lane & 7;
+                    const float4 v4 = *reinterpret_cast<const float4*>(stage + r * 128 + ((ch ^ (r & 7)) << 4));
+                    const int qr = row_base + r;
+                    if (qr < a.T)
+                        reinterpret_cast<float4*>(a.ao + (((size_t)it.seq * a.T + qr) * a.H + it.h) * HD + c * 32)[ch] = v4;
+                }
+                __syncwarp();
             }
         }
+        if (!ok && lane == 0) fail(PCU_DEVERR_FULL_WAIT);
     }
     tc_fence_before();
     __syncthreads();
     if (warp == WARP_TMA && lane == 0 && s_abort) {
-        // Copies issued but never consumed must land before shared memory goes away:
-        // the last STAGES tiles issued cover every copy that can still be in flight.
-        const int issued = s_issued;
-        for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
-            if (!mbar_wait(&bars[B_KV_FULL + j % STAGES], (j / STAGES) & 1)) record_error(a.err, PCU_DEVERR_DRAIN_WAIT);
-        if (!mbar_wait(&bars[B_Q], 0)) record_error(a.err, PCU_DEVERR_DRAIN_WAIT);
+        // Copies issued but never consumed must land before shared memory goes
+        // away: the last STAGES K/V tiles and the last Q cover every copy that
+        // can still be in flight.
+        const int issued = s_kv_issued;
+        for (int g = issued > STAGES ? issued - STAGES : 0; g < issued; ++g)
+            if (!mbar_wait(&bars[B_KV_FULL + g % STAGES], (g / STAGES) & 1)) record_error(a.err, PCU_DEVERR_DRAIN_WAIT);
+        if (s_q_issued > 0 && !mbar_wait(&bars[B_Q_FULL], (s_q_issued - 1) & 1))
+            record_error(a.err, PCU_DEVERR_DRAIN_WAIT);
     }
     if (warp == WARP_MMA) {
         tc_fence_after();
@@ -543,49 +612,42 @@ inline int make_tmap(CUtensorMap* map, const void* ptr, int T, int n_heads, char
     return 0;
 }
 
-// 4-D tensor map over the F32 output ao [n_seqs][T][H][D]: box 32 floats x 1 head
-// x 32 rows x 1 sequence, 128-byte swizzle (the epilogue's staging layout).
-inline int make_out_tmap(CUtensorMap* map, float* ao, int n_seqs, int T, int H, char* msg, size_t msg_len) {
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    if (!encode) {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn) {
-            snprintf(msg, msg_len, "cuTensorMapEncodeTiled not available");
-            return -9;
-        }
-        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
-    const cuuint64_t dims[4] = {(cuuint64_t)tc::HD, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)n_seqs};
-    const cuuint64_t strides[3] = {(cuuint64_t)tc::HD * 4, (cuuint64_t)H * tc::HD * 4, (cuuint64_t)T * H * tc::HD * 4};
-    const cuuint32_t box[4] = {32, 1, 32, 1};
-    const cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ao, dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-        snprintf(msg, msg_len, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
-        return -9;
-    }
-    return 0;
-}
+// The next-item counter of launches made without a handle (one per device;
+// such launches on one device must not overlap).
+static __device__ unsigned g_prefill_next_item;
 
 // q: [n_seqs][H][T][D], k/v: [n_seqs][HK][T][D] BF16 (rotated); ao: [n_seqs][T][H][D] F32.
+// next_item: a zeroed device counter owned by the caller (null: the shared
+// per-device counter above). One persistent CTA per SM.
 inline int prefill_tc_launch(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, float* ao,
-                             int n_seqs, int T, int H, int HK, int D, float scale, int* err, cudaStream_t st,
-                             char* msg, size_t msg_len) {
+                             int n_seqs, int T, int H, int HK, int D, float scale, int* err, unsigned* next_item,
+                             cudaStream_t st, char* msg, size_t msg_len) {
     if (D != tc::HD) {
         snprintf(msg, msg_len, "tensor-core prefill needs head_dim %d", tc::HD);
         return -6;
     }
-    alignas(64) CUtensorMap tq, tk, tv, to;
     if (reinterpret_cast<uintptr_t>(ao) % 16 != 0) {
         snprintf(msg, msg_len, "output must be 16-byte aligned");
         return -6;
     }
+    alignas(64) CUtensorMap tq, tk, tv;
     if (make_tmap(&tq, q, T, n_seqs * H, msg, msg_len) || make_tmap(&tk, k, T, n_seqs * HK, msg, msg_len) ||
-        make_tmap(&tv, v, T, n_seqs * HK, msg, msg_len) || make_out_tmap(&to, ao, n_seqs, T, H, msg, msg_len))
+        make_tmap(&tv, v, T, n_seqs * HK, msg, msg_len))
         return -9;
+    int device = 0, sms = 0;
+    if (cudaGetDevice(&device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+        snprintf(msg, msg_len, "device query failed");
+        return -9;
+    }
+    if (!next_item) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_prefill_next_item) != cudaSuccess) {
+            snprintf(msg, msg_len, "cudaGetSymbolAddress failed");
+            return -9;
+        }
+        next_item = static_cast<unsigned*>(ptr);
+    }
     static bool attr_set = false;
     if (!attr_set) {
         cudaError_t e = cudaFuncSetAttribute(tc::prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -602,10 +664,13 @@ inline int prefill_tc_launch(const __nv_bfloat16* q, const __nv_bfloat16* k, con
     a.H = H;
     a.HK = HK;
     a.n_qb = (T + 2 * tc::BM - 1) / (2 * tc::BM);
+    a.n_seqs = n_seqs;
+    a.n_items = n_seqs * a.n_qb * H;
     a.scale_log2 = scale * 1.4426950408889634f;
+    a.next_item = next_item;
     a.err = err;
-    dim3 grid((unsigned)H, (unsigned)a.n_qb, (unsigned)n_seqs);
-    tc::prefill_tc_kernel<<<grid, tc::THREADS, tc::SMEM_BYTES, st>>>(tq, tk, tv, to, a);
+    const int grid = a.n_items < sms ? a.n_items : sms;
+    tc::prefill_tc_kernel<<<grid, tc::THREADS, tc::SMEM_BYTES, st>>>(tq, tk, tv, a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         snprintf(msg, msg_len, "prefill_tc launch: %s", cudaGetErrorString(e));
