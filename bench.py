@@ -404,7 +404,7 @@ def run_ours_multi(args, rank, world, local_rank):
             "warmup": args.warmup, "ms_per_step": res["ms"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) cache and q/k/v, seeded",
             "config": {"workload": C4.name, "B": C4.B, "H": C4.H, "HK": C4.HK, "D": C4.D, "ctx": C4.ctx,
-                       "l2": "inputs larger than L2", "parallelism": f"kv-head shard x{world} + NCCL all-gather"},
+                       "l2": "inputs larger than L2", "parallelism": f"kv-head shard x{world} + NVLink peer exchange"},
             "frac_of_8TBps_per_gpu": gbps / world / 8000.0,
             "roofline": {"bound": "hbm", "achieved": res["kernel_GBps_per_gpu"], "peak": hbm, "unit": "GB/s",
                          "frac": res["kernel_GBps_per_gpu"] / hbm, "peak_source": f"{src} (hbm_gbs)",
@@ -412,8 +412,14 @@ def run_ours_multi(args, rank, world, local_rank):
             "e2e": res["e2e"],
             "gpu_launches": args.steps * res["launches_per_step"],   # per rank: split (+ merge); NCCL not counted
             "clocks": clk.summary() if clk else {"sm_mhz": None, "reasons": ["unsampled"]},
-            "extras": {"seq_sharded": {"workload": C5.name, "ms": res_seq["ms"],
-                                       "GBps": C5.kv_bytes / (res_seq["ms"] * 1e-3) / 1e9}},
+            "extras": {"exchange": "NVLink peer stores (pickle_cuda_xchg_put_dev), output equal to NCCL's: "
+                                   f"{res['exchange_matches_nccl']}",
+                       "nccl_all_gather": {"ms": res["nccl_all_gather_ms"],
+                                           "GBps": C4.kv_bytes / (res["nccl_all_gather_ms"] * 1e-3) / 1e9},
+                       "seq_sharded": {"workload": C5.name, "ms": res_seq["ms"],
+                                       "GBps": C5.kv_bytes / (res_seq["ms"] * 1e-3) / 1e9,
+                                       "nccl_all_gather_ms": res_seq["nccl_all_gather_ms"],
+                                       "exchange_matches_nccl": res_seq["exchange_matches_nccl"]}},
         }
         print(json.dumps(out), flush=True)
     dist.barrier()

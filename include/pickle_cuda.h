@@ -217,6 +217,37 @@ PICKLE_CUDA_API const char* pickle_cuda_last_error(pickle_cuda_t* h);
 
 PICKLE_CUDA_API int  pickle_cuda_abi_version(void);
 
+/* ---- Peer exchange of the sharded decodes (one process per GPU) ----
+ * No counterpart in the reference, which runs on one host: this replaces an
+ * NCCL all-gather for the small per-step payloads of the KV-head and
+ * sequence-chunk shards. Each rank creates an exchange with the same
+ * buf_bytes, shares pickle_cuda_xchg_handle's bytes with the other ranks
+ * (any host-side all-gather) and opens theirs. pickle_cuda_xchg_put_dev then
+ * copies `rows` rows of row_bytes (16-byte multiples) from this rank's src
+ * into every rank's receive buffer (pickle_cuda_xchg_buffer) at
+ * dst_offset + r * dst_stride, and completes on the GPU once every rank's
+ * rows of this call have arrived in this rank's buffer. A call first waits
+ * until each destination rank has started the same call, so a rank never
+ * overwrites rows another rank has not consumed (consume them on the stream
+ * that makes the next call). All ranks make the same sequence of calls; a
+ * rank that stops turns into an error (pickle_cuda_xchg_sync) on the others
+ * after a bounded 1 s wait. Plain peer stores through CUDA IPC mappings, no
+ * multicast; the call counters live on the device. */
+#define PICKLE_CUDA_XCHG_MAX_RANKS 8
+#define PICKLE_CUDA_IPC_HANDLE_BYTES 64
+typedef struct pickle_cuda_xchg pickle_cuda_xchg_t;
+PICKLE_CUDA_API int  pickle_cuda_xchg_create(int rank, int world, size_t buf_bytes, int device,
+                                             pickle_cuda_xchg_t** out);
+PICKLE_CUDA_API int  pickle_cuda_xchg_handle(pickle_cuda_xchg_t* x, void* handle_out);
+PICKLE_CUDA_API int  pickle_cuda_xchg_open(pickle_cuda_xchg_t* x, int peer, const void* handle);
+PICKLE_CUDA_API int  pickle_cuda_xchg_buffer(pickle_cuda_xchg_t* x, void** dev_ptr);
+PICKLE_CUDA_API int  pickle_cuda_xchg_put_dev(pickle_cuda_xchg_t* x, const void* src, size_t rows,
+                                              size_t row_bytes, size_t src_stride, size_t dst_offset,
+                                              size_t dst_stride, void* stream);
+PICKLE_CUDA_API int  pickle_cuda_xchg_sync(pickle_cuda_xchg_t* x, void* stream);
+PICKLE_CUDA_API const char* pickle_cuda_xchg_last_error(pickle_cuda_xchg_t* x);
+PICKLE_CUDA_API void pickle_cuda_xchg_free(pickle_cuda_xchg_t* x);
+
 #ifdef __cplusplus
 }
 #endif

@@ -65,7 +65,17 @@ SIGNATURES = {
     "pickle_cuda_prefill_attn_bf16_dev": ([_i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp], _i),
     "pickle_cuda_decode_noalloc": ([_i, _i, _i, _i, _i, _i, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp], _i),
+    "pickle_cuda_xchg_create": ([_i, _i, _sz, _i, ctypes.POINTER(_vp)], _i),
+    "pickle_cuda_xchg_handle": ([_vp, _vp], _i),
+    "pickle_cuda_xchg_open": ([_vp, _i, _vp], _i),
+    "pickle_cuda_xchg_buffer": ([_vp, ctypes.POINTER(_vp)], _i),
+    "pickle_cuda_xchg_put_dev": ([_vp, _vp, _sz, _sz, _sz, _sz, _sz, _vp], _i),
+    "pickle_cuda_xchg_sync": ([_vp, _vp], _i),
+    "pickle_cuda_xchg_last_error": ([_vp], ctypes.c_char_p),
+    "pickle_cuda_xchg_free": ([_vp], None),
 }
+
+IPC_HANDLE_BYTES = 64
 
 
 def lib():
@@ -258,3 +268,55 @@ def lse_merge_packed_dev(n_parts, n_rows, head_dim, parts, part_stride, out, str
 
 def abi_version():
     return lib().pickle_cuda_abi_version()
+
+
+class PeerExchange:
+    """pickle_cuda_xchg_t: one rank's side of the NVLink peer exchange of the
+    sharded decodes (plain peer stores through CUDA IPC, no NCCL).
+
+    Every rank creates one with the same buf_bytes, shares handle() with the
+    others and open()s theirs; put() then writes this rank's rows into every
+    rank's receive buffer (buffer()) and completes on the GPU when all ranks'
+    rows of that call have arrived here.
+    """
+
+    def __init__(self, rank, world, buf_bytes, device=0):
+        self.rank, self.world, self.buf_bytes, self.device = rank, world, buf_bytes, device
+        h = _vp()
+        rc = lib().pickle_cuda_xchg_create(rank, world, buf_bytes, device, ctypes.byref(h))
+        if rc != PICKLE_OK:
+            raise PickleError(rc, "pickle_cuda_xchg_create")
+        self._x = h
+
+    def _check(self, rc, what):
+        if rc != PICKLE_OK:
+            msg = lib().pickle_cuda_xchg_last_error(self._x)
+            raise PickleError(rc, what, msg.decode() if msg else "")
+
+    def handle(self):
+        buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        self._check(lib().pickle_cuda_xchg_handle(self._x, buf), "pickle_cuda_xchg_handle")
+        return buf.raw
+
+    def open(self, peer, handle):
+        buf = ctypes.create_string_buffer(bytes(handle), IPC_HANDLE_BYTES)
+        self._check(lib().pickle_cuda_xchg_open(self._x, peer, buf), "pickle_cuda_xchg_open")
+
+    def buffer(self, shape):
+        """Torch float32 view of this rank's receive buffer."""
+        import torch
+        ptr = _vp()
+        self._check(lib().pickle_cuda_xchg_buffer(self._x, ctypes.byref(ptr)), "pickle_cuda_xchg_buffer")
+        return torch.as_tensor(_DevArray(ptr.value, shape, self), device=torch.device("cuda", self.device))
+
+    def put(self, src, rows, row_bytes, src_stride, dst_offset, dst_stride, stream=None):
+        self._check(lib().pickle_cuda_xchg_put_dev(self._x, _ptr(src), rows, row_bytes, src_stride, dst_offset,
+                                                   dst_stride, _stream(stream)), "pickle_cuda_xchg_put_dev")
+
+    def sync(self, stream=None):
+        self._check(lib().pickle_cuda_xchg_sync(self._x, _stream(stream)), "pickle_cuda_xchg_sync")
+
+    def close(self):
+        if self._x:
+            lib().pickle_cuda_xchg_free(self._x)
+            self._x = None

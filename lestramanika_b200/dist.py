@@ -14,8 +14,11 @@ one host with OpenMP over heads only, src/pickle_fast.c:1960):
   triples are all-gathered and merged by log-sum-exp.
 
 The per-rank compute is a callable so the same orchestration runs with the
-B200 kernels (NCCL, device tensors) and, in the CPU tests, with a CPU
-computation over gloo. All ranks take the same collective steps in the same
+B200 kernels (device tensors) and, in the CPU tests, with a CPU computation
+over gloo. On GPUs the exchange step is either an NCCL all-gather or the
+library's NVLink peer exchange (open_exchange / pickle_cuda_xchg_put_dev):
+each rank stores its rows straight into every rank's receive buffer at
+their final place, so the head slices need no relayout. All ranks take the same collective steps in the same
 order; process groups are created with a short timeout so a rank that
 stops participating turns into an error on the others instead of a hang.
 """
@@ -34,6 +37,26 @@ def init_group(backend, rank, world, timeout_s=60, device=None):
     if device is not None:
         kw["device_id"] = torch.device("cuda", device)
     dist.init_process_group(backend, rank=rank, world_size=world, **kw)
+
+
+def open_exchange(rank, world, buf_bytes, device):
+    """Create this rank's PeerExchange and open every other rank's receive
+    region (the 64-byte CUDA IPC handles are all-gathered over the default
+    process group)."""
+    import torch
+    import torch.distributed as dist
+    from .api import IPC_HANDLE_BYTES, PeerExchange
+    x = PeerExchange(rank, world, buf_bytes, device)
+    dev = torch.device("cuda", device)
+    mine = torch.frombuffer(bytearray(x.handle()), dtype=torch.uint8).to(dev)
+    allh = torch.empty(world * IPC_HANDLE_BYTES, dtype=torch.uint8, device=dev)
+    dist.all_gather_into_tensor(allh, mine)
+    allh = allh.cpu().numpy().tobytes()
+    for p in range(world):
+        if p != rank:
+            x.open(p, allh[p * IPC_HANDLE_BYTES:(p + 1) * IPC_HANDLE_BYTES])
+    dist.barrier()
+    return x
 
 
 def merge_triples(m, l, acc):
@@ -55,10 +78,12 @@ class HeadShardedDecode:
     """KV-head-group sharded decode step for one rank.
 
     compute(q, k, v, out) fills out [B][H/N][D] for this rank's heads;
-    step() returns the all-gathered [B][H][D].
+    step() returns the all-gathered [B][H][D]. With exchange (a
+    PeerExchange of B*H*D*4 bytes) the rows go straight into every rank's
+    [B][H][D] receive buffer; without it, NCCL all-gather and a relayout.
     """
 
-    def __init__(self, B, H, HK, D, rank, world, compute, device=None, dtype=None):
+    def __init__(self, B, H, HK, D, rank, world, compute, device=None, dtype=None, exchange=None):
         import torch
         (self.h0, self.h1), (self.k0, self.k1) = head_shard_dims(H, HK, world, rank)
         self.B, self.H, self.HK, self.D, self.world = B, H, HK, D, world
@@ -69,6 +94,9 @@ class HeadShardedDecode:
         # Flat [N*B][H/N][D]: all_gather_into_tensor concatenates along dim 0.
         self.gathered = torch.empty((world * B, self.h1 - self.h0, D), device=dev, dtype=dtype)
         self.out = torch.empty((B, H, D), device=dev, dtype=dtype)
+        self.exchange = exchange
+        if exchange is not None:
+            self.out = exchange.buffer((B, H, D))
 
     def slice_inputs(self, q, k, v):
         """This rank's share of full [B][H][D] q and [B][HK][D] k/v."""
@@ -78,6 +106,12 @@ class HeadShardedDecode:
     def step(self, q_local, k_local, v_local):
         import torch.distributed as dist
         self.compute(q_local, k_local, v_local, self.local)
+        if self.exchange is not None:
+            import torch
+            row = (self.h1 - self.h0) * self.D * 4
+            self.exchange.put(self.local, self.B, row, row, self.h0 * self.D * 4, self.H * self.D * 4,
+                              torch.cuda.current_stream(self.local.device))
+            return self.out
         dist.all_gather_into_tensor(self.gathered, self.local)
         # [N][B][H/N][D] -> [B][N][H/N][D] = [B][H][D]
         g = self.gathered.view(self.world, self.B, self.h1 - self.h0, self.D)
@@ -99,10 +133,11 @@ class SeqShardedDecode:
     part = [acc (rows x D) | m (rows) | l (rows)], rows = B*H, so a step is
     one all-gather. compute(q, k, v, m, l, acc) fills this rank's views;
     merge(parts, part_stride, out) merges the gathered [N] parts (default:
-    merge_triples on views). step() returns out [B][H][D].
+    merge_triples on views). step() returns out [B][H][D]. With exchange (a
+    PeerExchange of N*part bytes) the parts land in its receive buffer.
     """
 
-    def __init__(self, B, H, D, ctx, rank, world, compute, merge=None, device=None):
+    def __init__(self, B, H, D, ctx, rank, world, compute, merge=None, device=None, exchange=None):
         import torch
         self.p0, self.p1 = seq_shard(ctx, world, rank)
         self.append = rank == world - 1
@@ -111,13 +146,17 @@ class SeqShardedDecode:
         self.merge = merge
         dev = torch.device("cpu") if device is None else torch.device("cuda", device)
         self.rows = rows = B * H
-        self.stride = rows * (D + 2)
+        self.stride = (rows * (D + 2) + 3) // 4 * 4          # parts start on 16-byte boundaries
         self.part = torch.empty(self.stride, device=dev)
         self.acc = self.part[:rows * D].view(rows, D)
         self.m = self.part[rows * D:rows * (D + 1)]
         self.l = self.part[rows * (D + 1):]
         self.parts = torch.empty(world * self.stride, device=dev)
         self.out = torch.empty((B, H, D), device=dev)
+        self.rank = rank
+        self.exchange = exchange
+        if exchange is not None:
+            self.parts = exchange.buffer((world * self.stride,))
 
     @property
     def n_local(self):
@@ -126,7 +165,12 @@ class SeqShardedDecode:
     def step(self, q, k, v):
         import torch.distributed as dist
         self.compute(q, k, v, self.m, self.l, self.acc)
-        dist.all_gather_into_tensor(self.parts, self.part)
+        if self.exchange is not None:
+            import torch
+            nb = self.stride * 4
+            self.exchange.put(self.part, 1, nb, nb, self.rank * nb, nb, torch.cuda.current_stream(self.part.device))
+        else:
+            dist.all_gather_into_tensor(self.parts, self.part)
         if self.merge is not None:
             self.merge(self.parts, self.stride, self.out)
         else:
@@ -149,21 +193,37 @@ def _max_over_ranks(ms, device):
     return float(t.item())
 
 
-def _timed(fn, steps, warmup, device):
+def _timed(fn, steps, warmup, device, graph=False):
+    """Device time per step (ms), max over ranks. graph=True captures the
+    `steps` calls (collectives included) in one CUDA graph and replays it
+    between the events, as a serving loop replays its decode step; the
+    graph is released before returning."""
     import torch
     import torch.distributed as dist
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize(device)
+    g = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(steps):
+                fn()
+        g.replay()
+        torch.cuda.synchronize(device)
     dist.barrier()
     torch.cuda.synchronize(device)
     st = torch.cuda.current_stream(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
-    for _ in range(steps):
-        fn()
+    if g is not None:
+        g.replay()
+    else:
+        for _ in range(steps):
+            fn()
     e1.record(st)
     torch.cuda.synchronize(device)
+    del g
     dist.barrier()
     return _max_over_ranks(e0.elapsed_time(e1) / steps, device)
 
@@ -187,11 +247,17 @@ def bench_head_sharded(w, rank, world, device, steps, warmup):
     st = torch.cuda.current_stream(device)
 
     def compute(qq, kk, vv, out):
-        cu.decode_batch_dev(0, w.B, w.ctx, qq, kk, vv, out, st)
+        cu.decode_batch_dev(0, w.B, w.ctx, qq, kk, vv, out, torch.cuda.current_stream(device))
 
-    hs = HeadShardedDecode(w.B, w.H, w.HK, w.D, rank, world, compute, device=device)
-    ms = _timed(lambda: hs.step(q, k, v), steps, warmup, device)
-    kernel_ms = _timed(lambda: compute(q, k, v, hs.local), steps, warmup, device)
+    # NCCL all-gather for reference, then the NVLink peer exchange (the headline).
+    hs_nccl = HeadShardedDecode(w.B, w.H, w.HK, w.D, rank, world, compute, device=device)
+    nccl_ms = _timed(lambda: hs_nccl.step(q, k, v), steps, warmup, device, graph=True)
+    ref_out = hs_nccl.step(q, k, v).clone()
+    x = open_exchange(rank, world, w.B * w.H * w.D * 4, device)
+    hs = HeadShardedDecode(w.B, w.H, w.HK, w.D, rank, world, compute, device=device, exchange=x)
+    ms = _timed(lambda: hs.step(q, k, v), steps, warmup, device, graph=True)
+    same = bool(torch.equal(hs.step(q, k, v), ref_out))
+    kernel_ms = _timed(lambda: compute(q, k, v, hs.local), steps, warmup, device, graph=True)
     hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
     hout = torch.empty(hs.out.shape).pin_memory()
 
@@ -203,11 +269,16 @@ def bench_head_sharded(w, rank, world, device, steps, warmup):
 
     e2e_ms = _timed(e2e_step, steps, warmup, device)
     cu.sync(st)
+    x.sync(st)
     splits = cu.decode_plan(w.B, w.ctx)[0]
     cu.close()
+    import torch.distributed as dist
+    dist.barrier()
+    x.close()
     per_gpu = w.kv_bytes / world
     return {"ms": ms, "kernel_ms": kernel_ms, "kernel_GBps_per_gpu": per_gpu / (kernel_ms * 1e-3) / 1e9,
-            "launches_per_step": 2 if splits > 1 else 1, "splits": splits,
+            "launches_per_step": (2 if splits > 1 else 1) + 1, "splits": splits,
+            "nccl_all_gather_ms": nccl_ms, "exchange_matches_nccl": same,
             "e2e": {"value": w.kv_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                     "h2d_bytes_per_step": sum(x.numel() * 4 for x in (hq, hk, hv)),
                     "d2h_bytes_per_step": hout.numel() * 4, "ms_per_step": e2e_ms}}
@@ -235,13 +306,23 @@ def bench_seq_sharded(w, rank, world, device, steps, warmup):
     st = torch.cuda.current_stream(device)
 
     def compute(qq, kk, vv, m, l, acc):
-        cu.decode_partial_dev(0, w.B, w.ctx, n_local, append, qq, kk, vv, m, l, acc, st)
+        cu.decode_partial_dev(0, w.B, w.ctx, n_local, append, qq, kk, vv, m, l, acc,
+                              torch.cuda.current_stream(device))
 
     def merge(parts, stride, out):
-        lse_merge_packed_dev(world, w.B * w.H, w.D, parts, stride, out, st)
+        lse_merge_packed_dev(world, w.B * w.H, w.D, parts, stride, out, torch.cuda.current_stream(device))
 
-    ss = SeqShardedDecode(w.B, w.H, w.D, w.ctx, rank, world, compute, merge=merge, device=device)
-    ms = _timed(lambda: ss.step(q, k, v), steps, warmup, device)
+    ss_nccl = SeqShardedDecode(w.B, w.H, w.D, w.ctx, rank, world, compute, merge=merge, device=device)
+    nccl_ms = _timed(lambda: ss_nccl.step(q, k, v), steps, warmup, device, graph=True)
+    ref_out = ss_nccl.step(q, k, v).clone()
+    x = open_exchange(rank, world, world * ss_nccl.stride * 4, device)
+    ss = SeqShardedDecode(w.B, w.H, w.D, w.ctx, rank, world, compute, merge=merge, device=device, exchange=x)
+    ms = _timed(lambda: ss.step(q, k, v), steps, warmup, device, graph=True)
+    same = bool(torch.equal(ss.step(q, k, v), ref_out))
     cu.sync(st)
+    x.sync(st)
     cu.close()
-    return {"ms": ms}
+    import torch.distributed as dist
+    dist.barrier()
+    x.close()
+    return {"ms": ms, "nccl_all_gather_ms": nccl_ms, "exchange_matches_nccl": same}

@@ -86,3 +86,44 @@ def test_sequence_chunks_merge_to_full_attention(world, packed):
         lse_merge_dev(world, rows, D, m_all, l_all, acc_all, out)
     torch.cuda.synchronize()
     assert_rel(out.cpu().numpy(), ref, what=f"sequence chunks x{world} packed={packed}")
+
+
+def test_peer_exchange_single_rank_places_rows_across_calls_and_graph_replays():
+    """The NVLink exchange with one rank: a [B][H/2][D] head slice lands at
+    its place in the [B][H][D] receive buffer, on consecutive calls (the
+    device-side call counters advance) and when the call is replayed from a
+    CUDA graph."""
+    from lestramanika_b200.api import PeerExchange
+    dev = torch.device("cuda", 0)
+    B, H, D, h0 = 3, 8, 128, 4
+    x = PeerExchange(0, 1, B * H * D * 4, 0)
+    buf = x.buffer((B, H, D))
+    row = (H // 2) * D * 4
+    st = torch.cuda.current_stream()
+    for call in range(2):
+        src = torch.randn((B, H // 2, D), device=dev)
+        x.put(src, B, row, row, h0 * D * 4, H * D * 4, st)
+        x.sync(st)
+        assert torch.equal(buf[:, h0:], src), f"call {call}"
+    src = torch.zeros((B, H // 2, D), device=dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        x.put(src, B, row, row, h0 * D * 4, H * D * 4, torch.cuda.current_stream())
+    for rep in range(2):
+        src.copy_(torch.randn((B, H // 2, D), device=dev))
+        g.replay()
+        x.sync(st)
+        assert torch.equal(buf[:, h0:], src), f"replay {rep}"
+    del g
+    x.close()
+
+
+def test_peer_exchange_rejects_rows_outside_the_buffer():
+    from lestramanika_b200 import PickleError
+    from lestramanika_b200.api import PeerExchange
+    x = PeerExchange(0, 1, 4096, 0)
+    src = torch.zeros(2048, device=torch.device("cuda", 0))
+    with pytest.raises(PickleError) as e:
+        x.put(src, 2, 4096, 4096, 0, 4096)
+    assert e.value.code == -7
+    x.close()
