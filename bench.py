@@ -10,9 +10,11 @@ N = 1: headline = Llama-3-8B-shaped decode, B=64, ctx 4096 (KV cache
        steps through enough layer caches that the set is twice L2, as a
        model's decode step does; its L2-write-flushed time is reported too.
 N > 1: headline = Llama-3-70B-shaped decode sharded by KV-head group
-       (B=16, ctx 32768), head outputs all-gathered over NVLink (NCCL);
-       extra = long-context decode sharded by sequence chunk (ctx 131072),
-       partial (m, l, acc) triples all-gathered and merged by log-sum-exp.
+       (B=16, ctx 32768), head outputs exchanged over NVLink by the
+       library's peer exchange (the NCCL all-gather time is reported
+       beside it); extra = long-context decode sharded by sequence chunk
+       (ctx 131072), partial (m, l, acc) triples exchanged and merged by
+       log-sum-exp. Steps replayed from a captured CUDA graph.
        Strong scaling: total work fixed. Time = max over ranks.
 
 One JSON line on rank 0. `--impl reference` times the reference's own

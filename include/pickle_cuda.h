@@ -208,7 +208,8 @@ PICKLE_CUDA_API int  pickle_cuda_kv_layout(pickle_cuda_t* h, int layer, float** 
 PICKLE_CUDA_API int  pickle_cuda_sync(pickle_cuda_t* h, void* stream);
 
 /* Number of KV splits the decode launch uses for (n_seqs, pos) on this
- * handle, and how many kernels it launches (1: split-combine is fused). */
+ * handle, and how many kernels it launches (the split kernel, plus the merge
+ * kernel when there is more than one split). */
 PICKLE_CUDA_API int  pickle_cuda_decode_plan(pickle_cuda_t* h, int n_seqs, size_t pos, int* n_splits,
                              int* n_launches);
 

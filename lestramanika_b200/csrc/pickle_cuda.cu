@@ -374,8 +374,9 @@ int pickle_cuda_decode_plan(pickle_cuda_t* h, int n_seqs, size_t pos, int* n_spl
     int rc = prepare_kernel(h, h->decode);
     if (rc != PICKLE_OK) return rc;
     const long long hist = (long long)pos;
-    if (n_splits) *n_splits = hist > 0 ? plan_splits(h, (long long)n_seqs * h->HK, hist) : 1;
-    if (n_launches) *n_launches = 1;
+    const int s = hist > 0 ? plan_splits(h, (long long)n_seqs * h->HK, hist) : 1;
+    if (n_splits) *n_splits = s;
+    if (n_launches) *n_launches = s > 1 ? 2 : 1;    // split kernel (+ merge kernel)
     return PICKLE_OK;
 }
 
