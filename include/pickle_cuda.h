@@ -154,6 +154,30 @@ PICKLE_CUDA_API int  pickle_cuda_decode_partial_dev(pickle_cuda_t* h, int layer,
                                     const float* q, const float* k, const float* v,
                                     float* m_out, float* l_out, float* acc_out, void* stream);
 
+/* Ragged decode for continuous batching (no counterpart in the reference,
+ * which decodes one sequence at a time): entry i of the batch (i < n) is
+ * the sequence in cache slot slot_dev[i] (slot_dev NULL: slot i) at its
+ * own position pos_dev[i] - it attends rows [0, pos_dev[i]) of that slot,
+ * rotates q and k with table row pos_dev[i] and appends k, v there, exactly
+ * as pickle_cuda_decode_batch_dev does for one position. pos_dev and
+ * slot_dev are device int arrays; max_pos (host) bounds every pos_dev[i]
+ * and must be < max_seq and < the RoPE table length (PICKLE_ERR_RANGE). An
+ * entry whose position exceeds max_pos or whose slot is outside
+ * [0, n_seqs) is skipped and recorded as a device error, reported by
+ * pickle_cuda_sync. Slots within one call must be distinct.
+ * q [n][H][D], k/v [n][HK][D], ao [n][H][D]. */
+PICKLE_CUDA_API int  pickle_cuda_decode_ragged_dev(pickle_cuda_t* h, int layer, int n, const int* pos_dev,
+                                                   const int* slot_dev, size_t max_pos, const float* q,
+                                                   const float* k, const float* v, float* ao, void* stream);
+
+/* pickle_cuda_prefill_dev for the one sequence in cache slot `slot` (no
+ * counterpart in the reference): the prompt of a request admitted into a
+ * free slot of a continuously batched decode. q [T][H][D], k/v [T][HK][D],
+ * ao [T][H][D]. */
+PICKLE_CUDA_API int  pickle_cuda_prefill_slot_dev(pickle_cuda_t* h, int layer, int slot, size_t pos0, size_t T,
+                                                  const float* q, const float* k, const float* v, float* ao,
+                                                  int precision, void* stream);
+
 /* Log-sum-exp merge of n_parts partial triples laid out
  * [n_parts][n_rows] (m, l) and [n_parts][n_rows][D] (acc):
  *   M = max_i m_i,  o = sum_i e^(m_i - M) acc_i / sum_i e^(m_i - M) l_i. */

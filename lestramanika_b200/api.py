@@ -65,6 +65,8 @@ SIGNATURES = {
     "pickle_cuda_prefill_attn_bf16_dev": ([_i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp], _i),
     "pickle_cuda_decode_noalloc": ([_i, _i, _i, _i, _i, _i, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp], _i),
+    "pickle_cuda_decode_ragged_dev": ([_vp, _i, _i, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp], _i),
+    "pickle_cuda_prefill_slot_dev": ([_vp, _i, _i, _sz, _sz, _vp, _vp, _vp, _vp, _i, _vp], _i),
     "pickle_cuda_xchg_create": ([_i, _i, _sz, _i, ctypes.POINTER(_vp)], _i),
     "pickle_cuda_xchg_handle": ([_vp, _vp], _i),
     "pickle_cuda_xchg_open": ([_vp, _i, _vp], _i),
@@ -197,6 +199,21 @@ class PickleCuda:
         self._check(lib().pickle_cuda_decode_batch_dev(self._h, layer, n_seqs, pos, _ptr(q), _ptr(k), _ptr(v),
                                                        _ptr(ao), _stream(stream)),
                     "pickle_cuda_decode_batch_dev")
+
+    def decode_ragged_dev(self, layer, pos, q, k, v, ao, slots=None, max_pos=None, stream=None):
+        """pickle_cuda_decode_ragged_dev: entry i (cache slot slots[i], or i) at its own
+        position pos[i] (int32 device tensors); max_pos defaults to pos.max() (a host sync)."""
+        if max_pos is None:
+            max_pos = int(pos.max().item())
+        self._check(lib().pickle_cuda_decode_ragged_dev(self._h, layer, int(pos.numel()), _ptr(pos), _ptr(slots),
+                                                        max_pos, _ptr(q), _ptr(k), _ptr(v), _ptr(ao),
+                                                        _stream(stream)),
+                    "pickle_cuda_decode_ragged_dev")
+
+    def prefill_slot_dev(self, layer, slot, pos0, T, q, k, v, ao, precision=PREFILL_F32, stream=None):
+        self._check(lib().pickle_cuda_prefill_slot_dev(self._h, layer, slot, pos0, T, _ptr(q), _ptr(k), _ptr(v),
+                                                       _ptr(ao), precision, _stream(stream)),
+                    "pickle_cuda_prefill_slot_dev")
 
     def prefill_dev(self, layer, n_seqs, pos0, T, q, k, v, ao, precision=PREFILL_F32, stream=None):
         self._check(lib().pickle_cuda_prefill_dev(self._h, layer, n_seqs, pos0, T, _ptr(q), _ptr(k), _ptr(v),

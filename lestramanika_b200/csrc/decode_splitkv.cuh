@@ -66,6 +66,14 @@ struct DecodeArgs {
     float* ws_l;
     float* ws_acc;           // [n_groups][G][n_splits][D]
     int* err;
+    // Ragged decode (continuous batching), else null: entry z attends its
+    // own seq_pos[z] cached rows, rotates with and appends at that position,
+    // in cache slot seq_slot[z] (null: slot z). Positions above max_pos and
+    // slots outside [0, n_slots) are rejected on the device (error word).
+    const int* seq_pos;
+    const int* seq_slot;
+    long long max_pos;
+    int n_slots;
 };
 
 constexpr int kMaxSplits = 256;
@@ -292,14 +300,25 @@ decode_splitkv_kernel(const DecodeArgs a) {
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, kvh = blockIdx.y, z = blockIdx.z;
-    const int seq = z / a.n_q, t = z % a.n_q;
-    const long long hist = a.hist_len0 + (long long)t * a.hist_step;
-    const long long row0 = (long long)split * a.chunk;
-    long long row1 = row0 + a.chunk;
+    int seq = z / a.n_q;
+    const int t = z % a.n_q;
+    long long hist = a.hist_len0 + (long long)t * a.hist_step;
+    long long chunk = a.chunk, qpos = a.q_pos0 + t, append_idx = a.append_idx;
+    if (a.seq_pos) {
+        const long long p = a.seq_pos[z];
+        if (a.seq_slot) seq = a.seq_slot[z];
+        if (p < 0 || p > a.max_pos || seq < 0 || seq >= a.n_slots) {
+            if (tid_is_first()) record_error(a.err, PCU_DEVERR_ARG);
+            return;
+        }
+        hist = qpos = append_idx = p;
+        chunk = p > 0 ? (p + a.n_splits - 1) / a.n_splits : 1;
+    }
+    const long long row0 = (long long)split * chunk;
+    long long row1 = row0 + chunk;
     if (row1 > hist) row1 = hist;
     const int n_rows = row1 > row0 ? (int)(row1 - row0) : 0;
     const bool do_append = a.append && split == a.n_splits - 1;
-    const long long qpos = a.q_pos0 + t;
     const size_t head_off = (size_t)seq * a.seq_stride + (size_t)kvh * a.head_stride;
     const float* kbase = a.kc + head_off + (size_t)row0 * D;
     const float* vbase = a.vc + head_off + (size_t)row0 * D;
@@ -344,10 +363,10 @@ decode_splitkv_kernel(const DecodeArgs a) {
         }
     } else {
         if (do_append) {
-            const float* kn = a.k_new + ((size_t)seq * a.HK + kvh) * D;
-            const float* vn = a.v_new + ((size_t)seq * a.HK + kvh) * D;
-            float4* kdst = reinterpret_cast<float4*>(a.kc + head_off + (size_t)a.append_idx * D);
-            float4* vdst = reinterpret_cast<float4*>(a.vc + head_off + (size_t)a.append_idx * D);
+            const float* kn = a.k_new + ((size_t)z * a.HK + kvh) * D;
+            const float* vn = a.v_new + ((size_t)z * a.HK + kvh) * D;
+            float4* kdst = reinterpret_cast<float4*>(a.kc + head_off + (size_t)append_idx * D);
+            float4* vdst = reinterpret_cast<float4*>(a.vc + head_off + (size_t)append_idx * D);
             for (int c = tid; c < C::NCH; c += C::NCW * 32) {
                 const float4 kk = load_row4(kn, c, a.rope, a.vec, a.half, sr, cr);
                 const float4 vv = ld4(vn + 4 * c);

@@ -15,6 +15,7 @@ enum : int {
     PCU_DEVERR_EMPTY_WAIT = 2,   // producer gave up waiting for a free stage
     PCU_DEVERR_DRAIN_WAIT = 3,   // copies still in flight at exit after an abort
     PCU_DEVERR_MMA_WAIT = 4,     // tensor-core completion never arrived
+    PCU_DEVERR_ARG = 5,          // a device-side argument (position, slot) out of range
 };
 
 // Every spin on an mbarrier gives up after this long and records an error
@@ -88,6 +89,8 @@ PCU_DEV void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint
 // prerequisite lets the dependent be scheduled once all its CTAs ran this.
 PCU_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 PCU_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+PCU_DEV bool tid_is_first() { return threadIdx.x == 0; }
 
 PCU_DEV void record_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);

@@ -263,7 +263,7 @@ int take_device_error(pickle_cuda* h, cudaStream_t st) {
 }
 
 int prefill_launch(pickle_cuda* h, int layer, int n_seqs, size_t pos0, size_t T, const float* q,
-                   const float* k, const float* v, float* ao, int precision, cudaStream_t st);
+                   const float* k, const float* v, float* ao, int precision, cudaStream_t st, int slot0 = 0);
 
 }  // namespace
 
@@ -390,6 +390,37 @@ int pickle_cuda_decode_batch_dev(pickle_cuda_t* h, int layer, int n_seqs, size_t
                          nullptr, nullptr, 0, (cudaStream_t)stream);
 }
 
+int pickle_cuda_decode_ragged_dev(pickle_cuda_t* h, int layer, int n, const int* pos_dev, const int* slot_dev,
+                                  size_t max_pos, const float* q, const float* k, const float* v, float* ao,
+                                  void* stream) {
+    int rc = check_layer(h, layer, n);
+    if (rc != PICKLE_OK) return rc;
+    if (!pos_dev || !q || !k || !v || !ao) return PICKLE_ERR_ARG;
+    if (max_pos >= (size_t)h->max_seq || max_pos >= (size_t)h->rope_len) return PICKLE_ERR_RANGE;
+    rc = prepare_kernel(h, h->decode);
+    if (rc != PICKLE_OK) return rc;
+    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)ao) % 16) {
+        snprintf(h->last_error, sizeof(h->last_error), "q, k, v and output rows must be 16-byte aligned");
+        return PICKLE_ERR_ARG;
+    }
+    // Splits are planned for the longest entry; each entry cuts its own
+    // history into that many pieces on the device.
+    DecodeArgs a = base_args(h, layer);
+    a.q = q;
+    a.k_new = k;
+    a.v_new = v;
+    a.rope = 1;
+    a.append = 1;
+    a.n_splits = max_pos > 0 ? plan_splits(h, (long long)n * h->HK, (long long)max_pos) : 1;
+    a.out_mode = 0;
+    a.ao = ao;
+    a.seq_pos = pos_dev;
+    a.seq_slot = slot_dev;
+    a.max_pos = (long long)max_pos;
+    a.n_slots = h->n_seqs;
+    return launch_decode(h, a, n, (cudaStream_t)stream);
+}
+
 int pickle_cuda_decode_partial_dev(pickle_cuda_t* h, int layer, int n_seqs, size_t pos, size_t n_local,
                                    int append, const float* q, const float* k, const float* v,
                                    float* m_out, float* l_out, float* acc_out, void* stream) {
@@ -459,6 +490,17 @@ int pickle_cuda_prefill_dev(pickle_cuda_t* h, int layer, int n_seqs, size_t pos0
     if (pos0 + T > (size_t)h->max_seq || pos0 + T > (size_t)h->rope_len) return PICKLE_ERR_RANGE;
     if (precision != PICKLE_CUDA_PREFILL_F32 && precision != PICKLE_CUDA_PREFILL_BF16) return PICKLE_ERR_ARG;
     return prefill_launch(h, layer, n_seqs, pos0, T, q, k, v, ao, precision, (cudaStream_t)stream);
+}
+
+int pickle_cuda_prefill_slot_dev(pickle_cuda_t* h, int layer, int slot, size_t pos0, size_t T, const float* q,
+                                 const float* k, const float* v, float* ao, int precision, void* stream) {
+    int rc = check_layer(h, layer, 1);
+    if (rc != PICKLE_OK) return rc;
+    if (slot < 0 || slot >= h->n_seqs) return PICKLE_ERR_RANGE;
+    if (!q || !k || !v || !ao || T == 0) return PICKLE_ERR_ARG;
+    if (pos0 + T > (size_t)h->max_seq || pos0 + T > (size_t)h->rope_len) return PICKLE_ERR_RANGE;
+    if (precision != PICKLE_CUDA_PREFILL_F32 && precision != PICKLE_CUDA_PREFILL_BF16) return PICKLE_ERR_ARG;
+    return prefill_launch(h, layer, 1, pos0, T, q, k, v, ao, precision, (cudaStream_t)stream, slot);
 }
 
 int pickle_cuda_prefill_attn_bf16_dev(int n_seqs, int T, int n_heads, int n_kv_heads, int head_dim,
@@ -555,7 +597,7 @@ void launch_rope_append(const RopeAppendArgs& ra, int T, int n_seqs, cudaStream_
 }
 
 int prefill_launch(pickle_cuda* h, int layer, int n_seqs, size_t pos0, size_t T, const float* q,
-                   const float* k, const float* v, float* ao, int precision, cudaStream_t st) {
+                   const float* k, const float* v, float* ao, int precision, cudaStream_t st, int slot0) {
     const size_t nq = (size_t)n_seqs * T * h->H * h->D;
     const size_t nk = (size_t)n_seqs * T * h->HK * h->D;
     if ((uintptr_t)ao % 16) {
@@ -565,8 +607,9 @@ int prefill_launch(pickle_cuda* h, int layer, int n_seqs, size_t pos0, size_t T,
     RopeAppendArgs ra;
     memset(&ra, 0, sizeof(ra));
     ra.q = q; ra.k = k; ra.v = v;
-    ra.kc = h->kc + (size_t)layer * h->layer_stride;
-    ra.vc = h->vc + (size_t)layer * h->layer_stride;
+    // Sequences [slot0, slot0 + n_seqs) of the cache.
+    ra.kc = h->kc + (size_t)layer * h->layer_stride + (size_t)slot0 * h->seq_stride;
+    ra.vc = h->vc + (size_t)layer * h->layer_stride + (size_t)slot0 * h->seq_stride;
     ra.seq_stride = (long long)h->seq_stride;
     ra.head_stride = (long long)h->head_stride;
     ra.sin_tab = h->sin_tab; ra.cos_tab = h->cos_tab;
@@ -583,6 +626,8 @@ int prefill_launch(pickle_cuda* h, int layer, int n_seqs, size_t pos0, size_t T,
         PCU_CHECK(h, cudaGetLastError());
         // Causal attention: query t of each sequence attends rows [0, pos0+t].
         DecodeArgs a = base_args(h, layer);
+        a.kc = ra.kc;
+        a.vc = ra.vc;
         a.q = (const float*)h->scratch;
         a.n_q = (int)T;
         a.q_pos0 = (long long)pos0;
