@@ -242,6 +242,23 @@ PICKLE_CUDA_API const char* pickle_cuda_last_error(pickle_cuda_t* h);
 
 PICKLE_CUDA_API int  pickle_cuda_abi_version(void);
 
+/* ---- Projections either side of the attention block ----
+ * y[v][o] = sum_i W[o][i] * x[v][i] for v < n_vec (1..8 vectors sharing one
+ * pass over W), with W [out_n][in_n] in its raw on-disk layout of GGML type
+ * `type`: 0 F32, 1 F16, 2 Q4_0, 8 Q8_0, 12 Q4_K, 14 Q6_K (the values of
+ * src/pickle.h:85-97). Replaces pickle_fast_matmul_dispatch
+ * (src/pickle_fast.c:1423-1474) for those types, with the same per-weight
+ * dequantization and a float activation (the reference's float paths);
+ * other types return PICKLE_ERR_TYPE like the dispatch. in_n must be a
+ * multiple of the type's block (4, 32 or 256 elements); W, x and y
+ * 16-byte aligned device buffers; x [n_vec][in_n], y [n_vec][out_n]. */
+#define PICKLE_CUDA_MATVEC_MAX_VEC 8
+PICKLE_CUDA_API int  pickle_cuda_matvec_dev(int type, const void* W, int out_n, int in_n, int n_vec,
+                                            const float* x, float* y, void* stream);
+/* Bytes of one W row of `type` for in_n elements (0: unsupported or not a
+ * whole number of blocks). */
+PICKLE_CUDA_API size_t pickle_cuda_matvec_row_bytes(int type, int in_n);
+
 /* ---- Peer exchange of the sharded decodes (one process per GPU) ----
  * No counterpart in the reference, which runs on one host: this replaces an
  * NCCL all-gather for the small per-step payloads of the KV-head and

@@ -67,6 +67,8 @@ SIGNATURES = {
                                     _vp], _i),
     "pickle_cuda_decode_ragged_dev": ([_vp, _i, _i, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp], _i),
     "pickle_cuda_prefill_slot_dev": ([_vp, _i, _i, _sz, _sz, _vp, _vp, _vp, _vp, _i, _vp], _i),
+    "pickle_cuda_matvec_dev": ([_i, _vp, _i, _i, _i, _vp, _vp, _vp], _i),
+    "pickle_cuda_matvec_row_bytes": ([_i, _i], _sz),
     "pickle_cuda_xchg_create": ([_i, _i, _sz, _i, ctypes.POINTER(_vp)], _i),
     "pickle_cuda_xchg_handle": ([_vp, _vp], _i),
     "pickle_cuda_xchg_open": ([_vp, _i, _vp], _i),
@@ -281,6 +283,21 @@ def lse_merge_packed_dev(n_parts, n_rows, head_dim, parts, part_stride, out, str
                                                 _stream(stream))
     if rc != PICKLE_OK:
         raise PickleError(rc, "pickle_cuda_lse_merge_packed_dev")
+
+
+# GGML weight types the device matvec takes (src/pickle.h:85-97).
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0, GGML_Q4_K, GGML_Q6_K = 0, 1, 2, 8, 12, 14
+
+
+def matvec_row_bytes(ggml_type, in_n):
+    return lib().pickle_cuda_matvec_row_bytes(ggml_type, in_n)
+
+
+def matvec_dev(ggml_type, W, out_n, in_n, x, y, n_vec=1, stream=None):
+    """pickle_cuda_matvec_dev: y [n_vec][out_n] = W x for raw GGML weight bytes W (uint8 device tensor)."""
+    rc = lib().pickle_cuda_matvec_dev(ggml_type, _ptr(W), out_n, in_n, n_vec, _ptr(x), _ptr(y), _stream(stream))
+    if rc != PICKLE_OK:
+        raise PickleError(rc, "pickle_cuda_matvec_dev")
 
 
 def abi_version():
