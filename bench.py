@@ -298,6 +298,87 @@ def prefill_line(w, device, steps, warmup, precision):
     return out
 
 
+MATVEC_SHAPE = (14336, 4096)        # Llama-3-8B FFN up/gate projection
+
+
+def matvec_line(device, steps, warmup, types=("F16", "Q8_0", "Q4_K", "Q6_K")):
+    """Device weight matvec (pickle_cuda_matvec_dev) on the Llama-3-8B FFN
+    up shape, one vector: weight GB/s. Steps rotate over enough weight copies
+    to total twice L2 and are replayed from a CUDA graph."""
+    torch = _torch()
+    from lestramanika_b200 import api
+    out_n, in_n = MATVEC_SHAPE
+    dev = torch.device("cuda", device)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    res = {}
+    for name in types:
+        t = getattr(api, "GGML_" + name)
+        wbytes = api.matvec_row_bytes(t, in_n) * out_n
+        copies = max(2, -(-2 * L2_BYTES // wbytes))
+        if t == api.GGML_F16:
+            w0 = torch.randn((out_n, in_n), device=dev, generator=gen).half().view(torch.uint8).reshape(-1)
+        else:      # random quant bytes with small positive f16 block scales
+            w0 = torch.randint(0, 256, (wbytes,), device=dev, dtype=torch.uint8, generator=gen)
+            blk = {api.GGML_Q8_0: (34, (0,)), api.GGML_Q4_K: (144, (0, 2)), api.GGML_Q6_K: (210, (208,)),
+                   api.GGML_Q4_0: (18, (0,))}[t]
+            b = w0.view(-1, blk[0])
+            for off in blk[1]:
+                sc = (torch.rand((b.shape[0],), device=dev, generator=gen) * 0.02 + 0.005).half()
+                b[:, off:off + 2] = sc.view(torch.uint8).view(-1, 2)
+        Ws = [w0] + [w0.clone() for _ in range(copies - 1)]
+        x = torch.randn((1, in_n), device=dev)
+        y = torch.empty((1, out_n), device=dev)
+        st = torch.cuda.current_stream()
+        for i in range(warmup):
+            api.matvec_dev(t, Ws[i % copies], out_n, in_n, x, y, 1, st)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            cs = torch.cuda.current_stream()
+            for i in range(steps):
+                api.matvec_dev(t, Ws[i % copies], out_n, in_n, x, y, 1, cs)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        g.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        res[name] = {"us": round(ms * 1e3, 2), "GBps": wbytes / (ms * 1e-3) / 1e9, "weight_bytes": wbytes,
+                     "copies_rotated": copies}
+        del g, Ws, w0
+        torch.cuda.empty_cache()
+    return {"shape": f"{out_n}x{in_n}", "n_vec": 1, "types": res}
+
+
+def matvec_cpu_baseline(types=("F16", "Q8_0", "Q4_K", "Q6_K"), seconds=2.0):
+    """The reference's own matvec kernels (oracle/_ref, OpenMP on all host
+    cores) on the same shape: weight GB/s."""
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+    import numpy as np
+    sys.path.insert(0, ROOT)
+    from oracle import matvec as mv
+    if mv.ref_lib() is None:
+        return {"unavailable": "oracle/_ref/libref_matvec.so not built"}
+    out_n, in_n = MATVEC_SHAPE
+    res = {}
+    for name in types:
+        t = mv.TYPES[name]
+        W = mv.random_weights(t, out_n, in_n, np.random.default_rng(t))
+        x = np.random.default_rng(1).standard_normal(in_n, dtype=np.float32)
+        mv.ref_matvec(t, W, out_n, in_n, x)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds / len(types):
+            mv.ref_matvec(t, W, out_n, in_n, x)
+            n += 1
+        dt = time.perf_counter() - t0
+        res[name] = {"GBps": W.nbytes * n / dt / 1e9, "calls": n}
+    return {"kind": "reference", "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+            "types": res}
+
+
 def cpu_baseline(seconds=10.0):
     """The reference's OpenMP attention (oracle/_ref, compiled from its sources)
     on the host cores, on whole sequences of the C2 workload (ctx 4096)."""
@@ -349,6 +430,13 @@ def run_ours_single(args):
         line, _ = decode_line(w, device, max(args.steps, 5), args.warmup, small)
         line["frac_of_measured_hbm"] = line["GBps"] / hbm
         extras[w.name] = line
+    try:
+        mvl = matvec_line(device, max(args.steps, 20), max(args.warmup, 3))
+        for r in mvl["types"].values():
+            r["frac_of_measured_hbm"] = r["GBps"] / hbm
+        extras["matvec"] = mvl
+    except Exception as exc:  # reported, not hidden
+        extras["matvec"] = {"error": str(exc)[:200]}
     try:
         from lestramanika_b200 import PREFILL_BF16
         pf = prefill_line(C3, device, max(5, min(args.steps, 10)), max(args.warmup, 3), PREFILL_BF16)
@@ -430,7 +518,7 @@ def run_ours_multi(args, rank, world, local_rank):
 
 C4_SMALL = Decode("llama3-70b decode B=2 ctx=32768 (profiling size)", 2, 64, 8, 128, 32768, 500000.0)
 ONLY = {"c2b1": (C2_B1, True), "c2b8": (C2_B8, False), "c2b64": (C2_B64, False), "c4": (C4, False),
-        "c4s": (C4_SMALL, False), "c5": (C5, False), "c3": (C3, None)}
+        "c4s": (C4_SMALL, False), "c5": (C5, False), "c3": (C3, None), "mv": (None, None)}
 
 
 def run_only(args):
@@ -438,7 +526,10 @@ def run_only(args):
     torch = _torch()
     torch.cuda.set_device(0)
     w, flush = ONLY[args.only]
-    if flush is None:
+    if args.only == "mv":
+        line = matvec_line(0, args.steps, args.warmup)
+        line["cpu_reference"] = matvec_cpu_baseline()
+    elif flush is None:
         from lestramanika_b200 import PREFILL_BF16
         line = prefill_line(w, 0, args.steps, args.warmup, PREFILL_BF16)
     else:

@@ -258,6 +258,10 @@ PICKLE_CUDA_API int  pickle_cuda_matvec_dev(int type, const void* W, int out_n, 
 /* Bytes of one W row of `type` for in_n elements (0: unsupported or not a
  * whole number of blocks). */
 PICKLE_CUDA_API size_t pickle_cuda_matvec_row_bytes(int type, int in_n);
+/* The device error word of the tensor-core matvec on `device` (a bounded
+ * wait that gave up: PCU_DEVERR codes 1-3, 0 = none), read and cleared.
+ * Synchronous. No reference counterpart (the reference has no device). */
+PICKLE_CUDA_API int  pickle_cuda_matvec_take_error(int device, int* code);
 
 /* ---- Peer exchange of the sharded decodes (one process per GPU) ----
  * No counterpart in the reference, which runs on one host: this replaces an

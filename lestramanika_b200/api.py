@@ -69,6 +69,7 @@ SIGNATURES = {
     "pickle_cuda_prefill_slot_dev": ([_vp, _i, _i, _sz, _sz, _vp, _vp, _vp, _vp, _i, _vp], _i),
     "pickle_cuda_matvec_dev": ([_i, _vp, _i, _i, _i, _vp, _vp, _vp], _i),
     "pickle_cuda_matvec_row_bytes": ([_i, _i], _sz),
+    "pickle_cuda_matvec_take_error": ([_i, ctypes.POINTER(ctypes.c_int)], _i),
     "pickle_cuda_xchg_create": ([_i, _i, _sz, _i, ctypes.POINTER(_vp)], _i),
     "pickle_cuda_xchg_handle": ([_vp, _vp], _i),
     "pickle_cuda_xchg_open": ([_vp, _i, _vp], _i),
@@ -298,6 +299,15 @@ def matvec_dev(ggml_type, W, out_n, in_n, x, y, n_vec=1, stream=None):
     rc = lib().pickle_cuda_matvec_dev(ggml_type, _ptr(W), out_n, in_n, n_vec, _ptr(x), _ptr(y), _stream(stream))
     if rc != PICKLE_OK:
         raise PickleError(rc, "pickle_cuda_matvec_dev")
+
+
+def matvec_take_error(device=0):
+    """pickle_cuda_matvec_take_error: the matvec's device error code (0 = none), cleared."""
+    code = ctypes.c_int(0)
+    rc = lib().pickle_cuda_matvec_take_error(device, ctypes.byref(code))
+    if rc != PICKLE_OK:
+        raise PickleError(rc, "pickle_cuda_matvec_take_error")
+    return code.value
 
 
 def abi_version():

@@ -22,6 +22,8 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 
+#include "matvec_tc.cuh"
+
 namespace {
 
 constexpr int kRows = 2;       // output rows per warp
@@ -217,10 +219,18 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_matvec_dev(int type, const void* W, i
     cudaError_t e = cudaErrorInvalidValue;
     switch (type) {
         case T_F32: e = launch_type<T_F32>(w, row_bytes, out_n, in_n, n_vec, x, y, st); break;
-        case T_F16: e = launch_type<T_F16>(w, row_bytes, out_n, in_n, n_vec, x, y, st); break;
+        case T_F16:
+            e = mvtc::tc_supported<T_F16>(w, row_bytes, in_n)
+                    ? mvtc::launch<T_F16>(w, row_bytes, out_n, in_n, n_vec, x, y, st)
+                    : launch_type<T_F16>(w, row_bytes, out_n, in_n, n_vec, x, y, st);
+            break;
         case T_Q4_0: e = launch_type<T_Q4_0>(w, row_bytes, out_n, in_n, n_vec, x, y, st); break;
         case T_Q8_0: e = launch_type<T_Q8_0>(w, row_bytes, out_n, in_n, n_vec, x, y, st); break;
-        case T_Q4_K: e = launch_type<T_Q4_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st); break;
+        case T_Q4_K:
+            e = mvtc::tc_supported<T_Q4_K>(w, row_bytes, in_n)
+                    ? mvtc::launch<T_Q4_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st)
+                    : launch_type<T_Q4_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st);
+            break;
         case T_Q6_K: e = launch_type<T_Q6_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st); break;
     }
     return e == cudaSuccess ? PICKLE_OK : PICKLE_ERR_DEVICE;
@@ -236,4 +246,16 @@ extern "C" PICKLE_CUDA_API size_t pickle_cuda_matvec_row_bytes(int type, int in_
         case T_Q6_K: return in_n % 256 ? 0 : (size_t)(in_n / 256) * 210;
         default: return 0;
     }
+}
+
+extern "C" PICKLE_CUDA_API int pickle_cuda_matvec_take_error(int device, int* code) {
+    if (!code) return PICKLE_ERR_ARG;
+    if (cudaSetDevice(device) != cudaSuccess) return PICKLE_ERR_DEVICE;
+    int v = 0;
+    const int zero = 0;
+    if (cudaMemcpyFromSymbol(&v, mvtc::g_mv_err, sizeof(int)) != cudaSuccess ||
+        cudaMemcpyToSymbol(mvtc::g_mv_err, &zero, sizeof(int)) != cudaSuccess)
+        return PICKLE_ERR_DEVICE;
+    *code = v;
+    return PICKLE_OK;
 }

@@ -41,13 +41,43 @@ def test_matvec_matches_reference_goldens(name):
 
 
 @pytest.mark.parametrize("name", sorted(mv.TYPES))
-@pytest.mark.parametrize("out_n,in_n,n_vec", [(1001, 4096, 1), (64, 14336, 3), (8, 256, 8), (5, 1024, 5)])
+@pytest.mark.parametrize("out_n,in_n,n_vec", [(1001, 4096, 1), (64, 14336, 3), (8, 256, 8), (5, 1024, 5),
+                                              (33, 1536, 2), (70, 2048, 4), (17, 6144, 7)])
 def test_matvec_matches_oracle_at_model_sizes(name, out_n, in_n, n_vec):
     t = mv.TYPES[name]
     rng = np.random.default_rng(out_n + in_n + t)
     W = mv.random_weights(t, out_n, in_n, rng)
     x = rng.standard_normal((n_vec, in_n), dtype=np.float32)
     _close(_run(t, W, out_n, in_n, x), mv.matvec(t, W, out_n, in_n, x), f"{name} {out_n}x{in_n} n_vec={n_vec}")
+    assert api.matvec_take_error(0) == 0
+
+
+@pytest.mark.parametrize("name", ["F16", "Q4_0", "Q8_0"])
+@pytest.mark.parametrize("out_n,in_n", [(3, 96), (40, 320)])
+def test_matvec_rows_not_16_byte_multiples(name, out_n, in_n):
+    # F16 rows of 96 or 320 halves, Q4_0 / Q8_0 rows of 3 or 10 blocks:
+    # rows that do not start on 16-byte boundaries.
+    t = mv.TYPES[name]
+    rng = np.random.default_rng(in_n + t)
+    W = mv.random_weights(t, out_n, in_n, rng)
+    x = rng.standard_normal((2, in_n), dtype=np.float32)
+    _close(_run(t, W, out_n, in_n, x), mv.matvec(t, W, out_n, in_n, x), f"{name} {out_n}x{in_n}")
+
+
+@pytest.mark.parametrize("name", sorted(mv.TYPES))
+@pytest.mark.parametrize("scale", [1e-30, 1e-3, 1e3, 1e30])
+def test_matvec_activation_magnitudes(name, scale):
+    # The tensor-core path rescales x by a power of two per chunk before
+    # splitting it into f16 halves; tiny and huge activations must come out
+    # to the same relative accuracy. One chunk of x is all zeros.
+    t = mv.TYPES[name]
+    out_n, in_n = 48, 4096
+    rng = np.random.default_rng(7 + t)
+    W = mv.random_weights(t, out_n, in_n, rng)
+    x = (rng.standard_normal((2, in_n)) * scale).astype(np.float32)
+    x[:, 1024:2048] = 0
+    x[1, :512] *= 1e-6
+    _close(_run(t, W, out_n, in_n, x), mv.matvec(t, W, out_n, in_n, x), f"{name} scale {scale}")
 
 
 def test_matvec_errors():
