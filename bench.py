@@ -301,7 +301,7 @@ def prefill_line(w, device, steps, warmup, precision):
 MATVEC_SHAPE = (14336, 4096)        # Llama-3-8B FFN up/gate projection
 
 
-def matvec_line(device, steps, warmup, types=("F16", "Q8_0", "Q4_K", "Q6_K")):
+def matvec_line(device, steps, warmup, types=("F16", "Q8_0", "Q6_K", "Q4_K", "Q4_0")):
     """Device weight matvec (pickle_cuda_matvec_dev) on the Llama-3-8B FFN
     up shape, one vector: weight GB/s. Steps rotate over enough weight copies
     to total twice L2 and are replayed from a CUDA graph."""
@@ -353,7 +353,7 @@ def matvec_line(device, steps, warmup, types=("F16", "Q8_0", "Q4_K", "Q6_K")):
     return {"shape": f"{out_n}x{in_n}", "n_vec": 1, "types": res}
 
 
-def matvec_cpu_baseline(types=("F16", "Q8_0", "Q4_K", "Q6_K"), seconds=2.0):
+def matvec_cpu_baseline(types=("F16", "Q8_0", "Q6_K", "Q4_K", "Q4_0"), seconds=2.0):
     """The reference's own matvec kernels (oracle/_ref, OpenMP on all host
     cores) on the same shape: weight GB/s."""
     os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))

@@ -224,14 +224,26 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_matvec_dev(int type, const void* W, i
                     ? mvtc::launch<T_F16>(w, row_bytes, out_n, in_n, n_vec, x, y, st)
                     : launch_type<T_F16>(w, row_bytes, out_n, in_n, n_vec, x, y, st);
             break;
-        case T_Q4_0: e = launch_type<T_Q4_0>(w, row_bytes, out_n, in_n, n_vec, x, y, st); break;
-        case T_Q8_0: e = launch_type<T_Q8_0>(w, row_bytes, out_n, in_n, n_vec, x, y, st); break;
+        case T_Q4_0:
+            e = mvtc::tc_supported<T_Q4_0>(w, row_bytes, in_n)
+                    ? mvtc::launch<T_Q4_0>(w, row_bytes, out_n, in_n, n_vec, x, y, st)
+                    : launch_type<T_Q4_0>(w, row_bytes, out_n, in_n, n_vec, x, y, st);
+            break;
+        case T_Q8_0:
+            e = mvtc::tc_supported<T_Q8_0>(w, row_bytes, in_n)
+                    ? mvtc::launch<T_Q8_0>(w, row_bytes, out_n, in_n, n_vec, x, y, st)
+                    : launch_type<T_Q8_0>(w, row_bytes, out_n, in_n, n_vec, x, y, st);
+            break;
         case T_Q4_K:
             e = mvtc::tc_supported<T_Q4_K>(w, row_bytes, in_n)
                     ? mvtc::launch<T_Q4_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st)
                     : launch_type<T_Q4_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st);
             break;
-        case T_Q6_K: e = launch_type<T_Q6_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st); break;
+        case T_Q6_K:
+            e = mvtc::tc_supported<T_Q6_K>(w, row_bytes, in_n)
+                    ? mvtc::launch<T_Q6_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st)
+                    : launch_type<T_Q6_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st);
+            break;
     }
     return e == cudaSuccess ? PICKLE_OK : PICKLE_ERR_DEVICE;
 }
