@@ -353,6 +353,57 @@ def matvec_line(device, steps, warmup, types=("F16", "Q8_0", "Q6_K", "Q4_K", "Q4
     return {"shape": f"{out_n}x{in_n}", "n_vec": 1, "types": res}
 
 
+MATMUL_SHAPE = (6144, 4096, 2048)   # Llama-3-8B fused QKV projection of a 2048-token prompt
+
+
+def matmul_line(device, steps, warmup, types=("Q4_K", "Q8_0", "F16")):
+    """Batched projection (pickle_cuda_matmul_dev, tensor-core GEMM) on the
+    QKV shape: useful TFLOP/s (2 out_n in_n n_tok per call) and the rate of
+    the tensor pipe, which also runs the hi/lo correction products (3 MMAs
+    per k for quantized weights, 2 for F16). Timed per call, including the x
+    split and row-scale pre-passes."""
+    torch = _torch()
+    from lestramanika_b200 import api
+    out_n, in_n, n_tok = MATMUL_SHAPE
+    dev = torch.device("cuda", device)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(12)
+    x = torch.randn((n_tok, in_n), device=dev, generator=gen)
+    y = torch.empty((n_tok, out_n), device=dev)
+    ws = torch.empty(api.matmul_workspace(out_n, in_n, n_tok), dtype=torch.uint8, device=dev)
+    res = {}
+    for name in types:
+        t = getattr(api, "GGML_" + name)
+        wbytes = api.matvec_row_bytes(t, in_n) * out_n
+        if t == api.GGML_F16:
+            W = torch.randn((out_n, in_n), device=dev, generator=gen).half().view(torch.uint8).reshape(-1)
+        else:      # random quant bytes with small positive f16 block scales
+            W = torch.randint(0, 256, (wbytes,), device=dev, dtype=torch.uint8, generator=gen)
+            bb, offs = {api.GGML_Q8_0: (34, (0,)), api.GGML_Q4_K: (144, (0, 2))}[t]
+            b = W.view(-1, bb)
+            for off in offs:
+                sc = (torch.rand((b.shape[0],), device=dev, generator=gen) * 0.02 + 0.005).half()
+                b[:, off:off + 2] = sc.view(torch.uint8).view(-1, 2)
+        st = torch.cuda.current_stream()
+        for _ in range(warmup):
+            api.matmul_dev(t, W, out_n, in_n, x, y, n_tok, workspace=ws, stream=st)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            api.matmul_dev(t, W, out_n, in_n, x, y, n_tok, workspace=ws, stream=st)
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        flop = 2.0 * out_n * in_n * n_tok
+        mult = 2 if t == api.GGML_F16 else 3
+        res[name] = {"ms": round(ms, 4), "TFLOPs_useful": flop / (ms * 1e-3) / 1e12,
+                     "TFLOPs_tensor_pipe": mult * flop / (ms * 1e-3) / 1e12, "mma_per_k16": mult}
+        del W
+    return {"shape": f"{out_n}x{in_n}, {n_tok} tokens", "types": res,
+            "note": "per call: x hi/lo split + per-row weight scales (pre-passes) + GEMM"}
+
+
 def matvec_cpu_baseline(types=("F16", "Q8_0", "Q6_K", "Q4_K", "Q4_0"), seconds=2.0):
     """The reference's own matvec kernels (oracle/_ref, OpenMP on all host
     cores) on the same shape: weight GB/s."""
@@ -438,6 +489,13 @@ def run_ours_single(args):
     except Exception as exc:  # reported, not hidden
         extras["matvec"] = {"error": str(exc)[:200]}
     try:
+        mml = matmul_line(device, max(min(args.steps, 10), 3), max(args.warmup, 3))
+        for r in mml["types"].values():
+            r["frac_of_measured_bf16_tensor"] = r["TFLOPs_tensor_pipe"] / bf16
+        extras["matmul"] = mml
+    except Exception as exc:  # reported, not hidden
+        extras["matmul"] = {"error": str(exc)[:200]}
+    try:
         from lestramanika_b200 import PREFILL_BF16
         pf = prefill_line(C3, device, max(5, min(args.steps, 10)), max(args.warmup, 3), PREFILL_BF16)
         pf["frac_of_measured_bf16"] = pf["TFLOPs"] / bf16
@@ -518,7 +576,7 @@ def run_ours_multi(args, rank, world, local_rank):
 
 C4_SMALL = Decode("llama3-70b decode B=2 ctx=32768 (profiling size)", 2, 64, 8, 128, 32768, 500000.0)
 ONLY = {"c2b1": (C2_B1, True), "c2b8": (C2_B8, False), "c2b64": (C2_B64, False), "c4": (C4, False),
-        "c4s": (C4_SMALL, False), "c5": (C5, False), "c3": (C3, None), "mv": (None, None)}
+        "c4s": (C4_SMALL, False), "c5": (C5, False), "c3": (C3, None), "mv": (None, None), "mm": (None, None)}
 
 
 def run_only(args):
@@ -529,6 +587,8 @@ def run_only(args):
     if args.only == "mv":
         line = matvec_line(0, args.steps, args.warmup)
         line["cpu_reference"] = matvec_cpu_baseline()
+    elif args.only == "mm":
+        line = matmul_line(0, args.steps, args.warmup)
     elif flush is None:
         from lestramanika_b200 import PREFILL_BF16
         line = prefill_line(w, 0, args.steps, args.warmup, PREFILL_BF16)

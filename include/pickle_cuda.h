@@ -263,6 +263,22 @@ PICKLE_CUDA_API size_t pickle_cuda_matvec_row_bytes(int type, int in_n);
  * Synchronous. No reference counterpart (the reference has no device). */
 PICKLE_CUDA_API int  pickle_cuda_matvec_take_error(int device, int* code);
 
+/* ---- The same projections for many activation rows (batched prefill) ----
+ * y[t][o] = sum_i W[o][i] * x[t][i] for t < n_tok: the reference's per-token
+ * pickle_fast_matmul_dispatch (src/pickle_fast.c:1423-1474, called once per
+ * token from the layer loop, :1903-1907, :2112, :2120-2133) for a whole
+ * prompt. With more than PICKLE_CUDA_MATVEC_MAX_VEC rows, F16, Q8_0, Q4_0,
+ * Q4_K and Q6_K weights whose rows are 16-byte multiples, with in_n a
+ * multiple of 256, go through a tensor-core GEMM that needs a caller-owned
+ * device workspace of pickle_cuda_matmul_workspace(out_n, in_n, n_tok) bytes
+ * (256-byte aligned); every other case (or workspace == NULL) runs the
+ * matvec over the rows in passes of eight. Same types, alignment and status
+ * codes as the matvec. */
+PICKLE_CUDA_API size_t pickle_cuda_matmul_workspace(int out_n, int in_n, int n_tok);
+PICKLE_CUDA_API int  pickle_cuda_matmul_dev(int type, const void* W, int out_n, int in_n, int n_tok,
+                                            const float* x, float* y, void* workspace, size_t ws_bytes,
+                                            void* stream);
+
 /* ---- Peer exchange of the sharded decodes (one process per GPU) ----
  * No counterpart in the reference, which runs on one host: this replaces an
  * NCCL all-gather for the small per-step payloads of the KV-head and

@@ -70,6 +70,8 @@ SIGNATURES = {
     "pickle_cuda_matvec_dev": ([_i, _vp, _i, _i, _i, _vp, _vp, _vp], _i),
     "pickle_cuda_matvec_row_bytes": ([_i, _i], _sz),
     "pickle_cuda_matvec_take_error": ([_i, ctypes.POINTER(ctypes.c_int)], _i),
+    "pickle_cuda_matmul_workspace": ([_i, _i, _i], _sz),
+    "pickle_cuda_matmul_dev": ([_i, _vp, _i, _i, _i, _vp, _vp, _vp, _sz, _vp], _i),
     "pickle_cuda_xchg_create": ([_i, _i, _sz, _i, ctypes.POINTER(_vp)], _i),
     "pickle_cuda_xchg_handle": ([_vp, _vp], _i),
     "pickle_cuda_xchg_open": ([_vp, _i, _vp], _i),
@@ -299,6 +301,21 @@ def matvec_dev(ggml_type, W, out_n, in_n, x, y, n_vec=1, stream=None):
     rc = lib().pickle_cuda_matvec_dev(ggml_type, _ptr(W), out_n, in_n, n_vec, _ptr(x), _ptr(y), _stream(stream))
     if rc != PICKLE_OK:
         raise PickleError(rc, "pickle_cuda_matvec_dev")
+
+
+def matmul_workspace(out_n, in_n, n_tok):
+    """pickle_cuda_matmul_workspace: device bytes the batched matmul's tensor-core path needs."""
+    return lib().pickle_cuda_matmul_workspace(out_n, in_n, n_tok)
+
+
+def matmul_dev(ggml_type, W, out_n, in_n, x, y, n_tok, workspace=None, stream=None):
+    """pickle_cuda_matmul_dev: y [n_tok][out_n] = x [n_tok][in_n] W^T for raw GGML weight bytes W.
+    `workspace` (a uint8 device tensor of matmul_workspace(...) bytes) enables the tensor-core GEMM."""
+    ws, nb = (None, 0) if workspace is None else (_ptr(workspace), workspace.numel() * workspace.element_size())
+    rc = lib().pickle_cuda_matmul_dev(ggml_type, _ptr(W), out_n, in_n, n_tok, _ptr(x), _ptr(y), ws, nb,
+                                      _stream(stream))
+    if rc != PICKLE_OK:
+        raise PickleError(rc, "pickle_cuda_matmul_dev")
 
 
 def matvec_take_error(device=0):

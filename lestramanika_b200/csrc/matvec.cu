@@ -23,6 +23,7 @@
 #include <cstdint>
 
 #include "matvec_tc.cuh"
+#include "matmul_tc.cuh"
 
 namespace {
 
@@ -269,5 +270,44 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_matvec_take_error(int device, int* co
         cudaMemcpyToSymbol(mvtc::g_mv_err, &zero, sizeof(int)) != cudaSuccess)
         return PICKLE_ERR_DEVICE;
     *code = v;
+    return PICKLE_OK;
+}
+
+extern "C" PICKLE_CUDA_API size_t pickle_cuda_matmul_workspace(int out_n, int in_n, int n_tok) {
+    if (out_n < 1 || in_n < 1 || n_tok < 1) return 0;
+    return mmtc::workspace_bytes(out_n, in_n, n_tok);
+}
+
+extern "C" PICKLE_CUDA_API int pickle_cuda_matmul_dev(int type, const void* W, int out_n, int in_n, int n_tok,
+                                                      const float* x, float* y, void* workspace, size_t ws_bytes,
+                                                      void* stream) {
+    if (!W || !x || !y || out_n < 1 || in_n < 1 || n_tok < 1) return PICKLE_ERR_ARG;
+    if (((uintptr_t)W | (uintptr_t)x | (uintptr_t)y) % 16) return PICKLE_ERR_ARG;
+    if (type != T_F32 && type != T_F16 && type != T_Q4_0 && type != T_Q8_0 && type != T_Q4_K && type != T_Q6_K)
+        return PICKLE_ERR_TYPE;
+    const size_t row_bytes = pickle_cuda_matvec_row_bytes(type, in_n);
+    if (row_bytes == 0) return PICKLE_ERR_ARG;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const unsigned char* w = static_cast<const unsigned char*>(W);
+    const bool ws_ok = workspace && (uintptr_t)workspace % 256 == 0 &&
+                       ws_bytes >= mmtc::workspace_bytes(out_n, in_n, n_tok);
+    if (n_tok > PICKLE_CUDA_MATVEC_MAX_VEC && ws_ok && type != T_F32 && mmtc::supported(w, row_bytes, in_n)) {
+        cudaError_t e = cudaErrorInvalidValue;
+        switch (type) {
+            case T_F16: e = mmtc::launch<T_F16>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st); break;
+            case T_Q4_0: e = mmtc::launch<T_Q4_0>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st); break;
+            case T_Q8_0: e = mmtc::launch<T_Q8_0>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st); break;
+            case T_Q4_K: e = mmtc::launch<T_Q4_K>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st); break;
+            case T_Q6_K: e = mmtc::launch<T_Q6_K>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st); break;
+        }
+        return e == cudaSuccess ? PICKLE_OK : PICKLE_ERR_DEVICE;
+    }
+    // Otherwise: the matvec, up to eight activation rows per pass over W.
+    for (int v0 = 0; v0 < n_tok; v0 += PICKLE_CUDA_MATVEC_MAX_VEC) {
+        const int nv = n_tok - v0 < PICKLE_CUDA_MATVEC_MAX_VEC ? n_tok - v0 : PICKLE_CUDA_MATVEC_MAX_VEC;
+        const int rc = pickle_cuda_matvec_dev(type, W, out_n, in_n, nv, x + (size_t)v0 * in_n,
+                                              y + (size_t)v0 * out_n, stream);
+        if (rc != PICKLE_OK) return rc;
+    }
     return PICKLE_OK;
 }
