@@ -404,6 +404,34 @@ def matmul_line(device, steps, warmup, types=("Q4_K", "Q8_0", "F16")):
             "note": "per call: x hi/lo split + per-row weight scales (pre-passes) + GEMM"}
 
 
+def matmul_cpu_baseline(types=("Q4_K", "Q8_0", "F16"), seconds=2.0):
+    """The reference's own per-token projection (oracle/_ref matvec kernels,
+    OpenMP on the host cores) on the QKV shape: ms per token, a bounded
+    sample of tokens timed and the prompt's time extrapolated."""
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+    import numpy as np
+    sys.path.insert(0, ROOT)
+    from oracle import matvec as mv
+    if mv.ref_lib() is None:
+        return {"unavailable": "oracle/_ref/libref_matvec.so not built"}
+    out_n, in_n, n_tok = MATMUL_SHAPE
+    res = {}
+    for name in types:
+        t = mv.TYPES[name]
+        W = mv.random_weights(t, out_n, in_n, np.random.default_rng(t))
+        x = np.random.default_rng(1).standard_normal(in_n, dtype=np.float32)
+        mv.ref_matvec(t, W, out_n, in_n, x)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds / len(types):
+            mv.ref_matvec(t, W, out_n, in_n, x)
+            n += 1
+        ms_tok = (time.perf_counter() - t0) / n * 1e3
+        res[name] = {"ms_per_token": ms_tok, "ms_per_prompt": ms_tok * n_tok, "tokens_timed": n,
+                     "TFLOPs": 2.0 * out_n * in_n / (ms_tok * 1e-3) / 1e12}
+    return {"kind": "reference", "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+            "sample": f"one token per call, {n_tok}-token prompt extrapolated", "types": res}
+
+
 def matvec_cpu_baseline(types=("F16", "Q8_0", "Q6_K", "Q4_K", "Q4_0"), seconds=2.0):
     """The reference's own matvec kernels (oracle/_ref, OpenMP on all host
     cores) on the same shape: weight GB/s."""
@@ -589,6 +617,11 @@ def run_only(args):
         line["cpu_reference"] = matvec_cpu_baseline()
     elif args.only == "mm":
         line = matmul_line(0, args.steps, args.warmup)
+        line["cpu_reference"] = matmul_cpu_baseline()
+        for k, r in line["types"].items():
+            ref = line["cpu_reference"].get("types", {}).get(k)
+            if ref:
+                r["speedup_vs_reference"] = ref["ms_per_prompt"] / r["ms"]
     elif flush is None:
         from lestramanika_b200 import PREFILL_BF16
         line = prefill_line(w, 0, args.steps, args.warmup, PREFILL_BF16)
