@@ -432,6 +432,107 @@ def matmul_cpu_baseline(types=("Q4_K", "Q8_0", "F16"), seconds=2.0):
             "sample": f"one token per call, {n_tok}-token prompt extrapolated", "types": res}
 
 
+# Llama-3-8B attention half of one layer for a 2048-token prompt (hidden
+# 4096, 32 query heads, 8 KV heads, head dim 128), Q4_K weights.
+PL_SHAPE = dict(hidden=4096, H=32, HK=8, D=128, T=2048, wtype="Q4_K", theta=500000.0)
+
+
+def prefill_layer_line(device, steps, warmup):
+    """LayerPrefill (q/k/v GEMMs -> RoPE, cache append, BF16 tensor-core
+    causal attention -> output GEMM) for one prompt: ms per layer and prompt
+    tokens per second per layer."""
+    torch = _torch()
+    from lestramanika_b200 import PREFILL_BF16, PickleCuda, api
+    from lestramanika_b200.prefill_layer import LayerPrefill
+    c = PL_SHAPE
+    dev = torch.device("cuda", device)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(21)
+    t = getattr(api, "GGML_" + c["wtype"])
+    qd, kd = c["H"] * c["D"], c["HK"] * c["D"]
+
+    def weights(out_n, in_n):
+        W = torch.randint(0, 256, (api.matvec_row_bytes(t, in_n) * out_n,), device=dev, dtype=torch.uint8,
+                          generator=gen)
+        b = W.view(-1, 144)
+        for off in (0, 2):
+            sc = (torch.rand((b.shape[0],), device=dev, generator=gen) * 0.002 + 0.0005).half()
+            b[:, off:off + 2] = sc.view(torch.uint8).view(-1, 2)
+        return (t, W)
+
+    cu = PickleCuda(1, c["H"], c["HK"], c["D"], c["T"] + 8, rope_theta=c["theta"], device=device)
+    lp = LayerPrefill(cu, weights(qd, c["hidden"]), weights(kd, c["hidden"]), weights(kd, c["hidden"]),
+                      weights(c["hidden"], qd), hidden=c["hidden"], max_tokens=c["T"])
+    x = torch.randn((c["T"], c["hidden"]), device=dev, generator=gen) * 0.05
+    out = torch.empty((c["T"], c["hidden"]), device=dev)
+    st = torch.cuda.current_stream()
+    for _ in range(warmup):
+        lp.run(0, 0, x, out, PREFILL_BF16, st)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        lp.run(0, 0, x, out, PREFILL_BF16, st)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    cu.close()
+    flop_proj = 2.0 * c["T"] * c["hidden"] * (2 * qd + 2 * kd)
+    flop_attn = 4.0 * c["D"] * c["H"] * c["T"] * (c["T"] + 1) / 2
+    return {"workload": "llama3-8b attention half of one layer, %d-token prompt, %s weights, BF16 attention"
+                        % (c["T"], c["wtype"]),
+            "ms_per_layer": round(ms, 4), "prompt_tokens_per_s": c["T"] / (ms * 1e-3),
+            "TFLOPs_useful": (flop_proj + flop_attn) / (ms * 1e-3) / 1e12}
+
+
+def prefill_layer_cpu(seconds=6.0):
+    """The reference's own token-by-token cost of the same work on the host
+    cores: its matvec kernels for the four projections of one token, and its
+    attention block (oracle/_ref) at sampled positions of the prompt;
+    extrapolated to the prompt."""
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+    import numpy as np
+    sys.path.insert(0, ROOT)
+    import oracle
+    from oracle import matvec as mv
+    if mv.ref_lib() is None or not oracle.RefBlock.available():
+        return {"unavailable": "oracle/_ref libraries not built"}
+    c = PL_SHAPE
+    t = mv.TYPES[c["wtype"]]
+    qd, kd = c["H"] * c["D"], c["HK"] * c["D"]
+    rng = np.random.default_rng(3)
+    proj_ms = 0.0
+    for out_n, in_n in ((qd, c["hidden"]), (kd, c["hidden"]), (kd, c["hidden"]), (c["hidden"], qd)):
+        W = mv.random_weights(t, out_n, in_n, rng)
+        xv = rng.standard_normal(in_n, dtype=np.float32)
+        mv.ref_matvec(t, W, out_n, in_n, xv)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds / 8:
+            mv.ref_matvec(t, W, out_n, in_n, xv)
+            n += 1
+        proj_ms += (time.perf_counter() - t0) / n * 1e3
+    blk = oracle.RefBlock(1, c["H"], c["HK"], c["D"], c["T"] + 1, c["theta"])
+    lib = oracle.RefBlock.lib()
+    n_el = (c["T"] + 1) * c["HK"] * c["D"]
+    np.ctypeslib.as_array(lib.ref_block_k_cache(blk._h), shape=(n_el,))[:] = rng.standard_normal(n_el, dtype=np.float32)
+    np.ctypeslib.as_array(lib.ref_block_v_cache(blk._h), shape=(n_el,))[:] = rng.standard_normal(n_el, dtype=np.float32)
+    q = rng.standard_normal(qd, dtype=np.float32)
+    k = rng.standard_normal(kd, dtype=np.float32)
+    v = rng.standard_normal(kd, dtype=np.float32)
+    positions = np.linspace(0, c["T"] - 1, 16).astype(int)
+    blk.decode(0, int(positions[-1]), q, k, v)
+    t0 = time.perf_counter()
+    for p in positions:
+        blk.decode(0, int(p), q, k, v)
+    attn_ms = (time.perf_counter() - t0) / len(positions) * 1e3
+    blk.close()
+    per_tok = proj_ms + attn_ms
+    return {"kind": "reference", "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+            "sample": "one token's four projections, attention at 16 positions spread over the prompt",
+            "ms_per_token": per_tok, "ms_per_layer": per_tok * c["T"], "projections_ms_per_token": proj_ms,
+            "attention_ms_per_token": attn_ms}
+
+
 def matvec_cpu_baseline(types=("F16", "Q8_0", "Q6_K", "Q4_K", "Q4_0"), seconds=2.0):
     """The reference's own matvec kernels (oracle/_ref, OpenMP on all host
     cores) on the same shape: weight GB/s."""
@@ -524,6 +625,10 @@ def run_ours_single(args):
     except Exception as exc:  # reported, not hidden
         extras["matmul"] = {"error": str(exc)[:200]}
     try:
+        extras["prefill_layer"] = prefill_layer_line(device, max(min(args.steps, 10), 3), max(args.warmup, 3))
+    except Exception as exc:  # reported, not hidden
+        extras["prefill_layer"] = {"error": str(exc)[:200]}
+    try:
         from lestramanika_b200 import PREFILL_BF16
         pf = prefill_line(C3, device, max(5, min(args.steps, 10)), max(args.warmup, 3), PREFILL_BF16)
         pf["frac_of_measured_bf16"] = pf["TFLOPs"] / bf16
@@ -604,7 +709,8 @@ def run_ours_multi(args, rank, world, local_rank):
 
 C4_SMALL = Decode("llama3-70b decode B=2 ctx=32768 (profiling size)", 2, 64, 8, 128, 32768, 500000.0)
 ONLY = {"c2b1": (C2_B1, True), "c2b8": (C2_B8, False), "c2b64": (C2_B64, False), "c4": (C4, False),
-        "c4s": (C4_SMALL, False), "c5": (C5, False), "c3": (C3, None), "mv": (None, None), "mm": (None, None)}
+        "c4s": (C4_SMALL, False), "c5": (C5, False), "c3": (C3, None), "mv": (None, None), "mm": (None, None),
+        "pl": (None, None)}
 
 
 def run_only(args):
@@ -615,6 +721,11 @@ def run_only(args):
     if args.only == "mv":
         line = matvec_line(0, args.steps, args.warmup)
         line["cpu_reference"] = matvec_cpu_baseline()
+    elif args.only == "pl":
+        line = prefill_layer_line(0, args.steps, args.warmup)
+        line["cpu_reference"] = prefill_layer_cpu()
+        if "ms_per_layer" in line["cpu_reference"]:
+            line["speedup_vs_reference"] = line["cpu_reference"]["ms_per_layer"] / line["ms_per_layer"]
     elif args.only == "mm":
         line = matmul_line(0, args.steps, args.warmup)
         line["cpu_reference"] = matmul_cpu_baseline()
