@@ -533,6 +533,170 @@ def prefill_layer_cpu(seconds=6.0):
             "attention_ms_per_token": attn_ms}
 
 
+FW_SHAPE = dict(n_layers=32, hidden=4096, ffn=14336, H=32, HK=8, D=128, vocab=128256, max_seq=4096, prompt=2048,
+                n_gen=64, theta=500000.0)
+# Q4_K_M-like mix (the per-tensor choice of llama.cpp's Q4_K_M files); token_embd F16, norms F32
+FW_MIX = dict(attn_q="Q4_K", attn_k="Q4_K", attn_v="Q6_K", attn_output="Q4_K", ffn_gate="Q4_K", ffn_up="Q4_K",
+              ffn_down="Q6_K", output="Q6_K")
+
+
+def _fw_model(device, c):
+    """Synthetic Llama-3-8B-shaped weights generated on the device (raw GGML
+    blocks, random quants, block scales giving weights of a few hundredths)
+    and a PickleModel over them."""
+    torch = _torch()
+    from lestramanika_b200 import api
+    from lestramanika_b200.model import PickleModel
+    dev = torch.device("cuda", device)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(33)
+    HD, ID, VS, qd, kd = c["hidden"], c["ffn"], c["vocab"], c["H"] * c["D"], c["HK"] * c["D"]
+    scale_at = {"Q4_K": ((0, 1e-4, 3e-4), (2, 1e-4, 3e-4)), "Q6_K": ((208, 1e-5, 3e-5),)}
+
+    def quant(name, out_n, in_n):
+        t = getattr(api, "GGML_" + name)
+        W = torch.randint(0, 256, (api.matvec_row_bytes(t, in_n) * out_n,), device=dev, dtype=torch.uint8,
+                          generator=gen)
+        b = W.view(-1, 144 if name == "Q4_K" else 210)
+        for off, lo, hi in scale_at[name]:
+            sc = (torch.rand((b.shape[0],), device=dev, generator=gen) * (hi - lo) + lo).half()
+            b[:, off:off + 2] = sc.view(torch.uint8).view(-1, 2)
+        return (t, W)
+
+    def norm():
+        return (0, (1.0 + 0.1 * torch.randn(HD, device=dev, generator=gen)).contiguous())
+
+    shapes = {"attn_q": (qd, HD), "attn_k": (kd, HD), "attn_v": (kd, HD), "attn_output": (HD, qd),
+              "ffn_gate": (ID, HD), "ffn_up": (ID, HD), "ffn_down": (HD, ID)}
+    t = {"token_embd.weight": (1, (torch.randn((VS, HD), device=dev, generator=gen) * 0.02).half()),
+         "output_norm.weight": norm(), "output.weight": quant(FW_MIX["output"], VS, HD)}
+    for L in range(c["n_layers"]):
+        t[f"blk.{L}.attn_norm.weight"] = norm()
+        t[f"blk.{L}.ffn_norm.weight"] = norm()
+        for n, (o, i) in shapes.items():
+            t[f"blk.{L}.{n}.weight"] = quant(FW_MIX[n], o, i)
+    arch = dict(n_layers=c["n_layers"], hidden_dim=HD, intermediate_dim=ID, n_heads=c["H"], n_kv_heads=c["HK"],
+                head_dim=c["D"], vocab_size=VS, max_seq=c["max_seq"], rms_eps=1e-5, rope_theta=c["theta"])
+    weight_bytes = sum(v[1].numel() * v[1].element_size() for k, v in t.items() if k != "token_embd.weight")
+    return t, arch, weight_bytes
+
+
+def forward_line(device, steps, warmup):
+    """The whole forward pass on the device (pickle_cuda_model_*), Llama-3-8B
+    shape, Q4_K_M-like weights: a 2048-token prompt through all 32 layers
+    (GEMMs + BF16 causal attention), then greedy decode steps at context
+    2048+ (matvecs + split-KV decode + argmax, the id fed back on the
+    device); and the same through the host API pickle_cuda_generate (prompt
+    from host memory, ids and logits back)."""
+    torch = _torch()
+    from lestramanika_b200 import PREFILL_BF16
+    from lestramanika_b200.model import PickleModel
+    c = FW_SHAPE
+    dev = torch.device("cuda", device)
+    tensors, arch, wbytes = _fw_model(device, c)
+    m = PickleModel(tensors, arch, device=device, max_tokens=c["prompt"], precision=PREFILL_BF16)
+    g = torch.Generator()
+    g.manual_seed(5)
+    prompt = torch.randint(3, c["vocab"], (c["prompt"],), generator=g, dtype=torch.int32)
+    tok = prompt.to(dev)
+    logits = torch.empty(c["vocab"], device=dev)
+    nxt = torch.zeros(1, dtype=torch.int32, device=dev)
+    st = torch.cuda.Stream(device=dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # prefill
+    for _ in range(warmup):
+        m.forward_dev(tok, 0, logits, nxt, stream=st)
+    m.sync(stream=st)
+    n_pf = max(2, min(steps, 5))
+    e0.record(st)
+    for _ in range(n_pf):
+        m.forward_dev(tok, 0, logits, nxt, stream=st)
+    e1.record(st)
+    m.sync(stream=st)
+    pf_ms = e0.elapsed_time(e1) / n_pf
+    # decode: n_gen greedy steps after the prompt, ids fed back on the device
+    n_dec = c["n_gen"]
+    for i in range(max(warmup, 3)):
+        m.forward_dev(nxt, c["prompt"] + i, logits, nxt, stream=st)
+    m.sync(stream=st)
+    m.forward_dev(tok, 0, logits, nxt, stream=st)
+    e0.record(st)
+    for i in range(n_dec):
+        m.forward_dev(nxt, c["prompt"] + i, logits, nxt, stream=st)
+    e1.record(st)
+    m.sync(stream=st)
+    dec_ms = e0.elapsed_time(e1) / n_dec
+    # end to end through the host API
+    m.generate(prompt.numpy(), 4)
+    t0 = time.perf_counter()
+    ids, _, pos = m.generate(prompt.numpy(), n_dec)
+    e2e_s = time.perf_counter() - t0
+    m.close()
+    kv_bytes = 2 * c["n_layers"] * c["HK"] * c["D"] * 4 * (c["prompt"] + n_dec / 2)   # f32 cache read per step
+    dec_bytes = wbytes + c["hidden"] * 2 + kv_bytes
+    return {"workload": "llama3-8b forward, Q4_K_M-like weights (synthetic, on device), %d-token prompt with "
+                        "BF16 causal attention, then %d greedy decode steps" % (c["prompt"], n_dec),
+            "prefill_ms": round(pf_ms, 3), "prefill_tokens_per_s": c["prompt"] / (pf_ms * 1e-3),
+            "decode_ms_per_token": round(dec_ms, 4), "decode_tokens_per_s": 1e3 / dec_ms,
+            "decode_bytes_per_token": dec_bytes, "decode_GBps": dec_bytes / (dec_ms * 1e-3) / 1e9,
+            "weight_bytes": wbytes,
+            "e2e_generate": {"s": e2e_s, "n_prompt": c["prompt"], "n_gen": int(len(ids)), "kv_pos": int(pos),
+                             "h2d_bytes": c["prompt"] * 4, "d2h_bytes": int(len(ids)) * 4 + c["vocab"] * 4,
+                             "tokens_per_s": (c["prompt"] + len(ids)) / e2e_s}}
+
+
+def forward_cpu(seconds=8.0):
+    """The reference's own per-token cost of the same forward on the host
+    cores: its matvec kernels (oracle/_ref) for every projection shape and
+    type of one layer and for the lm_head, and its attention block at
+    context 2048; one token = 32 layers of that + the lm_head. The reference
+    runs the prompt through the same per-token loop."""
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+    import numpy as np
+    sys.path.insert(0, ROOT)
+    import oracle
+    from oracle import matvec as mv
+    if mv.ref_lib() is None or not oracle.RefBlock.available():
+        return {"unavailable": "oracle/_ref libraries not built"}
+    c = FW_SHAPE
+    HD, ID, qd, kd = c["hidden"], c["ffn"], c["H"] * c["D"], c["HK"] * c["D"]
+    shapes = {"attn_q": (qd, HD), "attn_k": (kd, HD), "attn_v": (kd, HD), "attn_output": (HD, qd),
+              "ffn_gate": (ID, HD), "ffn_up": (ID, HD), "ffn_down": (HD, ID), "output": (c["vocab"], HD)}
+    rng = np.random.default_rng(4)
+    ms = {}
+    for n, (out_n, in_n) in shapes.items():
+        t = mv.TYPES[FW_MIX[n]]
+        W = mv.random_weights(t, out_n, in_n, rng)
+        xv = rng.standard_normal(in_n, dtype=np.float32)
+        mv.ref_matvec(t, W, out_n, in_n, xv)
+        k, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds / 10 or k < 2:
+            mv.ref_matvec(t, W, out_n, in_n, xv)
+            k += 1
+        ms[n] = (time.perf_counter() - t0) / k * 1e3
+        del W
+    P = c["prompt"]
+    blk = oracle.RefBlock(1, c["H"], c["HK"], c["D"], P + 1, c["theta"])
+    lib = oracle.RefBlock.lib()
+    n_el = (P + 1) * c["HK"] * c["D"]
+    np.ctypeslib.as_array(lib.ref_block_k_cache(blk._h), shape=(n_el,))[:] = rng.standard_normal(n_el, dtype=np.float32)
+    np.ctypeslib.as_array(lib.ref_block_v_cache(blk._h), shape=(n_el,))[:] = rng.standard_normal(n_el, dtype=np.float32)
+    q, k_, v = (rng.standard_normal(d, dtype=np.float32) for d in (qd, kd, kd))
+    blk.decode(0, P, q, k_, v)
+    t0 = time.perf_counter()
+    for _ in range(8):
+        blk.decode(0, P, q, k_, v)
+    attn_ms = (time.perf_counter() - t0) / 8 * 1e3
+    blk.close()
+    layer_ms = sum(v for n, v in ms.items() if n != "output") + attn_ms
+    tok_ms = c["n_layers"] * layer_ms + ms["output"]
+    return {"kind": "reference", "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+            "sample": "one token: each projection shape/type of a layer once, attention at context 2048, "
+                      "lm_head; x 32 layers",
+            "decode_ms_per_token": tok_ms, "decode_tokens_per_s": 1e3 / tok_ms,
+            "prefill_ms_upper": P * tok_ms, "projection_ms": ms, "attention_ms_at_2048": attn_ms}
+
+
 def matvec_cpu_baseline(types=("F16", "Q8_0", "Q6_K", "Q4_K", "Q4_0"), seconds=2.0):
     """The reference's own matvec kernels (oracle/_ref, OpenMP on all host
     cores) on the same shape: weight GB/s."""
@@ -710,7 +874,7 @@ def run_ours_multi(args, rank, world, local_rank):
 C4_SMALL = Decode("llama3-70b decode B=2 ctx=32768 (profiling size)", 2, 64, 8, 128, 32768, 500000.0)
 ONLY = {"c2b1": (C2_B1, True), "c2b8": (C2_B8, False), "c2b64": (C2_B64, False), "c4": (C4, False),
         "c4s": (C4_SMALL, False), "c5": (C5, False), "c3": (C3, None), "mv": (None, None), "mm": (None, None),
-        "pl": (None, None)}
+        "pl": (None, None), "fw": (None, None)}
 
 
 def run_only(args):
@@ -726,6 +890,12 @@ def run_only(args):
         line["cpu_reference"] = prefill_layer_cpu()
         if "ms_per_layer" in line["cpu_reference"]:
             line["speedup_vs_reference"] = line["cpu_reference"]["ms_per_layer"] / line["ms_per_layer"]
+    elif args.only == "fw":
+        line = forward_line(0, args.steps, args.warmup)
+        line["cpu_reference"] = forward_cpu()
+        ref = line["cpu_reference"]
+        if "decode_ms_per_token" in ref:
+            line["decode_speedup_vs_reference"] = ref["decode_ms_per_token"] / line["decode_ms_per_token"]
     elif args.only == "mm":
         line = matmul_line(0, args.steps, args.warmup)
         line["cpu_reference"] = matmul_cpu_baseline()

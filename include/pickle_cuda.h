@@ -279,6 +279,85 @@ PICKLE_CUDA_API int  pickle_cuda_matmul_dev(int type, const void* W, int out_n, 
                                             const float* x, float* y, void* workspace, size_t ws_bytes,
                                             void* stream);
 
+/* ---- The whole forward pass on the device ----
+ * Replaces pickle_fast_state_init + pickle_fast_forward
+ * (src/pickle_fast.c:1497-1662, 1822-2184) and the greedy decode loop of
+ * pickle_chat_loop (src/pickle_host.c:473-521) for Llama-family GGUF models.
+ * A model is loaded from the same tensors pickle_fast_state_init finds by
+ * name (:1530-1633); each is its raw GGML bytes, [out][in] as on disk. */
+typedef struct pickle_cuda_model pickle_cuda_model_t;
+
+typedef struct {
+    int         type;    /* GGML type: 0 F32, 1 F16, 2 Q4_0, 8 Q8_0, 12 Q4_K, 14 Q6_K */
+    const void* data;    /* host bytes, or device bytes when weights_on_device; NULL = absent */
+    size_t      nbytes;  /* must equal rows * pickle_cuda_matvec_row_bytes(type, cols) */
+} pickle_cuda_tensor_t;
+
+/* Per-layer tensors, in this order ("blk.<L>.<name>.weight"):
+ * attn_norm, attn_q, attn_k, attn_v, attn_output, ffn_norm, ffn_gate,
+ * ffn_up, ffn_down. Norm weights are F32. */
+#define PICKLE_CUDA_LAYER_TENSORS 9
+
+typedef struct {
+    int   n_layers, hidden_dim, intermediate_dim;   /* state->n_layers, hidden_dim, intermediate_dim */
+    int   n_heads, n_kv_heads, head_dim;            /* H, HK, D (D a multiple of 4) */
+    int   vocab_size, max_seq;                      /* VS, cache positions (arch->max_seq_len) */
+    float rms_eps, rope_theta;                      /* state->rms_eps; theta when rope_inv_freq is NULL */
+    const float* rope_inv_freq;                     /* host [min(D/2, 64)] or NULL, as pickle_cuda_params_t */
+    int   max_tokens;         /* prompt tokens per device pass (activation buffers and GEMM workspace
+                                 are sized for it); longer prompts run in chunks */
+    int   prefill_precision;  /* PICKLE_CUDA_PREFILL_F32 (parity) or PICKLE_CUDA_PREFILL_BF16 */
+    int   weights_on_device;  /* 0: data are host pointers, copied into one device allocation at load;
+                                 1: data are 16-byte aligned device pointers used in place (the caller
+                                 keeps them alive until pickle_cuda_model_free) */
+    pickle_cuda_tensor_t token_embd;   /* "token_embd.weight", F32 or F16 [vocab][hidden] (the reference
+                                          dequantizes other types to F32 at state init, :1551-1584) */
+    pickle_cuda_tensor_t output_norm;  /* "output_norm.weight", F32 [hidden]; NULL = no final norm */
+    pickle_cuda_tensor_t output;       /* "output.weight" [vocab][hidden]; NULL = token_embd (tied) */
+    const pickle_cuda_tensor_t* layers; /* [n_layers][PICKLE_CUDA_LAYER_TENSORS] */
+} pickle_cuda_model_params_t;
+
+/* Uploads the weights and allocates the device KV cache (one sequence),
+ * the activations and the GEMM workspace. PICKLE_ERR_ARCH: a required
+ * tensor is missing; PICKLE_ERR_TYPE: a type the device path does not run;
+ * PICKLE_ERR_ARG: a size that does not match the dimensions. */
+PICKLE_CUDA_API int  pickle_cuda_model_load(const pickle_cuda_model_params_t* params, int device,
+                                            pickle_cuda_model_t** out);
+PICKLE_CUDA_API void pickle_cuda_model_free(pickle_cuda_model_t* m);
+/* The attention handle inside the model (its KV cache, decode plan). */
+PICKLE_CUDA_API pickle_cuda_t* pickle_cuda_model_attn(pickle_cuda_model_t* m);
+PICKLE_CUDA_API const char* pickle_cuda_model_last_error(pickle_cuda_model_t* m);
+
+/* pickle_fast_forward with host buffers: n_tokens tokens at positions
+ * *kv_pos .. *kv_pos + n_tokens - 1; out_logits [vocab] gets the last
+ * token's logits; *kv_pos advances by n_tokens. Synchronous.
+ * PICKLE_ERR_RANGE for a token outside [0, vocab) or a position >= max_seq
+ * (nothing is computed and *kv_pos is kept, as the reference keeps it). */
+PICKLE_CUDA_API int  pickle_cuda_forward(pickle_cuda_model_t* m, const int32_t* tokens, size_t n_tokens,
+                                         float* out_logits, size_t* kv_pos);
+/* The same on device buffers, asynchronous on `stream`: tokens_dev [n_tokens]
+ * at positions pos0.., logits_dev [vocab] (last token), and, when next_dev is
+ * not NULL, its pickle_fast_argmax id in *next_dev. Device-side errors (a token
+ * id out of range, a bounded wait that gave up) are reported by
+ * pickle_cuda_model_sync. */
+PICKLE_CUDA_API int  pickle_cuda_forward_dev(pickle_cuda_model_t* m, const int32_t* tokens_dev, size_t n_tokens,
+                                             size_t pos0, float* logits_dev, int32_t* next_dev, void* stream);
+PICKLE_CUDA_API int  pickle_cuda_model_sync(pickle_cuda_model_t* m, void* stream);
+/* pickle_fast_argmax (src/pickle_fast.c:2186-2194) on the device: the first
+ * index holding the largest value, as a scan that keeps the first strictly
+ * larger one finds it (so 0 when logits[0] is NaN, other NaNs never win).
+ * logits [n] and out (one int32) are device buffers; asynchronous. */
+PICKLE_CUDA_API int  pickle_cuda_argmax_dev(const float* logits, int n, int32_t* out, void* stream);
+/* Greedy generation as pickle_chat_loop runs it with temp <= 0: forward the
+ * prompt, then n_gen times take the argmax id, stop after eos_id (>= 0;
+ * -1 = none) or when the cache is full, else forward that id. The ids stay
+ * on the device between steps. out_ids [n_gen] gets *n_out ids, last_logits
+ * [vocab] (optional) the logits the last id was taken from, or those after
+ * its forward when it was forwarded, and *kv_pos the next free position. */
+PICKLE_CUDA_API int  pickle_cuda_generate(pickle_cuda_model_t* m, const int32_t* prompt, size_t n_prompt,
+                                          int n_gen, int eos_id, int32_t* out_ids, int* n_out,
+                                          float* last_logits, size_t* kv_pos);
+
 /* ---- Peer exchange of the sharded decodes (one process per GPU) ----
  * No counterpart in the reference, which runs on one host: this replaces an
  * NCCL all-gather for the small per-step payloads of the KV-head and

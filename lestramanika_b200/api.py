@@ -44,6 +44,28 @@ class Params(ctypes.Structure):
 
 _lib = None
 _vp, _fp, _i, _sz = ctypes.c_void_p, ctypes.POINTER(ctypes.c_float), ctypes.c_int, ctypes.c_size_t
+_i32p = ctypes.POINTER(ctypes.c_int32)
+
+LAYER_TENSORS = 9   # PICKLE_CUDA_LAYER_TENSORS
+
+
+class Tensor(ctypes.Structure):
+    """pickle_cuda_tensor_t: one tensor's raw GGML bytes."""
+    _fields_ = [("type", _i), ("data", _vp), ("nbytes", _sz)]
+
+
+class ModelParams(ctypes.Structure):
+    """pickle_cuda_model_params_t."""
+    _fields_ = [
+        ("n_layers", _i), ("hidden_dim", _i), ("intermediate_dim", _i),
+        ("n_heads", _i), ("n_kv_heads", _i), ("head_dim", _i),
+        ("vocab_size", _i), ("max_seq", _i),
+        ("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float),
+        ("rope_inv_freq", _fp),
+        ("max_tokens", _i), ("prefill_precision", _i), ("weights_on_device", _i),
+        ("token_embd", Tensor), ("output_norm", Tensor), ("output", Tensor),
+        ("layers", ctypes.POINTER(Tensor)),
+    ]
 
 SIGNATURES = {
     "pickle_cuda_abi_version": ([], _i),
@@ -72,6 +94,15 @@ SIGNATURES = {
     "pickle_cuda_matvec_take_error": ([_i, ctypes.POINTER(ctypes.c_int)], _i),
     "pickle_cuda_matmul_workspace": ([_i, _i, _i], _sz),
     "pickle_cuda_matmul_dev": ([_i, _vp, _i, _i, _i, _vp, _vp, _vp, _sz, _vp], _i),
+    "pickle_cuda_model_load": ([ctypes.POINTER(ModelParams), _i, ctypes.POINTER(_vp)], _i),
+    "pickle_cuda_model_free": ([_vp], None),
+    "pickle_cuda_model_attn": ([_vp], _vp),
+    "pickle_cuda_model_last_error": ([_vp], ctypes.c_char_p),
+    "pickle_cuda_forward": ([_vp, _i32p, _sz, _fp, ctypes.POINTER(_sz)], _i),
+    "pickle_cuda_forward_dev": ([_vp, _vp, _sz, _sz, _vp, _vp, _vp], _i),
+    "pickle_cuda_model_sync": ([_vp, _vp], _i),
+    "pickle_cuda_argmax_dev": ([_vp, _i, _vp, _vp], _i),
+    "pickle_cuda_generate": ([_vp, _i32p, _sz, _i, _i, _i32p, ctypes.POINTER(_i), _fp, ctypes.POINTER(_sz)], _i),
     "pickle_cuda_xchg_create": ([_i, _i, _sz, _i, ctypes.POINTER(_vp)], _i),
     "pickle_cuda_xchg_handle": ([_vp, _vp], _i),
     "pickle_cuda_xchg_open": ([_vp, _i, _vp], _i),
@@ -325,6 +356,13 @@ def matvec_take_error(device=0):
     if rc != PICKLE_OK:
         raise PickleError(rc, "pickle_cuda_matvec_take_error")
     return code.value
+
+
+def argmax_dev(logits, out, stream=None):
+    """pickle_fast_argmax on a device f32 vector into a device int32 (asynchronous)."""
+    rc = lib().pickle_cuda_argmax_dev(_ptr(logits), logits.numel(), _ptr(out), _stream(stream))
+    if rc != PICKLE_OK:
+        raise PickleError(rc, "pickle_cuda_argmax_dev")
 
 
 def abi_version():

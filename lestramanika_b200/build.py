@@ -39,7 +39,8 @@ def build_lib(force=False, verbose=False):
     cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
            "-Xcompiler", "-fvisibility=hidden", "-I" + os.path.join(ROOT, "include"), "-I" + CSRC,
            "-DPICKLE_CUDA_BUILD", "-o", LIB + ".tmp", os.path.join(CSRC, "pickle_cuda.cu"),
-           os.path.join(CSRC, "decode_noalloc.cu"), os.path.join(CSRC, "peer_xchg.cu"), os.path.join(CSRC, "matvec.cu")]
+           os.path.join(CSRC, "decode_noalloc.cu"), os.path.join(CSRC, "peer_xchg.cu"), os.path.join(CSRC, "matvec.cu"),
+           os.path.join(CSRC, "forward.cu")]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)

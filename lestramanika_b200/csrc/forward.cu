@@ -1,0 +1,609 @@
+// forward.cu - pickle_fast_forward on the device.
+//
+// The reference's forward pass (lee-muriithi-kingori/lestramanika
+// src/pickle_fast.c:1822-2184) runs every prompt token through every layer on
+// the host:
+//   x = token_embd[tok]                                        :1887-1897
+//   per layer L:
+//     xn = rmsnorm(x, attn_norm)                               :1899-1901
+//     q, k, v = Wq xn, Wk xn, Wv xn                            :1903-1908
+//     ao = attention block (RoPE, cache append, softmax . V)   :1910-2109
+//     x += Wo ao                                               :2112-2114
+//     xn2 = rmsnorm(x, ffn_norm)                               :2117-2118
+//     act = silu(Wgate xn2) * (Wup xn2)                        :2120-2131
+//     x += Wdown act                                           :2133-2135
+//   last token: x = rmsnorm(x, output_norm); logits = Wout x   :2138-2174
+// and the caller picks the next token with pickle_fast_argmax (:2186-2194).
+//
+// Here all of it stays in HBM: the weights are uploaded once, in their raw
+// GGML blocks, into one allocation; a prompt chunk of T tokens goes through
+// each projection as one GEMM (pickle_cuda_matmul_dev) and through the
+// attention block as one causal prefill (pickle_cuda_prefill_dev); a decode
+// step (T = 1) uses the matvec and the split-KV decode. The elementwise work
+// of the reference's loop is fused into four small kernels below (norm with
+// the residual add before it, embedding with the first norm, SwiGLU, argmax).
+// The greedy loop feeds each argmax id back on the device, so a generation
+// of n tokens needs no host round trip per token.
+#include "pickle_cuda.h"
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "pcu_common.cuh"
+
+namespace {
+
+enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
+
+constexpr int kNormThreads = 256;
+constexpr int kArgmaxThreads = 1024;
+constexpr int kLayerTensors = PICKLE_CUDA_LAYER_TENSORS;
+
+// Block-wide float sum (kNormThreads threads); every thread gets the total.
+__device__ float block_sum(float v) {
+    __shared__ float part[kNormThreads / 32];
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) part[w] = v;
+    __syncthreads();
+    float t = l < kNormThreads / 32 ? part[l] : 0.0f;
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    return t;
+}
+
+// pickle_fast_rmsnorm (src/pickle_fast.c:114-120) of row x into xn:
+//   rsq = 1 / sqrtf(sum(x^2) / n + eps);  xn[i] = x[i] * w[i] * rsq.
+// w == nullptr copies x (a model without output_norm, state->t_norm < 0).
+__device__ void norm_row(const float* x, const float* w, float* xn, int n, float eps, float ss) {
+    if (!w) {
+        for (int i = threadIdx.x; i < n; i += kNormThreads) xn[i] = x[i];
+        return;
+    }
+    const float mean = ss / (float)n;
+    const float rsq = 1.0f / sqrtf(mean + eps);
+    for (int i = threadIdx.x; i < n; i += kNormThreads) xn[i] = (x[i] * w[i]) * rsq;
+}
+
+// One CTA per token row r = blockIdx.x: x[r] += delta[r] (the residual add
+// after a projection, skipped when delta is null), then
+// xn[r] = rmsnorm(x[r], w).
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta,
+                                                                   const float* __restrict__ w, float* __restrict__ xn,
+                                                                   int n, float eps) {
+    const size_t r = blockIdx.x;
+    float* xr = x + r * n;
+    const float* dr = delta ? delta + r * n : nullptr;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += kNormThreads) {
+        float v = xr[i];
+        if (dr) {
+            v += dr[i];
+            xr[i] = v;
+        }
+        ss += v * v;
+    }
+    ss = block_sum(ss);
+    norm_row(xr, w, xn + r * n, n, eps, ss);
+}
+
+// Embedding lookup (src/pickle_fast.c:1887-1897: F32 rows, or F16 rows
+// converted exactly) fused with the first layer's attention norm. A token
+// outside [0, vocab) is recorded as PCU_DEVERR_ARG and looked up as 0; the
+// host entry points check host tokens before they are uploaded.
+__global__ void __launch_bounds__(kNormThreads) embed_rmsnorm_kernel(const int32_t* __restrict__ tok,
+                                                                     const void* __restrict__ emb, int emb_f16,
+                                                                     int vocab, const float* __restrict__ w,
+                                                                     float* __restrict__ x, float* __restrict__ xn,
+                                                                     int n, float eps, int* err) {
+    const size_t r = blockIdx.x;
+    int t = tok[r];
+    if (t < 0 || t >= vocab) {
+        if (threadIdx.x == 0) record_error(err, PCU_DEVERR_ARG);
+        t = 0;
+    }
+    float* xr = x + r * n;
+    float ss = 0.0f;
+    if (emb_f16) {
+        const __half* e = static_cast<const __half*>(emb) + (size_t)t * n;
+        for (int i = threadIdx.x; i < n; i += kNormThreads) {
+            const float v = __half2float(e[i]);
+            xr[i] = v;
+            ss += v * v;
+        }
+    } else {
+        const float* e = static_cast<const float*>(emb) + (size_t)t * n;
+        for (int i = threadIdx.x; i < n; i += kNormThreads) {
+            const float v = e[i];
+            xr[i] = v;
+            ss += v * v;
+        }
+    }
+    ss = block_sum(ss);
+    norm_row(xr, w, xn + r * n, n, eps, ss);
+}
+
+// SwiGLU (src/pickle_fast.c:2124-2131), in place over the gate rows:
+//   g[i] = g[i] * (1 / (1 + expf(-g[i]))) * up[i].
+__global__ void swiglu_kernel(float* __restrict__ g, const float* __restrict__ up, size_t n) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const float gv = g[i];
+        const float sig = 1.0f / (1.0f + expf(-gv));
+        g[i] = gv * sig * up[i];
+    }
+}
+
+// pickle_fast_argmax (src/pickle_fast.c:2186-2194): a scan from index 0 that
+// keeps the first strictly larger value. Equivalent parallel form: 0 when
+// logits[0] is NaN (nothing compares greater than it); otherwise the first
+// index of the largest non-NaN value, and 0 when no value exceeds -inf.
+// One CTA; each thread scans its strided indices in increasing order, then
+// the CTA keeps the larger value, ties going to the lower index.
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ logits, int n,
+                                                                int32_t* __restrict__ out) {
+    __shared__ float sv[kArgmaxThreads / 32];
+    __shared__ int si[kArgmaxThreads / 32];
+    float best = -INFINITY;
+    int bi = INT32_MAX;
+    for (int i = threadIdx.x; i < n; i += kArgmaxThreads) {
+        const float v = logits[i];
+        if (v > best) {
+            best = v;
+            bi = i;
+        }
+    }
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oi != INT32_MAX && (bi == INT32_MAX || ov > best || (ov == best && oi < bi))) {
+            best = ov;
+            bi = oi;
+        }
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) {
+        sv[w] = best;
+        si[w] = bi;
+    }
+    __syncthreads();
+    if (w == 0) {
+        best = l < kArgmaxThreads / 32 ? sv[l] : -INFINITY;
+        bi = l < kArgmaxThreads / 32 ? si[l] : INT32_MAX;
+        #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi != INT32_MAX && (bi == INT32_MAX || ov > best || (ov == best && oi < bi))) {
+                best = ov;
+                bi = oi;
+            }
+        }
+        if (l == 0) *out = (bi == INT32_MAX || isnan(logits[0])) ? 0 : bi;
+    }
+}
+
+size_t row_bytes_of(int type, int in_n) { return pickle_cuda_matvec_row_bytes(type, in_n); }
+
+size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+struct DevTensor {
+    int type = -1;
+    const void* d = nullptr;
+};
+
+}  // namespace
+
+// Tensor roles of one layer, in the order of pickle_cuda_model_params_t.layers.
+enum { R_ATTN_NORM, R_Q, R_K, R_V, R_O, R_FFN_NORM, R_GATE, R_UP, R_DOWN };
+
+struct pickle_cuda_model {
+    int device = 0;
+    int NL = 0, HD = 0, ID = 0, H = 0, HK = 0, D = 0, VS = 0, max_seq = 0, max_tok = 0, precision = 0;
+    float eps = 0;
+    pickle_cuda_t* attn = nullptr;
+    void* blob = nullptr;            // the uploaded weights (null: caller-owned device pointers)
+    DevTensor embd, out_norm, out;   // out.d == embd.d when tied
+    std::vector<DevTensor> lt;       // [NL][9]
+    // activations [max_tok][...] and the GEMM workspace
+    float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *ao = nullptr, *proj = nullptr,
+          *gate = nullptr, *up = nullptr, *logits = nullptr, *logits2 = nullptr;
+    int32_t *tok = nullptr, *ids = nullptr;   // ids: [max_seq + 1]
+    int* err = nullptr;
+    int32_t* ids_host = nullptr;              // pinned [max_seq + 1]
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    void* act_blob = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev = nullptr;
+    std::string last_error;
+};
+
+namespace {
+
+int fail(pickle_cuda_model* m, int rc, const char* what) {
+    if (m) m->last_error = what;
+    return rc;
+}
+
+int mm(pickle_cuda_model* m, const DevTensor& w, const float* x, float* y, int out_n, int in_n, int T,
+       cudaStream_t st) {
+    return pickle_cuda_matmul_dev(w.type, w.d, out_n, in_n, T, x, y, m->ws, m->ws_bytes, st);
+}
+
+// T tokens (device ids at tok_dev) at positions [pos0, pos0 + T), T <= max_tok,
+// all layers; when with_logits, the last row's logits go to logits_dev and
+// its argmax to next_dev (when non-null). Asynchronous on st.
+int run_chunk(pickle_cuda_model* m, const int32_t* tok_dev, int T, size_t pos0, bool with_logits, float* logits_dev,
+              int32_t* next_dev, cudaStream_t st) {
+    const int HD = m->HD, ID = m->ID, qd = m->H * m->D, kd = m->HK * m->D;
+    const DevTensor* L0 = &m->lt[0];
+    embed_rmsnorm_kernel<<<T, kNormThreads, 0, st>>>(tok_dev, m->embd.d, m->embd.type == T_F16, m->VS,
+                                                     static_cast<const float*>(L0[R_ATTN_NORM].d), m->x, m->xn, HD,
+                                                     m->eps, m->err);
+    if (cudaGetLastError() != cudaSuccess) return fail(m, PICKLE_ERR_DEVICE, "embedding launch failed");
+    int rc = PICKLE_OK;
+    for (int L = 0; L < m->NL; ++L) {
+        const DevTensor* W = &m->lt[(size_t)L * kLayerTensors];
+        if (L > 0) {
+            add_rmsnorm_kernel<<<T, kNormThreads, 0, st>>>(m->x, m->proj, static_cast<const float*>(W[R_ATTN_NORM].d),
+                                                           m->xn, HD, m->eps);
+            if (cudaGetLastError() != cudaSuccess) return fail(m, PICKLE_ERR_DEVICE, "norm launch failed");
+        }
+        if ((rc = mm(m, W[R_Q], m->xn, m->q, qd, HD, T, st)) != PICKLE_OK) return fail(m, rc, "q projection");
+        if ((rc = mm(m, W[R_K], m->xn, m->k, kd, HD, T, st)) != PICKLE_OK) return fail(m, rc, "k projection");
+        if ((rc = mm(m, W[R_V], m->xn, m->v, kd, HD, T, st)) != PICKLE_OK) return fail(m, rc, "v projection");
+        rc = T == 1 ? pickle_cuda_decode_batch_dev(m->attn, L, 1, pos0, m->q, m->k, m->v, m->ao, st)
+                    : pickle_cuda_prefill_dev(m->attn, L, 1, pos0, (size_t)T, m->q, m->k, m->v, m->ao, m->precision,
+                                              st);
+        if (rc != PICKLE_OK) return fail(m, rc, pickle_cuda_last_error(m->attn));
+        if ((rc = mm(m, W[R_O], m->ao, m->proj, HD, qd, T, st)) != PICKLE_OK) return fail(m, rc, "output projection");
+        add_rmsnorm_kernel<<<T, kNormThreads, 0, st>>>(m->x, m->proj, static_cast<const float*>(W[R_FFN_NORM].d),
+                                                       m->xn, HD, m->eps);
+        if (cudaGetLastError() != cudaSuccess) return fail(m, PICKLE_ERR_DEVICE, "norm launch failed");
+        if ((rc = mm(m, W[R_GATE], m->xn, m->gate, ID, HD, T, st)) != PICKLE_OK) return fail(m, rc, "gate projection");
+        if ((rc = mm(m, W[R_UP], m->xn, m->up, ID, HD, T, st)) != PICKLE_OK) return fail(m, rc, "up projection");
+        const size_t n_act = (size_t)T * ID;
+        const int blocks = (int)((n_act + 255) / 256 < 148 * 8 ? (n_act + 255) / 256 : 148 * 8);
+        swiglu_kernel<<<blocks, 256, 0, st>>>(m->gate, m->up, n_act);
+        if (cudaGetLastError() != cudaSuccess) return fail(m, PICKLE_ERR_DEVICE, "swiglu launch failed");
+        if ((rc = mm(m, W[R_DOWN], m->gate, m->proj, HD, ID, T, st)) != PICKLE_OK) return fail(m, rc, "down projection");
+    }
+    // A chunk before the last one leaves only its cache rows behind.
+    if (!with_logits) return PICKLE_OK;
+    // Last token only: x += down; xn = rmsnorm(x, output_norm); logits.
+    const size_t last = (size_t)(T - 1) * HD;
+    add_rmsnorm_kernel<<<1, kNormThreads, 0, st>>>(m->x + last, m->proj + last,
+                                                   static_cast<const float*>(m->out_norm.d), m->xn + last, HD, m->eps);
+    if (cudaGetLastError() != cudaSuccess) return fail(m, PICKLE_ERR_DEVICE, "norm launch failed");
+    if ((rc = mm(m, m->out, m->xn + last, logits_dev, m->VS, HD, 1, st)) != PICKLE_OK)
+        return fail(m, rc, "output projection (lm_head)");
+    if (next_dev) {
+        argmax_kernel<<<1, kArgmaxThreads, 0, st>>>(logits_dev, m->VS, next_dev);
+        if (cudaGetLastError() != cudaSuccess) return fail(m, PICKLE_ERR_DEVICE, "argmax launch failed");
+    }
+    return PICKLE_OK;
+}
+
+// n tokens already on the device, chunked by max_tok; only the last chunk
+// computes logits.
+int run_tokens(pickle_cuda_model* m, const int32_t* tok_dev, size_t n, size_t pos0, float* logits_dev,
+               int32_t* next_dev, cudaStream_t st) {
+    for (size_t c0 = 0; c0 < n; c0 += (size_t)m->max_tok) {
+        const int T = (int)(n - c0 < (size_t)m->max_tok ? n - c0 : (size_t)m->max_tok);
+        const bool last = c0 + (size_t)T == n;
+        const int rc = run_chunk(m, tok_dev + c0, T, pos0 + c0, last, logits_dev, next_dev, st);
+        if (rc != PICKLE_OK) return rc;
+    }
+    return PICKLE_OK;
+}
+
+// Waits for the stream, then collects the device error words: the model's
+// (token ids out of range), the attention handle's (bounded waits, device
+// argument checks) and the matvec's (bounded waits).
+int finish(pickle_cuda_model* m, cudaStream_t st) {
+    if (cudaStreamSynchronize(st) != cudaSuccess) return fail(m, PICKLE_ERR_DEVICE, "stream synchronize failed");
+    int e = 0;
+    if (cudaMemcpy(&e, m->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return fail(m, PICKLE_ERR_DEVICE, "error word read failed");
+    if (e) {
+        cudaMemset(m->err, 0, sizeof(int));
+        return fail(m, PICKLE_ERR_RANGE, "token id outside [0, vocab) on the device");
+    }
+    int rc = pickle_cuda_sync(m->attn, st);
+    if (rc != PICKLE_OK) return fail(m, rc, pickle_cuda_last_error(m->attn));
+    int code = 0;
+    if (pickle_cuda_matvec_take_error(m->device, &code) != PICKLE_OK || code)
+        return fail(m, PICKLE_ERR_DEVICE, "projection kernel gave up waiting");
+    return PICKLE_OK;
+}
+
+void free_model(pickle_cuda_model* m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->attn) pickle_cuda_free(m->attn);
+    cudaFree(m->blob);
+    cudaFree(m->act_blob);
+    cudaFree(m->ws);
+    if (m->ids_host) cudaFreeHost(m->ids_host);
+    if (m->ev) cudaEventDestroy(m->ev);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+int check_matrix(const pickle_cuda_tensor_t& t, int out_n, int in_n, bool on_dev) {
+    if (!t.data) return PICKLE_ERR_ARCH;
+    const size_t rb = row_bytes_of(t.type, in_n);
+    if (t.type != T_F32 && t.type != T_F16 && t.type != T_Q4_0 && t.type != T_Q8_0 && t.type != T_Q4_K &&
+        t.type != T_Q6_K)
+        return PICKLE_ERR_TYPE;
+    if (rb == 0 || t.nbytes != rb * (size_t)out_n) return PICKLE_ERR_ARG;
+    if (on_dev && (uintptr_t)t.data % 16) return PICKLE_ERR_ARG;
+    return PICKLE_OK;
+}
+
+int check_vector(const pickle_cuda_tensor_t& t, int n, bool on_dev) {
+    if (!t.data) return PICKLE_ERR_ARCH;
+    if (t.type != T_F32) return PICKLE_ERR_TYPE;
+    if (t.nbytes != (size_t)n * 4) return PICKLE_ERR_ARG;
+    if (on_dev && (uintptr_t)t.data % 16) return PICKLE_ERR_ARG;
+    return PICKLE_OK;
+}
+
+}  // namespace
+
+extern "C" PICKLE_CUDA_API int pickle_cuda_model_load(const pickle_cuda_model_params_t* p, int device,
+                                                      pickle_cuda_model_t** out) {
+    if (!p || !out) return PICKLE_ERR_ARG;
+    *out = nullptr;
+    if (p->n_layers < 1 || p->hidden_dim < 4 || p->hidden_dim % 4 || p->intermediate_dim < 4 ||
+        p->intermediate_dim % 4 || p->n_heads < 1 || p->n_kv_heads < 1 || p->n_heads % p->n_kv_heads ||
+        p->head_dim < 4 || p->head_dim % 4 || p->vocab_size < 1 || p->max_seq < 1 || p->max_tokens < 1 ||
+        !(p->rms_eps >= 0.0f) || !p->layers ||
+        (p->prefill_precision != PICKLE_CUDA_PREFILL_F32 && p->prefill_precision != PICKLE_CUDA_PREFILL_BF16))
+        return PICKLE_ERR_ARG;
+    const bool on_dev = p->weights_on_device != 0;
+    const int HD = p->hidden_dim, ID = p->intermediate_dim, qd = p->n_heads * p->head_dim,
+              kd = p->n_kv_heads * p->head_dim;
+    // Shapes and types, as pickle_fast_state_init finds them (src/pickle_fast.c:1530-1633).
+    const pickle_cuda_tensor_t& E = p->token_embd;
+    if (!E.data) return PICKLE_ERR_ARCH;
+    if (E.type != T_F32 && E.type != T_F16) return PICKLE_ERR_TYPE;
+    if (E.nbytes != (size_t)p->vocab_size * HD * (E.type == T_F32 ? 4 : 2)) return PICKLE_ERR_ARG;
+    int rc;
+    if (p->output_norm.data && (rc = check_vector(p->output_norm, HD, on_dev)) != PICKLE_OK) return rc;
+    if (p->output.data && (rc = check_matrix(p->output, p->vocab_size, HD, on_dev)) != PICKLE_OK) return rc;
+    for (int L = 0; L < p->n_layers; ++L) {
+        const pickle_cuda_tensor_t* t = p->layers + (size_t)L * kLayerTensors;
+        if ((rc = check_vector(t[R_ATTN_NORM], HD, on_dev)) != PICKLE_OK) return rc;
+        if ((rc = check_vector(t[R_FFN_NORM], HD, on_dev)) != PICKLE_OK) return rc;
+        if ((rc = check_matrix(t[R_Q], qd, HD, on_dev)) != PICKLE_OK) return rc;
+        if ((rc = check_matrix(t[R_K], kd, HD, on_dev)) != PICKLE_OK) return rc;
+        if ((rc = check_matrix(t[R_V], kd, HD, on_dev)) != PICKLE_OK) return rc;
+        if ((rc = check_matrix(t[R_O], HD, qd, on_dev)) != PICKLE_OK) return rc;
+        if ((rc = check_matrix(t[R_GATE], ID, HD, on_dev)) != PICKLE_OK) return rc;
+        if ((rc = check_matrix(t[R_UP], ID, HD, on_dev)) != PICKLE_OK) return rc;
+        if ((rc = check_matrix(t[R_DOWN], HD, ID, on_dev)) != PICKLE_OK) return rc;
+    }
+    if (on_dev && (uintptr_t)E.data % 16) return PICKLE_ERR_ARG;
+
+    pickle_cuda_model* m = new (std::nothrow) pickle_cuda_model();
+    if (!m) return PICKLE_ERR_MEMORY;
+    m->device = device;
+    m->NL = p->n_layers; m->HD = HD; m->ID = ID; m->H = p->n_heads; m->HK = p->n_kv_heads; m->D = p->head_dim;
+    m->VS = p->vocab_size; m->max_seq = p->max_seq; m->max_tok = p->max_tokens; m->precision = p->prefill_precision;
+    m->eps = p->rms_eps;
+    if (cudaSetDevice(device) != cudaSuccess) { free_model(m); return PICKLE_ERR_DEVICE; }
+
+    // Attention block state: the device KV cache and RoPE table.
+    pickle_cuda_params_t ap{};
+    ap.n_layers = p->n_layers; ap.n_heads = p->n_heads; ap.n_kv_heads = p->n_kv_heads; ap.head_dim = p->head_dim;
+    ap.max_seq = p->max_seq; ap.half = p->head_dim / 2 < 64 ? p->head_dim / 2 : 64;
+    ap.rope_inv_freq = p->rope_inv_freq; ap.rope_theta = p->rope_theta; ap.n_seqs = 1; ap.rope_len = 0;
+    if ((rc = pickle_cuda_init(&ap, device, &m->attn)) != PICKLE_OK) { free_model(m); return rc; }
+
+    // Weights: one allocation, every tensor 256-byte aligned, uploaded once.
+    std::vector<const pickle_cuda_tensor_t*> all;
+    all.push_back(&p->token_embd);
+    if (p->output_norm.data) all.push_back(&p->output_norm);
+    if (p->output.data) all.push_back(&p->output);
+    for (size_t i = 0; i < (size_t)p->n_layers * kLayerTensors; ++i) all.push_back(p->layers + i);
+    std::vector<const void*> where(all.size());
+    if (on_dev) {
+        for (size_t i = 0; i < all.size(); ++i) where[i] = all[i]->data;
+    } else {
+        size_t total = 0;
+        for (auto* t : all) total += align256(t->nbytes);
+        if (cudaMalloc(&m->blob, total) != cudaSuccess) { free_model(m); return PICKLE_ERR_MEMORY; }
+        size_t off = 0;
+        for (size_t i = 0; i < all.size(); ++i) {
+            char* dst = static_cast<char*>(m->blob) + off;
+            if (cudaMemcpy(dst, all[i]->data, all[i]->nbytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+                free_model(m);
+                return PICKLE_ERR_DEVICE;
+            }
+            where[i] = dst;
+            off += align256(all[i]->nbytes);
+        }
+    }
+    size_t wi = 0;
+    m->embd = {E.type, where[wi++]};
+    m->out_norm = p->output_norm.data ? DevTensor{T_F32, where[wi++]} : DevTensor{};
+    // A model without output.weight (or with tied embeddings) projects with
+    // token_embd (src/pickle_fast.c:2142-2166).
+    m->out = p->output.data ? DevTensor{p->output.type, where[wi++]} : m->embd;
+    m->lt.resize((size_t)p->n_layers * kLayerTensors);
+    for (size_t i = 0; i < m->lt.size(); ++i) m->lt[i] = {p->layers[i].type, where[wi++]};
+
+    // Activations for max_tok rows.
+    const size_t T = (size_t)m->max_tok;
+    const size_t sizes[] = {T * HD * 4, T * HD * 4, T * qd * 4, T * kd * 4, T * kd * 4, T * qd * 4, T * HD * 4,
+                            T * ID * 4, T * ID * 4, (size_t)m->VS * 4, (size_t)m->VS * 4, T * 4, ((size_t)m->max_seq + 1) * 4, 256};
+    size_t total = 0;
+    for (size_t s : sizes) total += align256(s);
+    if (cudaMalloc(&m->act_blob, total) != cudaSuccess) { free_model(m); return PICKLE_ERR_MEMORY; }
+    char* a = static_cast<char*>(m->act_blob);
+    void** dst[] = {(void**)&m->x, (void**)&m->xn, (void**)&m->q, (void**)&m->k, (void**)&m->v, (void**)&m->ao,
+                    (void**)&m->proj, (void**)&m->gate, (void**)&m->up, (void**)&m->logits, (void**)&m->logits2, (void**)&m->tok,
+                    (void**)&m->ids, (void**)&m->err};
+    for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); ++i) {
+        *dst[i] = a;
+        a += align256(sizes[i]);
+    }
+    if (cudaMemset(m->err, 0, sizeof(int)) != cudaSuccess) { free_model(m); return PICKLE_ERR_DEVICE; }
+    const int shapes[][2] = {{qd, HD}, {kd, HD}, {HD, qd}, {ID, HD}, {HD, ID}};
+    for (auto& s : shapes) {
+        const size_t b = pickle_cuda_matmul_workspace(s[0], s[1], m->max_tok);
+        if (b > m->ws_bytes) m->ws_bytes = b;
+    }
+    if (cudaMalloc(&m->ws, m->ws_bytes) != cudaSuccess) { free_model(m); return PICKLE_ERR_MEMORY; }
+    if (cudaHostAlloc((void**)&m->ids_host, ((size_t)m->max_seq + 1) * 4, cudaHostAllocDefault) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&m->ev, cudaEventDisableTiming) != cudaSuccess) {
+        free_model(m);
+        return PICKLE_ERR_DEVICE;
+    }
+    *out = m;
+    return PICKLE_OK;
+}
+
+extern "C" PICKLE_CUDA_API void pickle_cuda_model_free(pickle_cuda_model_t* m) { free_model(m); }
+
+extern "C" PICKLE_CUDA_API pickle_cuda_t* pickle_cuda_model_attn(pickle_cuda_model_t* m) {
+    return m ? m->attn : nullptr;
+}
+
+extern "C" PICKLE_CUDA_API const char* pickle_cuda_model_last_error(pickle_cuda_model_t* m) {
+    return m ? m->last_error.c_str() : "null model";
+}
+
+extern "C" PICKLE_CUDA_API int pickle_cuda_forward(pickle_cuda_model_t* m, const int32_t* tokens, size_t n_tokens,
+                                                   float* out_logits, size_t* kv_pos) {
+    if (!m || !tokens || !out_logits || !kv_pos || n_tokens == 0) return PICKLE_ERR_ARG;
+    if (cudaSetDevice(m->device) != cudaSuccess) return PICKLE_ERR_DEVICE;
+    const size_t pos0 = *kv_pos;
+    // The reference stops at the first token outside [0, vocab) or at a
+    // position >= max_seq (src/pickle_fast.c:1881-1885) and leaves kv_pos
+    // where it was; checking them all first gives the same status and kv_pos.
+    for (size_t i = 0; i < n_tokens; ++i)
+        if (tokens[i] < 0 || tokens[i] >= m->VS) return fail(m, PICKLE_ERR_RANGE, "token id outside [0, vocab)");
+    if (pos0 + n_tokens > (size_t)m->max_seq) return fail(m, PICKLE_ERR_RANGE, "position >= max_seq");
+    cudaStream_t st = m->stream;
+    for (size_t c0 = 0; c0 < n_tokens; c0 += (size_t)m->max_tok) {
+        const size_t T = n_tokens - c0 < (size_t)m->max_tok ? n_tokens - c0 : (size_t)m->max_tok;
+        if (cudaMemcpyAsync(m->tok, tokens + c0, T * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+            return fail(m, PICKLE_ERR_DEVICE, "token upload failed");
+        const bool last = c0 + T == n_tokens;
+        const int rc = run_chunk(m, m->tok, (int)T, pos0 + c0, last, m->logits, nullptr, st);
+        if (rc != PICKLE_OK) return rc;
+        if (!last && cudaStreamSynchronize(st) != cudaSuccess)   // m->tok is reused by the next chunk
+            return fail(m, PICKLE_ERR_DEVICE, "stream synchronize failed");
+    }
+    if (cudaMemcpyAsync(out_logits, m->logits, (size_t)m->VS * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return fail(m, PICKLE_ERR_DEVICE, "logits download failed");
+    const int rc = finish(m, st);
+    if (rc != PICKLE_OK) return rc;
+    *kv_pos = pos0 + n_tokens;
+    return PICKLE_OK;
+}
+
+extern "C" PICKLE_CUDA_API int pickle_cuda_forward_dev(pickle_cuda_model_t* m, const int32_t* tokens_dev,
+                                                       size_t n_tokens, size_t pos0, float* logits_dev,
+                                                       int32_t* next_dev, void* stream) {
+    if (!m || !tokens_dev || !logits_dev || n_tokens == 0) return PICKLE_ERR_ARG;
+    if ((uintptr_t)logits_dev % 16) return PICKLE_ERR_ARG;
+    if (pos0 + n_tokens > (size_t)m->max_seq) return fail(m, PICKLE_ERR_RANGE, "position >= max_seq");
+    if (cudaSetDevice(m->device) != cudaSuccess) return PICKLE_ERR_DEVICE;
+    return run_tokens(m, tokens_dev, n_tokens, pos0, logits_dev, next_dev, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" PICKLE_CUDA_API int pickle_cuda_argmax_dev(const float* logits, int n, int32_t* out, void* stream) {
+    if (!logits || !out || n < 1) return PICKLE_ERR_ARG;
+    argmax_kernel<<<1, kArgmaxThreads, 0, static_cast<cudaStream_t>(stream)>>>(logits, n, out);
+    return cudaGetLastError() == cudaSuccess ? PICKLE_OK : PICKLE_ERR_DEVICE;
+}
+
+extern "C" PICKLE_CUDA_API int pickle_cuda_model_sync(pickle_cuda_model_t* m, void* stream) {
+    if (!m) return PICKLE_ERR_ARG;
+    if (cudaSetDevice(m->device) != cudaSuccess) return PICKLE_ERR_DEVICE;
+    return finish(m, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" PICKLE_CUDA_API int pickle_cuda_generate(pickle_cuda_model_t* m, const int32_t* prompt, size_t n_prompt,
+                                                    int n_gen, int eos_id, int32_t* out_ids, int* n_out,
+                                                    float* last_logits, size_t* kv_pos) {
+    if (!m || !prompt || n_prompt == 0 || n_gen < 0 || (n_gen > 0 && !out_ids) || !n_out || !kv_pos)
+        return PICKLE_ERR_ARG;
+    *n_out = 0;
+    if (cudaSetDevice(m->device) != cudaSuccess) return PICKLE_ERR_DEVICE;
+    for (size_t i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= m->VS) return fail(m, PICKLE_ERR_RANGE, "token id outside [0, vocab)");
+    size_t pos = *kv_pos;
+    if (pos + n_prompt > (size_t)m->max_seq) return fail(m, PICKLE_ERR_RANGE, "position >= max_seq");
+    cudaStream_t st = m->stream;
+    // The prompt in one forward (src/pickle_host.c:473-475); its argmax is id 0.
+    for (size_t c0 = 0; c0 < n_prompt; c0 += (size_t)m->max_tok) {
+        const size_t T = n_prompt - c0 < (size_t)m->max_tok ? n_prompt - c0 : (size_t)m->max_tok;
+        if (cudaMemcpyAsync(m->tok, prompt + c0, T * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+            return fail(m, PICKLE_ERR_DEVICE, "token upload failed");
+        const bool last = c0 + T == n_prompt;
+        const int rc = run_chunk(m, m->tok, (int)T, pos + c0, last, m->logits, m->ids, st);
+        if (rc != PICKLE_OK) return rc;
+        if (!last && cudaStreamSynchronize(st) != cudaSuccess)   // m->tok is reused by the next chunk
+            return fail(m, PICKLE_ERR_DEVICE, "stream synchronize failed");
+    }
+    pos += n_prompt;
+    // The greedy decode loop of pickle_chat_loop (src/pickle_host.c:489-521):
+    // id i is the argmax of the current logits; the loop stops after an id
+    // equal to eos_id, or when the cache is full, and otherwise forwards id i
+    // at the next position, whose argmax is id i + 1. The ids stay on the
+    // device (ids[i] feeds the next embedding lookup). Without an eos_id the
+    // host only enqueues. With one, the host copies id i out before it
+    // enqueues the forward of id i and checks it while that forward runs; a
+    // forward after the eos id is thrown away: its logits went to the other
+    // of two buffers, and the cache row it wrote lies beyond the returned
+    // kv_pos.
+    const bool eos = eos_id >= 0;
+    float* lbuf[2] = {m->logits, m->logits2};
+    int cur = 0, done = 0;
+    for (int i = 0; i < n_gen; ++i) {
+        if (eos && (cudaMemcpyAsync(m->ids_host + i, m->ids + i, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                    cudaEventRecord(m->ev, st) != cudaSuccess))
+            return fail(m, PICKLE_ERR_DEVICE, "id download failed");
+        const bool full = pos >= (size_t)m->max_seq;
+        const int nxt = eos ? cur ^ 1 : cur;
+        if (!full) {
+            const int rc = run_chunk(m, m->ids + i, 1, pos, true, lbuf[nxt], m->ids + i + 1, st);
+            if (rc != PICKLE_OK) return rc;
+        }
+        done = i + 1;
+        if (eos) {
+            if (cudaEventSynchronize(m->ev) != cudaSuccess) return fail(m, PICKLE_ERR_DEVICE, "event wait failed");
+            if (m->ids_host[i] == eos_id) break;
+        }
+        if (full) break;
+        pos += 1;
+        cur = nxt;
+    }
+    int rc = finish(m, st);
+    if (rc != PICKLE_OK) return rc;
+    if (done > 0 && cudaMemcpy(out_ids, m->ids, (size_t)done * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return fail(m, PICKLE_ERR_DEVICE, "ids download failed");
+    if (last_logits &&
+        cudaMemcpy(last_logits, lbuf[cur], (size_t)m->VS * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return fail(m, PICKLE_ERR_DEVICE, "logits download failed");
+    *n_out = done;
+    *kv_pos = pos;
+    return PICKLE_OK;
+}

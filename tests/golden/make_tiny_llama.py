@@ -53,26 +53,9 @@ def _s(b):
     return struct.pack("<Q", len(b)) + b
 
 
-def write_model(path, seed=0):
-    rng = np.random.Generator(np.random.Philox(seed))
-    meta = [
-        ("general.architecture", GGUF_STR, "llama"),
-        ("general.name", GGUF_STR, "pickle-b200-tiny"),
-        ("llama.block_count", GGUF_U32, N_LAYERS),
-        ("llama.embedding_length", GGUF_U32, HIDDEN),
-        ("llama.feed_forward_length", GGUF_U32, FFN),
-        ("llama.attention.head_count", GGUF_U32, N_HEADS),
-        ("llama.attention.head_count_kv", GGUF_U32, N_KV_HEADS),
-        ("llama.context_length", GGUF_U32, CTX),
-        ("llama.rope.dimension_count", GGUF_U32, HEAD_DIM),
-        ("llama.vocab_size", GGUF_U32, VOCAB),
-        ("llama.attention.layer_norm_rms_epsilon", GGUF_F32, EPS),
-        ("llama.rope.freq_base", GGUF_F32, THETA),
-        ("llama.tie_word_embeddings", GGUF_BOOL, False),
-    ]
-    tensors = _tensors()
-    datas = [rng.standard_normal(int(np.prod(shape)), dtype=np.float32) * np.float32(0.02)
-             for _, shape in tensors]
+def write_gguf(path, meta, tensors):
+    """meta: [(key, GGUF value type, value)]; tensors: [(name, shape, ggml_type,
+    raw bytes)] with shape in [out][in] order (written reversed, GGUF order)."""
     head = bytearray()
     head += struct.pack("<IIQQ", 0x46554747, 3, len(tensors), len(meta))
     for key, typ, val in meta:
@@ -87,21 +70,49 @@ def write_model(path, seed=0):
             head += struct.pack("<B", 1 if val else 0)
     off = 0
     offsets = []
-    for (name, shape), d in zip(tensors, datas):
+    for _, _, _, raw in tensors:
         offsets.append(off)
-        off += d.nbytes
+        off += len(raw)
         off += (-off) % ALIGN
-    for (name, shape), o in zip(tensors, offsets):
+    for (name, shape, gtype, _), o in zip(tensors, offsets):
         dims = tuple(reversed(shape))          # GGUF: ne[0] is the contiguous dim
         head += _s(name) + struct.pack("<I", len(dims))
         head += b"".join(struct.pack("<Q", d) for d in dims)
-        head += struct.pack("<IQ", 0, o)       # GGML_F32, offset
+        head += struct.pack("<IQ", gtype, o)
     head += b"\0" * ((-len(head)) % ALIGN)
     with open(path, "wb") as f:
         f.write(head)
-        for d, o in zip(datas, offsets):
-            f.write(d.tobytes())
-            f.write(b"\0" * ((-d.nbytes) % ALIGN))
+        for _, _, _, raw in tensors:
+            f.write(raw)
+            f.write(b"\0" * ((-len(raw)) % ALIGN))
+
+
+def llama_meta(n_layers, hidden, ffn, n_heads, n_kv_heads, head_dim, vocab, ctx, theta=THETA, eps=EPS,
+               name="pickle-b200-tiny"):
+    return [
+        ("general.architecture", GGUF_STR, "llama"),
+        ("general.name", GGUF_STR, name),
+        ("llama.block_count", GGUF_U32, n_layers),
+        ("llama.embedding_length", GGUF_U32, hidden),
+        ("llama.feed_forward_length", GGUF_U32, ffn),
+        ("llama.attention.head_count", GGUF_U32, n_heads),
+        ("llama.attention.head_count_kv", GGUF_U32, n_kv_heads),
+        ("llama.context_length", GGUF_U32, ctx),
+        ("llama.rope.dimension_count", GGUF_U32, head_dim),
+        ("llama.vocab_size", GGUF_U32, vocab),
+        ("llama.attention.layer_norm_rms_epsilon", GGUF_F32, eps),
+        ("llama.rope.freq_base", GGUF_F32, theta),
+        ("llama.tie_word_embeddings", GGUF_BOOL, False),
+    ]
+
+
+def write_model(path, seed=0):
+    rng = np.random.Generator(np.random.Philox(seed))
+    meta = llama_meta(N_LAYERS, HIDDEN, FFN, N_HEADS, N_KV_HEADS, HEAD_DIM, VOCAB, CTX)
+    tensors = _tensors()
+    datas = [rng.standard_normal(int(np.prod(shape)), dtype=np.float32) * np.float32(0.02)
+             for _, shape in tensors]
+    write_gguf(path, meta, [(name, shape, 0, d.tobytes()) for (name, shape), d in zip(tensors, datas)])
     return prompt_ids(seed)
 
 
