@@ -553,15 +553,21 @@ def _fw_model(device, c):
     HD, ID, VS, qd, kd = c["hidden"], c["ffn"], c["vocab"], c["H"] * c["D"], c["HK"] * c["D"]
     scale_at = {"Q4_K": ((0, 1e-4, 3e-4), (2, 1e-4, 3e-4)), "Q6_K": ((208, 1e-5, 3e-5),)}
 
-    def quant(name, out_n, in_n):
+    def quant(name, *shape):
+        """One allocation for same-type matrices that follow each other
+        (q|k, gate|up), as the model packs them; -> a view per matrix."""
         t = getattr(api, "GGML_" + name)
-        W = torch.randint(0, 256, (api.matvec_row_bytes(t, in_n) * out_n,), device=dev, dtype=torch.uint8,
-                          generator=gen)
+        sizes = [api.matvec_row_bytes(t, i) * o for o, i in shape]
+        W = torch.randint(0, 256, (sum(sizes),), device=dev, dtype=torch.uint8, generator=gen)
         b = W.view(-1, 144 if name == "Q4_K" else 210)
         for off, lo, hi in scale_at[name]:
             sc = (torch.rand((b.shape[0],), device=dev, generator=gen) * (hi - lo) + lo).half()
             b[:, off:off + 2] = sc.view(torch.uint8).view(-1, 2)
-        return (t, W)
+        out, o0 = [], 0
+        for n in sizes:
+            out.append((t, W[o0:o0 + n]))
+            o0 += n
+        return out
 
     def norm():
         return (0, (1.0 + 0.1 * torch.randn(HD, device=dev, generator=gen)).contiguous())
@@ -569,12 +575,15 @@ def _fw_model(device, c):
     shapes = {"attn_q": (qd, HD), "attn_k": (kd, HD), "attn_v": (kd, HD), "attn_output": (HD, qd),
               "ffn_gate": (ID, HD), "ffn_up": (ID, HD), "ffn_down": (HD, ID)}
     t = {"token_embd.weight": (1, (torch.randn((VS, HD), device=dev, generator=gen) * 0.02).half()),
-         "output_norm.weight": norm(), "output.weight": quant(FW_MIX["output"], VS, HD)}
+         "output_norm.weight": norm(), "output.weight": quant(FW_MIX["output"], (VS, HD))[0]}
+    groups = [("attn_q", "attn_k"), ("attn_v",), ("attn_output",), ("ffn_gate", "ffn_up"), ("ffn_down",)]
     for L in range(c["n_layers"]):
         t[f"blk.{L}.attn_norm.weight"] = norm()
         t[f"blk.{L}.ffn_norm.weight"] = norm()
-        for n, (o, i) in shapes.items():
-            t[f"blk.{L}.{n}.weight"] = quant(FW_MIX[n], o, i)
+        for grp in groups:
+            assert len({FW_MIX[n] for n in grp}) == 1
+            for n, w in zip(grp, quant(FW_MIX[grp[0]], *[shapes[n] for n in grp])):
+                t[f"blk.{L}.{n}.weight"] = w
     arch = dict(n_layers=c["n_layers"], hidden_dim=HD, intermediate_dim=ID, n_heads=c["H"], n_kv_heads=c["HK"],
                 head_dim=c["D"], vocab_size=VS, max_seq=c["max_seq"], rms_eps=1e-5, rope_theta=c["theta"])
     weight_bytes = sum(v[1].numel() * v[1].element_size() for k, v in t.items() if k != "token_embd.weight")
@@ -643,6 +652,36 @@ def forward_line(device, steps, warmup):
             "e2e_generate": {"s": e2e_s, "n_prompt": c["prompt"], "n_gen": int(len(ids)), "kv_pos": int(pos),
                              "h2d_bytes": c["prompt"] * 4, "d2h_bytes": int(len(ids)) * 4 + c["vocab"] * 4,
                              "tokens_per_s": (c["prompt"] + len(ids)) / e2e_s}}
+
+
+def forward_decode_line(device, steps, warmup):
+    """Decode steps of the device forward alone (Llama-3-8B shape,
+    Q4_K_M-like weights) at context 2048 of the device cache, which holds
+    zeros (the step reads the same bytes whatever they hold): the command the
+    per-kernel launch list of a decode step is taken with."""
+    torch = _torch()
+    from lestramanika_b200.model import PickleModel
+    c = FW_SHAPE
+    dev = torch.device("cuda", device)
+    tensors, arch, wbytes = _fw_model(device, c)
+    m = PickleModel(tensors, arch, device=device, max_tokens=16)
+    logits = torch.empty(c["vocab"], device=dev)
+    nxt = torch.full((1,), 7, dtype=torch.int32, device=dev)
+    st = torch.cuda.Stream(device=dev)
+    P = c["prompt"]
+    for i in range(warmup):
+        m.forward_dev(nxt, P + i, logits, nxt, stream=st)
+    m.sync(stream=st)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(steps):
+        m.forward_dev(nxt, P + i, logits, nxt, stream=st)
+    e1.record(st)
+    m.sync(stream=st)
+    ms = e0.elapsed_time(e1) / steps
+    m.close()
+    return {"workload": "llama3-8b decode steps at context %d, Q4_K_M-like weights" % P, "ms_per_token": ms,
+            "tokens_per_s": 1e3 / ms, "weight_bytes": wbytes}
 
 
 def forward_cpu(seconds=8.0):
@@ -874,7 +913,7 @@ def run_ours_multi(args, rank, world, local_rank):
 C4_SMALL = Decode("llama3-70b decode B=2 ctx=32768 (profiling size)", 2, 64, 8, 128, 32768, 500000.0)
 ONLY = {"c2b1": (C2_B1, True), "c2b8": (C2_B8, False), "c2b64": (C2_B64, False), "c4": (C4, False),
         "c4s": (C4_SMALL, False), "c5": (C5, False), "c3": (C3, None), "mv": (None, None), "mm": (None, None),
-        "pl": (None, None), "fw": (None, None)}
+        "pl": (None, None), "fw": (None, None), "fwd": (None, None)}
 
 
 def run_only(args):
@@ -896,6 +935,8 @@ def run_only(args):
         ref = line["cpu_reference"]
         if "decode_ms_per_token" in ref:
             line["decode_speedup_vs_reference"] = ref["decode_ms_per_token"] / line["decode_ms_per_token"]
+    elif args.only == "fwd":
+        line = forward_decode_line(0, args.steps, args.warmup)
     elif args.only == "mm":
         line = matmul_line(0, args.steps, args.warmup)
         line["cpu_reference"] = matmul_cpu_baseline()

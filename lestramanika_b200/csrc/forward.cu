@@ -38,15 +38,17 @@
 #include <string>
 #include <vector>
 
+#include "matvec_ex.h"
 #include "pcu_common.cuh"
 
 namespace {
 
 enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
 
-constexpr int kNormThreads = 256;
+constexpr int kNormThreads = 512;
 constexpr int kArgmaxThreads = 1024;
 constexpr int kLayerTensors = PICKLE_CUDA_LAYER_TENSORS;
+constexpr int kMaxNormVec = 16;      // float4s per thread: rows up to 4 * 16 * 512 = 32768 floats
 
 // Block-wide float sum (kNormThreads threads); every thread gets the total.
 __device__ float block_sum(float v) {
@@ -62,85 +64,178 @@ __device__ float block_sum(float v) {
     return t;
 }
 
-// pickle_fast_rmsnorm (src/pickle_fast.c:114-120) of row x into xn:
+__device__ __forceinline__ float sumsq4(float4 a) { return a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w; }
+
+// pickle_fast_rmsnorm (src/pickle_fast.c:114-120) of the row held in v
+// (thread-strided float4s) into xn:
 //   rsq = 1 / sqrtf(sum(x^2) / n + eps);  xn[i] = x[i] * w[i] * rsq.
 // w == nullptr copies x (a model without output_norm, state->t_norm < 0).
-__device__ void norm_row(const float* x, const float* w, float* xn, int n, float eps, float ss) {
-    if (!w) {
-        for (int i = threadIdx.x; i < n; i += kNormThreads) xn[i] = x[i];
-        return;
+template <int V>
+__device__ void norm_row(const float4 (&v)[V], const float* w, float* xn, int n, float eps, float ss) {
+    const int n4 = n >> 2;
+    float4* o = reinterpret_cast<float4*>(xn);
+    const float rsq = w ? 1.0f / sqrtf(ss / (float)n + eps) : 1.0f;
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    #pragma unroll
+    for (int j = 0; j < V; ++j) {
+        const int i = threadIdx.x + j * kNormThreads;
+        if (i < n4) {
+            if (!w) {
+                o[i] = v[j];
+            } else {
+                const float4 ww = w4[i];
+                o[i] = make_float4((v[j].x * ww.x) * rsq, (v[j].y * ww.y) * rsq, (v[j].z * ww.z) * rsq,
+                                   (v[j].w * ww.w) * rsq);
+            }
+        }
     }
-    const float mean = ss / (float)n;
-    const float rsq = 1.0f / sqrtf(mean + eps);
-    for (int i = threadIdx.x; i < n; i += kNormThreads) xn[i] = (x[i] * w[i]) * rsq;
 }
 
 // One CTA per token row r = blockIdx.x: x[r] += delta[r] (the residual add
 // after a projection, skipped when delta is null), then
-// xn[r] = rmsnorm(x[r], w).
+// xn[r] = rmsnorm(x[r], w). n is a multiple of 4 and at most
+// 4 * V * kNormThreads; each thread keeps its V float4s in registers.
+// Launched with programmatic stream serialization.
+template <int V>
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta,
                                                                    const float* __restrict__ w, float* __restrict__ xn,
                                                                    int n, float eps) {
+    griddep_launch_dependents();
+    griddep_wait();
     const size_t r = blockIdx.x;
-    float* xr = x + r * n;
-    const float* dr = delta ? delta + r * n : nullptr;
+    const int n4 = n >> 2;
+    float4* xr = reinterpret_cast<float4*>(x + r * n);
+    const float4* dr = delta ? reinterpret_cast<const float4*>(delta + r * n) : nullptr;
+    float4 v[V];
     float ss = 0.0f;
-    for (int i = threadIdx.x; i < n; i += kNormThreads) {
-        float v = xr[i];
-        if (dr) {
-            v += dr[i];
-            xr[i] = v;
+    #pragma unroll
+    for (int j = 0; j < V; ++j) {
+        const int i = threadIdx.x + j * kNormThreads;
+        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < n4) {
+            float4 a = xr[i];
+            if (dr) {
+                const float4 d = dr[i];
+                a = make_float4(a.x + d.x, a.y + d.y, a.z + d.z, a.w + d.w);
+                xr[i] = a;
+            }
+            v[j] = a;
+            ss += sumsq4(a);
         }
-        ss += v * v;
     }
     ss = block_sum(ss);
-    norm_row(xr, w, xn + r * n, n, eps, ss);
+    norm_row<V>(v, w, xn + r * n, n, eps, ss);
 }
 
 // Embedding lookup (src/pickle_fast.c:1887-1897: F32 rows, or F16 rows
 // converted exactly) fused with the first layer's attention norm. A token
 // outside [0, vocab) is recorded as PCU_DEVERR_ARG and looked up as 0; the
 // host entry points check host tokens before they are uploaded.
+template <int V>
 __global__ void __launch_bounds__(kNormThreads) embed_rmsnorm_kernel(const int32_t* __restrict__ tok,
                                                                      const void* __restrict__ emb, int emb_f16,
                                                                      int vocab, const float* __restrict__ w,
                                                                      float* __restrict__ x, float* __restrict__ xn,
                                                                      int n, float eps, int* err) {
+    griddep_launch_dependents();
+    griddep_wait();
     const size_t r = blockIdx.x;
     int t = tok[r];
     if (t < 0 || t >= vocab) {
         if (threadIdx.x == 0) record_error(err, PCU_DEVERR_ARG);
         t = 0;
     }
-    float* xr = x + r * n;
+    const int n4 = n >> 2;
+    float4* xr = reinterpret_cast<float4*>(x + r * n);
+    float4 v[V];
     float ss = 0.0f;
-    if (emb_f16) {
-        const __half* e = static_cast<const __half*>(emb) + (size_t)t * n;
-        for (int i = threadIdx.x; i < n; i += kNormThreads) {
-            const float v = __half2float(e[i]);
-            xr[i] = v;
-            ss += v * v;
-        }
-    } else {
-        const float* e = static_cast<const float*>(emb) + (size_t)t * n;
-        for (int i = threadIdx.x; i < n; i += kNormThreads) {
-            const float v = e[i];
-            xr[i] = v;
-            ss += v * v;
+    #pragma unroll
+    for (int j = 0; j < V; ++j) {
+        const int i = threadIdx.x + j * kNormThreads;
+        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < n4) {
+            float4 a;
+            if (emb_f16) {
+                const uint2 h = reinterpret_cast<const uint2*>(static_cast<const __half*>(emb) + (size_t)t * n)[i];
+                const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+                const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+                a = make_float4(lo.x, lo.y, hi.x, hi.y);
+            } else {
+                a = reinterpret_cast<const float4*>(static_cast<const float*>(emb) + (size_t)t * n)[i];
+            }
+            xr[i] = a;
+            v[j] = a;
+            ss += sumsq4(a);
         }
     }
     ss = block_sum(ss);
-    norm_row(xr, w, xn + r * n, n, eps, ss);
+    norm_row<V>(v, w, xn + r * n, n, eps, ss);
 }
 
-// SwiGLU (src/pickle_fast.c:2124-2131), in place over the gate rows:
-//   g[i] = g[i] * (1 / (1 + expf(-g[i]))) * up[i].
-__global__ void swiglu_kernel(float* __restrict__ g, const float* __restrict__ up, size_t n) {
+// SwiGLU (src/pickle_fast.c:2124-2131) over T rows of ID:
+//   act[t][i] = g * (1 / (1 + expf(-g))) * up,  g = gate[t * ld + i],
+//   up = gate[t * ld + up_off + i]
+// (gate and up either one [T][2 ID] output of the fused projection, or
+// act == gate with up_off the distance to a separate up buffer and ld = ID).
+__global__ void swiglu_kernel(const float* __restrict__ gate, long long up_off, long long ld, int ID, int T,
+                              float* act) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const size_t n = (size_t)T * ID;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-        const float gv = g[i];
+    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += stride) {
+        const size_t t = e / ID, i = e - t * ID;
+        const float gv = gate[t * ld + i];
+        const float up = gate[t * ld + up_off + i];
         const float sig = 1.0f / (1.0f + expf(-gv));
-        g[i] = gv * sig * up[i];
+        act[e] = gv * sig * up;
+    }
+}
+
+// Launch with programmatic stream serialization: the kernel may be
+// scheduled before the previous one in the stream ends, and waits for it
+// with griddepcontrol.wait before it reads anything.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*k)(KArgs...), unsigned grid, unsigned block, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
+// Float4s per thread for a row of n floats, as a template choice.
+int norm_vec(int n) {
+    const int per = (n / 4 + kNormThreads - 1) / kNormThreads;
+    int v = 1;
+    while (v < per) v <<= 1;
+    return v;
+}
+
+cudaError_t launch_add_rmsnorm(int T, float* x, const float* delta, const float* w, float* xn, int n, float eps,
+                               cudaStream_t st) {
+    switch (norm_vec(n)) {
+        case 1: return launch_pdl(add_rmsnorm_kernel<1>, T, kNormThreads, st, x, delta, w, xn, n, eps);
+        case 2: return launch_pdl(add_rmsnorm_kernel<2>, T, kNormThreads, st, x, delta, w, xn, n, eps);
+        case 4: return launch_pdl(add_rmsnorm_kernel<4>, T, kNormThreads, st, x, delta, w, xn, n, eps);
+        case 8: return launch_pdl(add_rmsnorm_kernel<8>, T, kNormThreads, st, x, delta, w, xn, n, eps);
+        default: return launch_pdl(add_rmsnorm_kernel<16>, T, kNormThreads, st, x, delta, w, xn, n, eps);
+    }
+}
+
+cudaError_t launch_embed_rmsnorm(int T, const int32_t* tok, const void* emb, int f16, int vocab, const float* w,
+                                 float* x, float* xn, int n, float eps, int* err, cudaStream_t st) {
+    switch (norm_vec(n)) {
+        case 1: return launch_pdl(embed_rmsnorm_kernel<1>, T, kNormThreads, st, tok, emb, f16, vocab, w, x, xn, n, eps, err);
+        case 2: return launch_pdl(embed_rmsnorm_kernel<2>, T, kNormThreads, st, tok, emb, f16, vocab, w, x, xn, n, eps, err);
+        case 4: return launch_pdl(embed_rmsnorm_kernel<4>, T, kNormThreads, st, tok, emb, f16, vocab, w, x, xn, n, eps, err);
+        case 8: return launch_pdl(embed_rmsnorm_kernel<8>, T, kNormThreads, st, tok, emb, f16, vocab, w, x, xn, n, eps, err);
+        default: return launch_pdl(embed_rmsnorm_kernel<16>, T, kNormThreads, st, tok, emb, f16, vocab, w, x, xn, n, eps, err);
     }
 }
 
@@ -152,6 +247,8 @@ __global__ void swiglu_kernel(float* __restrict__ g, const float* __restrict__ u
 // the CTA keeps the larger value, ties going to the lower index.
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ logits, int n,
                                                                 int32_t* __restrict__ out) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ float sv[kArgmaxThreads / 32];
     __shared__ int si[kArgmaxThreads / 32];
     float best = -INFINITY;
@@ -201,6 +298,7 @@ size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 struct DevTensor {
     int type = -1;
     const void* d = nullptr;
+    size_t nbytes = 0;
 };
 
 }  // namespace
@@ -216,9 +314,14 @@ struct pickle_cuda_model {
     void* blob = nullptr;            // the uploaded weights (null: caller-owned device pointers)
     DevTensor embd, out_norm, out;   // out.d == embd.d when tied
     std::vector<DevTensor> lt;       // [NL][9]
-    // activations [max_tok][...] and the GEMM workspace
+    // Per layer: how many of q, k, v (1..3) form one matrix (same type, rows
+    // back to back in memory), and whether gate and up do.
+    std::vector<int> qkv_run;
+    std::vector<char> gu_fused;
+    // activations [max_tok][...] and the GEMM workspace; gate holds
+    // [max_tok][2 ID] (the fused gate|up output), qkv1 one token's q|k|v
     float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *ao = nullptr, *proj = nullptr,
-          *gate = nullptr, *up = nullptr, *logits = nullptr, *logits2 = nullptr;
+          *gate = nullptr, *up = nullptr, *logits = nullptr, *logits2 = nullptr, *qkv1 = nullptr;
     int32_t *tok = nullptr, *ids = nullptr;   // ids: [max_seq + 1]
     int* err = nullptr;
     int32_t* ids_host = nullptr;              // pinned [max_seq + 1]
@@ -237,9 +340,10 @@ int fail(pickle_cuda_model* m, int rc, const char* what) {
     return rc;
 }
 
+// A projection with the model's own (constant) weights.
 int mm(pickle_cuda_model* m, const DevTensor& w, const float* x, float* y, int out_n, int in_n, int T,
        cudaStream_t st) {
-    return pickle_cuda_matmul_dev(w.type, w.d, out_n, in_n, T, x, y, m->ws, m->ws_bytes, st);
+    return pcu_matmul_ex(w.type, w.d, out_n, in_n, T, x, y, m->ws, m->ws_bytes, st, true);
 }
 
 // T tokens (device ids at tok_dev) at positions [pos0, pos0 + T), T <= max_tok,
@@ -249,50 +353,76 @@ int run_chunk(pickle_cuda_model* m, const int32_t* tok_dev, int T, size_t pos0, 
               int32_t* next_dev, cudaStream_t st) {
     const int HD = m->HD, ID = m->ID, qd = m->H * m->D, kd = m->HK * m->D;
     const DevTensor* L0 = &m->lt[0];
-    embed_rmsnorm_kernel<<<T, kNormThreads, 0, st>>>(tok_dev, m->embd.d, m->embd.type == T_F16, m->VS,
-                                                     static_cast<const float*>(L0[R_ATTN_NORM].d), m->x, m->xn, HD,
-                                                     m->eps, m->err);
-    if (cudaGetLastError() != cudaSuccess) return fail(m, PICKLE_ERR_DEVICE, "embedding launch failed");
+    if (launch_embed_rmsnorm(T, tok_dev, m->embd.d, m->embd.type == T_F16, m->VS,
+                             static_cast<const float*>(L0[R_ATTN_NORM].d), m->x, m->xn, HD, m->eps, m->err,
+                             st) != cudaSuccess)
+        return fail(m, PICKLE_ERR_DEVICE, "embedding launch failed");
     int rc = PICKLE_OK;
     for (int L = 0; L < m->NL; ++L) {
         const DevTensor* W = &m->lt[(size_t)L * kLayerTensors];
-        if (L > 0) {
-            add_rmsnorm_kernel<<<T, kNormThreads, 0, st>>>(m->x, m->proj, static_cast<const float*>(W[R_ATTN_NORM].d),
-                                                           m->xn, HD, m->eps);
-            if (cudaGetLastError() != cudaSuccess) return fail(m, PICKLE_ERR_DEVICE, "norm launch failed");
+        if (L > 0 && launch_add_rmsnorm(T, m->x, m->proj, static_cast<const float*>(W[R_ATTN_NORM].d), m->xn, HD,
+                                        m->eps, st) != cudaSuccess)
+            return fail(m, PICKLE_ERR_DEVICE, "norm launch failed");
+        // q, k, v. One token: into one q|k|v vector, with the projections
+        // that share a matrix in one launch. A prompt: [T][..] each, as the
+        // causal prefill reads them.
+        float *q = m->q, *k = m->k, *v = m->v;
+        if (T == 1) {
+            q = m->qkv1;
+            k = q + qd;
+            v = k + kd;
+            const int run = m->qkv_run[L];
+            const int rows1 = run == 3 ? qd + 2 * kd : run == 2 ? qd + kd : qd;
+            if ((rc = mm(m, W[R_Q], m->xn, q, rows1, HD, 1, st)) != PICKLE_OK) return fail(m, rc, "q projection");
+            if (run < 2 && (rc = mm(m, W[R_K], m->xn, k, kd, HD, 1, st)) != PICKLE_OK)
+                return fail(m, rc, "k projection");
+            if (run < 3 && (rc = mm(m, W[R_V], m->xn, v, kd, HD, 1, st)) != PICKLE_OK)
+                return fail(m, rc, "v projection");
+        } else {
+            if ((rc = mm(m, W[R_Q], m->xn, q, qd, HD, T, st)) != PICKLE_OK) return fail(m, rc, "q projection");
+            if ((rc = mm(m, W[R_K], m->xn, k, kd, HD, T, st)) != PICKLE_OK) return fail(m, rc, "k projection");
+            if ((rc = mm(m, W[R_V], m->xn, v, kd, HD, T, st)) != PICKLE_OK) return fail(m, rc, "v projection");
         }
-        if ((rc = mm(m, W[R_Q], m->xn, m->q, qd, HD, T, st)) != PICKLE_OK) return fail(m, rc, "q projection");
-        if ((rc = mm(m, W[R_K], m->xn, m->k, kd, HD, T, st)) != PICKLE_OK) return fail(m, rc, "k projection");
-        if ((rc = mm(m, W[R_V], m->xn, m->v, kd, HD, T, st)) != PICKLE_OK) return fail(m, rc, "v projection");
-        rc = T == 1 ? pickle_cuda_decode_batch_dev(m->attn, L, 1, pos0, m->q, m->k, m->v, m->ao, st)
-                    : pickle_cuda_prefill_dev(m->attn, L, 1, pos0, (size_t)T, m->q, m->k, m->v, m->ao, m->precision,
-                                              st);
+        rc = T == 1 ? pickle_cuda_decode_batch_dev(m->attn, L, 1, pos0, q, k, v, m->ao, st)
+                    : pickle_cuda_prefill_dev(m->attn, L, 1, pos0, (size_t)T, q, k, v, m->ao, m->precision, st);
         if (rc != PICKLE_OK) return fail(m, rc, pickle_cuda_last_error(m->attn));
         if ((rc = mm(m, W[R_O], m->ao, m->proj, HD, qd, T, st)) != PICKLE_OK) return fail(m, rc, "output projection");
-        add_rmsnorm_kernel<<<T, kNormThreads, 0, st>>>(m->x, m->proj, static_cast<const float*>(W[R_FFN_NORM].d),
-                                                       m->xn, HD, m->eps);
-        if (cudaGetLastError() != cudaSuccess) return fail(m, PICKLE_ERR_DEVICE, "norm launch failed");
-        if ((rc = mm(m, W[R_GATE], m->xn, m->gate, ID, HD, T, st)) != PICKLE_OK) return fail(m, rc, "gate projection");
-        if ((rc = mm(m, W[R_UP], m->xn, m->up, ID, HD, T, st)) != PICKLE_OK) return fail(m, rc, "up projection");
+        if (launch_add_rmsnorm(T, m->x, m->proj, static_cast<const float*>(W[R_FFN_NORM].d), m->xn, HD, m->eps,
+                               st) != cudaSuccess)
+            return fail(m, PICKLE_ERR_DEVICE, "norm launch failed");
+        // gate and up: one [T][2 ID] output when they share a matrix, else
+        // [T][ID] each; act goes to the up buffer.
+        long long up_off, ld;
+        if (m->gu_fused[L]) {
+            if ((rc = mm(m, W[R_GATE], m->xn, m->gate, 2 * ID, HD, T, st)) != PICKLE_OK)
+                return fail(m, rc, "gate/up projection");
+            up_off = ID;
+            ld = 2LL * ID;
+        } else {
+            if ((rc = mm(m, W[R_GATE], m->xn, m->gate, ID, HD, T, st)) != PICKLE_OK)
+                return fail(m, rc, "gate projection");
+            if ((rc = mm(m, W[R_UP], m->xn, m->up, ID, HD, T, st)) != PICKLE_OK) return fail(m, rc, "up projection");
+            up_off = m->up - m->gate;
+            ld = ID;
+        }
         const size_t n_act = (size_t)T * ID;
-        const int blocks = (int)((n_act + 255) / 256 < 148 * 8 ? (n_act + 255) / 256 : 148 * 8);
-        swiglu_kernel<<<blocks, 256, 0, st>>>(m->gate, m->up, n_act);
-        if (cudaGetLastError() != cudaSuccess) return fail(m, PICKLE_ERR_DEVICE, "swiglu launch failed");
-        if ((rc = mm(m, W[R_DOWN], m->gate, m->proj, HD, ID, T, st)) != PICKLE_OK) return fail(m, rc, "down projection");
+        const unsigned blocks = (unsigned)((n_act + 255) / 256 < 148 * 8 ? (n_act + 255) / 256 : 148 * 8);
+        if (launch_pdl(swiglu_kernel, blocks, 256, st, m->gate, up_off, ld, ID, T, m->up) != cudaSuccess)
+            return fail(m, PICKLE_ERR_DEVICE, "swiglu launch failed");
+        if ((rc = mm(m, W[R_DOWN], m->up, m->proj, HD, ID, T, st)) != PICKLE_OK) return fail(m, rc, "down projection");
     }
     // A chunk before the last one leaves only its cache rows behind.
     if (!with_logits) return PICKLE_OK;
     // Last token only: x += down; xn = rmsnorm(x, output_norm); logits.
     const size_t last = (size_t)(T - 1) * HD;
-    add_rmsnorm_kernel<<<1, kNormThreads, 0, st>>>(m->x + last, m->proj + last,
-                                                   static_cast<const float*>(m->out_norm.d), m->xn + last, HD, m->eps);
-    if (cudaGetLastError() != cudaSuccess) return fail(m, PICKLE_ERR_DEVICE, "norm launch failed");
+    if (launch_add_rmsnorm(1, m->x + last, m->proj + last, static_cast<const float*>(m->out_norm.d), m->xn + last, HD,
+                           m->eps, st) != cudaSuccess)
+        return fail(m, PICKLE_ERR_DEVICE, "norm launch failed");
     if ((rc = mm(m, m->out, m->xn + last, logits_dev, m->VS, HD, 1, st)) != PICKLE_OK)
         return fail(m, rc, "output projection (lm_head)");
-    if (next_dev) {
-        argmax_kernel<<<1, kArgmaxThreads, 0, st>>>(logits_dev, m->VS, next_dev);
-        if (cudaGetLastError() != cudaSuccess) return fail(m, PICKLE_ERR_DEVICE, "argmax launch failed");
-    }
+    if (next_dev && launch_pdl(argmax_kernel, 1, kArgmaxThreads, st, (const float*)logits_dev, m->VS, next_dev) !=
+                        cudaSuccess)
+        return fail(m, PICKLE_ERR_DEVICE, "argmax launch failed");
     return PICKLE_OK;
 }
 
@@ -370,6 +500,7 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_model_load(const pickle_cuda_model_pa
     if (p->n_layers < 1 || p->hidden_dim < 4 || p->hidden_dim % 4 || p->intermediate_dim < 4 ||
         p->intermediate_dim % 4 || p->n_heads < 1 || p->n_kv_heads < 1 || p->n_heads % p->n_kv_heads ||
         p->head_dim < 4 || p->head_dim % 4 || p->vocab_size < 1 || p->max_seq < 1 || p->max_tokens < 1 ||
+        p->hidden_dim > 4 * kMaxNormVec * kNormThreads ||
         !(p->rms_eps >= 0.0f) || !p->layers ||
         (p->prefill_precision != PICKLE_CUDA_PREFILL_F32 && p->prefill_precision != PICKLE_CUDA_PREFILL_BF16))
         return PICKLE_ERR_ARG;
@@ -413,56 +544,81 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_model_load(const pickle_cuda_model_pa
     ap.rope_inv_freq = p->rope_inv_freq; ap.rope_theta = p->rope_theta; ap.n_seqs = 1; ap.rope_len = 0;
     if ((rc = pickle_cuda_init(&ap, device, &m->attn)) != PICKLE_OK) { free_model(m); return rc; }
 
-    // Weights: one allocation, every tensor 256-byte aligned, uploaded once.
+    // Weights: one allocation, uploaded once, every tensor 256-byte aligned
+    // except that k follows q, v follows k and up follows gate with no gap
+    // when they have the same type (and the previous one's size is a
+    // multiple of 16 bytes): such a run is one [rows][in] matrix, and a
+    // decode step projects it in one launch.
     std::vector<const pickle_cuda_tensor_t*> all;
     all.push_back(&p->token_embd);
     if (p->output_norm.data) all.push_back(&p->output_norm);
     if (p->output.data) all.push_back(&p->output);
+    const size_t lbase = all.size();
     for (size_t i = 0; i < (size_t)p->n_layers * kLayerTensors; ++i) all.push_back(p->layers + i);
+    auto packs = [&](size_t i) {
+        if (i < lbase) return false;
+        const int role = (int)((i - lbase) % kLayerTensors);
+        if (role != R_K && role != R_V && role != R_UP) return false;
+        if (role == R_V && !(all[i - 1]->type == all[i - 2]->type && all[i - 2]->nbytes % 16 == 0)) return false;
+        return all[i]->type == all[i - 1]->type && all[i - 1]->nbytes % 16 == 0;
+    };
     std::vector<const void*> where(all.size());
     if (on_dev) {
         for (size_t i = 0; i < all.size(); ++i) where[i] = all[i]->data;
     } else {
+        std::vector<size_t> off(all.size());
         size_t total = 0;
-        for (auto* t : all) total += align256(t->nbytes);
-        if (cudaMalloc(&m->blob, total) != cudaSuccess) { free_model(m); return PICKLE_ERR_MEMORY; }
-        size_t off = 0;
         for (size_t i = 0; i < all.size(); ++i) {
-            char* dst = static_cast<char*>(m->blob) + off;
+            off[i] = i > 0 && packs(i) ? off[i - 1] + all[i - 1]->nbytes : align256(total);
+            total = off[i] + all[i]->nbytes;
+        }
+        if (cudaMalloc(&m->blob, align256(total)) != cudaSuccess) { free_model(m); return PICKLE_ERR_MEMORY; }
+        for (size_t i = 0; i < all.size(); ++i) {
+            char* dst = static_cast<char*>(m->blob) + off[i];
             if (cudaMemcpy(dst, all[i]->data, all[i]->nbytes, cudaMemcpyHostToDevice) != cudaSuccess) {
                 free_model(m);
                 return PICKLE_ERR_DEVICE;
             }
             where[i] = dst;
-            off += align256(all[i]->nbytes);
         }
     }
     size_t wi = 0;
-    m->embd = {E.type, where[wi++]};
-    m->out_norm = p->output_norm.data ? DevTensor{T_F32, where[wi++]} : DevTensor{};
+    m->embd = {E.type, where[wi++], E.nbytes};
+    m->out_norm = p->output_norm.data ? DevTensor{T_F32, where[wi++], p->output_norm.nbytes} : DevTensor{};
     // A model without output.weight (or with tied embeddings) projects with
     // token_embd (src/pickle_fast.c:2142-2166).
-    m->out = p->output.data ? DevTensor{p->output.type, where[wi++]} : m->embd;
+    m->out = p->output.data ? DevTensor{p->output.type, where[wi++], p->output.nbytes} : m->embd;
     m->lt.resize((size_t)p->n_layers * kLayerTensors);
-    for (size_t i = 0; i < m->lt.size(); ++i) m->lt[i] = {p->layers[i].type, where[wi++]};
+    for (size_t i = 0; i < m->lt.size(); ++i) m->lt[i] = {p->layers[i].type, where[wi++], p->layers[i].nbytes};
+    auto follows = [](const DevTensor& a, const DevTensor& b) {   // b continues matrix a
+        return a.type == b.type && static_cast<const char*>(a.d) + a.nbytes == static_cast<const char*>(b.d);
+    };
+    m->qkv_run.assign(p->n_layers, 1);
+    m->gu_fused.assign(p->n_layers, 0);
+    for (int L = 0; L < p->n_layers; ++L) {
+        const DevTensor* W = &m->lt[(size_t)L * kLayerTensors];
+        if (follows(W[R_Q], W[R_K])) m->qkv_run[L] = follows(W[R_K], W[R_V]) ? 3 : 2;
+        m->gu_fused[L] = follows(W[R_GATE], W[R_UP]);
+    }
 
     // Activations for max_tok rows.
     const size_t T = (size_t)m->max_tok;
     const size_t sizes[] = {T * HD * 4, T * HD * 4, T * qd * 4, T * kd * 4, T * kd * 4, T * qd * 4, T * HD * 4,
-                            T * ID * 4, T * ID * 4, (size_t)m->VS * 4, (size_t)m->VS * 4, T * 4, ((size_t)m->max_seq + 1) * 4, 256};
+                            2 * T * ID * 4, T * ID * 4, (size_t)m->VS * 4, (size_t)m->VS * 4, T * 4,
+                            ((size_t)m->max_seq + 1) * 4, 256, (size_t)(qd + 2 * kd) * 4};
     size_t total = 0;
     for (size_t s : sizes) total += align256(s);
     if (cudaMalloc(&m->act_blob, total) != cudaSuccess) { free_model(m); return PICKLE_ERR_MEMORY; }
     char* a = static_cast<char*>(m->act_blob);
     void** dst[] = {(void**)&m->x, (void**)&m->xn, (void**)&m->q, (void**)&m->k, (void**)&m->v, (void**)&m->ao,
                     (void**)&m->proj, (void**)&m->gate, (void**)&m->up, (void**)&m->logits, (void**)&m->logits2, (void**)&m->tok,
-                    (void**)&m->ids, (void**)&m->err};
+                    (void**)&m->ids, (void**)&m->err, (void**)&m->qkv1};
     for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); ++i) {
         *dst[i] = a;
         a += align256(sizes[i]);
     }
     if (cudaMemset(m->err, 0, sizeof(int)) != cudaSuccess) { free_model(m); return PICKLE_ERR_DEVICE; }
-    const int shapes[][2] = {{qd, HD}, {kd, HD}, {HD, qd}, {ID, HD}, {HD, ID}};
+    const int shapes[][2] = {{qd, HD}, {kd, HD}, {HD, qd}, {ID, HD}, {2 * ID, HD}, {HD, ID}};
     for (auto& s : shapes) {
         const size_t b = pickle_cuda_matmul_workspace(s[0], s[1], m->max_tok);
         if (b > m->ws_bytes) m->ws_bytes = b;

@@ -24,6 +24,7 @@
 
 #include "matvec_tc.cuh"
 #include "matmul_tc.cuh"
+#include "matvec_ex.h"
 
 namespace {
 
@@ -198,8 +199,12 @@ cudaError_t launch_type(const unsigned char* W, size_t row_bytes, int out_n, int
 
 }  // namespace
 
-extern "C" PICKLE_CUDA_API int pickle_cuda_matvec_dev(int type, const void* W, int out_n, int in_n, int n_vec,
-                                                      const float* x, float* y, void* stream) {
+// pickle_cuda_matvec_dev, and for the model's own projections (w_static:
+// W is never written while the model lives) the same with the weight
+// stream of the tensor-core kernel started before the previous kernel in
+// the stream has finished.
+int pcu_matvec_ex(int type, const void* W, int out_n, int in_n, int n_vec, const float* x, float* y, void* stream,
+                  bool w_static) {
     if (!W || !x || !y || out_n < 1 || in_n < 1 || n_vec < 1 || n_vec > PICKLE_CUDA_MATVEC_MAX_VEC)
         return PICKLE_ERR_ARG;
     if (((uintptr_t)W | (uintptr_t)x | (uintptr_t)y) % 16) return PICKLE_ERR_ARG;
@@ -222,31 +227,36 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_matvec_dev(int type, const void* W, i
         case T_F32: e = launch_type<T_F32>(w, row_bytes, out_n, in_n, n_vec, x, y, st); break;
         case T_F16:
             e = mvtc::tc_supported<T_F16>(w, row_bytes, in_n)
-                    ? mvtc::launch<T_F16>(w, row_bytes, out_n, in_n, n_vec, x, y, st)
+                    ? mvtc::launch<T_F16>(w, row_bytes, out_n, in_n, n_vec, x, y, st, w_static)
                     : launch_type<T_F16>(w, row_bytes, out_n, in_n, n_vec, x, y, st);
             break;
         case T_Q4_0:
             e = mvtc::tc_supported<T_Q4_0>(w, row_bytes, in_n)
-                    ? mvtc::launch<T_Q4_0>(w, row_bytes, out_n, in_n, n_vec, x, y, st)
+                    ? mvtc::launch<T_Q4_0>(w, row_bytes, out_n, in_n, n_vec, x, y, st, w_static)
                     : launch_type<T_Q4_0>(w, row_bytes, out_n, in_n, n_vec, x, y, st);
             break;
         case T_Q8_0:
             e = mvtc::tc_supported<T_Q8_0>(w, row_bytes, in_n)
-                    ? mvtc::launch<T_Q8_0>(w, row_bytes, out_n, in_n, n_vec, x, y, st)
+                    ? mvtc::launch<T_Q8_0>(w, row_bytes, out_n, in_n, n_vec, x, y, st, w_static)
                     : launch_type<T_Q8_0>(w, row_bytes, out_n, in_n, n_vec, x, y, st);
             break;
         case T_Q4_K:
             e = mvtc::tc_supported<T_Q4_K>(w, row_bytes, in_n)
-                    ? mvtc::launch<T_Q4_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st)
+                    ? mvtc::launch<T_Q4_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st, w_static)
                     : launch_type<T_Q4_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st);
             break;
         case T_Q6_K:
             e = mvtc::tc_supported<T_Q6_K>(w, row_bytes, in_n)
-                    ? mvtc::launch<T_Q6_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st)
+                    ? mvtc::launch<T_Q6_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st, w_static)
                     : launch_type<T_Q6_K>(w, row_bytes, out_n, in_n, n_vec, x, y, st);
             break;
     }
     return e == cudaSuccess ? PICKLE_OK : PICKLE_ERR_DEVICE;
+}
+
+extern "C" PICKLE_CUDA_API int pickle_cuda_matvec_dev(int type, const void* W, int out_n, int in_n, int n_vec,
+                                                      const float* x, float* y, void* stream) {
+    return pcu_matvec_ex(type, W, out_n, in_n, n_vec, x, y, stream, false);
 }
 
 extern "C" PICKLE_CUDA_API size_t pickle_cuda_matvec_row_bytes(int type, int in_n) {
@@ -278,9 +288,8 @@ extern "C" PICKLE_CUDA_API size_t pickle_cuda_matmul_workspace(int out_n, int in
     return mmtc::workspace_bytes(out_n, in_n, n_tok);
 }
 
-extern "C" PICKLE_CUDA_API int pickle_cuda_matmul_dev(int type, const void* W, int out_n, int in_n, int n_tok,
-                                                      const float* x, float* y, void* workspace, size_t ws_bytes,
-                                                      void* stream) {
+int pcu_matmul_ex(int type, const void* W, int out_n, int in_n, int n_tok, const float* x, float* y,
+                  void* workspace, size_t ws_bytes, void* stream, bool w_static) {
     if (!W || !x || !y || out_n < 1 || in_n < 1 || n_tok < 1) return PICKLE_ERR_ARG;
     if (((uintptr_t)W | (uintptr_t)x | (uintptr_t)y) % 16) return PICKLE_ERR_ARG;
     if (type != T_F32 && type != T_F16 && type != T_Q4_0 && type != T_Q8_0 && type != T_Q4_K && type != T_Q6_K)
@@ -305,9 +314,15 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_matmul_dev(int type, const void* W, i
     // Otherwise: the matvec, up to eight activation rows per pass over W.
     for (int v0 = 0; v0 < n_tok; v0 += PICKLE_CUDA_MATVEC_MAX_VEC) {
         const int nv = n_tok - v0 < PICKLE_CUDA_MATVEC_MAX_VEC ? n_tok - v0 : PICKLE_CUDA_MATVEC_MAX_VEC;
-        const int rc = pickle_cuda_matvec_dev(type, W, out_n, in_n, nv, x + (size_t)v0 * in_n,
-                                              y + (size_t)v0 * out_n, stream);
+        const int rc = pcu_matvec_ex(type, W, out_n, in_n, nv, x + (size_t)v0 * in_n, y + (size_t)v0 * out_n,
+                                     stream, w_static);
         if (rc != PICKLE_OK) return rc;
     }
     return PICKLE_OK;
+}
+
+extern "C" PICKLE_CUDA_API int pickle_cuda_matmul_dev(int type, const void* W, int out_n, int in_n, int n_tok,
+                                                      const float* x, float* y, void* workspace, size_t ws_bytes,
+                                                      void* stream) {
+    return pcu_matmul_ex(type, W, out_n, in_n, n_tok, x, y, workspace, ws_bytes, stream, false);
 }

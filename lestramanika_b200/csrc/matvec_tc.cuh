@@ -319,7 +319,7 @@ PCU_DEV void convert_x(const float* __restrict__ x, int in_n, uint8_t* smem, con
 template <int TYPE, int NV>
 __global__ void __launch_bounds__(Warps<TYPE, NV>::THREADS, 1)
     matvec_tc_kernel(const __grid_constant__ CUtensorMap tm, int out_n, int in_n, const float* __restrict__ x,
-                     float* __restrict__ y) {
+                     float* __restrict__ y, int w_early) {
     using F = Fmt<TYPE>;
     constexpr int CW = Warps<TYPE, NV>::CW, THREADS = Warps<TYPE, NV>::THREADS;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -360,15 +360,18 @@ __global__ void __launch_bounds__(Warps<TYPE, NV>::THREADS, 1)
         if (++p_slot == STAGES) p_slot = 0;
     };
     // Launched with programmatic stream serialization: let the next kernel
-    // be scheduled now, and read nothing in global memory before the
-    // previous one has completed.
+    // be scheduled now, and read nothing the previous kernel may write
+    // before it has completed. W is such memory unless the caller says it
+    // is constant (w_early): then the first stages of W are already on
+    // their way while the previous kernel finishes.
     griddep_launch_dependents();
-    griddep_wait();
+    if (!w_early) griddep_wait();
     if (warp == CW && lane == 0)
         for (int s = 0; s < min(STAGES, n_st); ++s) {
             issue(p_slot, p_k, p_j);
             p_next();
         }
+    if (w_early) griddep_wait();
     convert_x<TYPE, NV, THREADS>(x, in_n, smem, L);
     __syncthreads();
 
@@ -767,7 +770,8 @@ inline bool tc_supported(const void* W, size_t row_bytes, int in_n) {
 }
 
 template <int TYPE, int NV>
-inline cudaError_t launch_nv(const CUtensorMap& tm, int out_n, int in_n, const float* x, float* y, cudaStream_t st) {
+inline cudaError_t launch_nv(const CUtensorMap& tm, int out_n, int in_n, const float* x, float* y, cudaStream_t st,
+                             bool w_early) {
     const Smem L = smem_layout<TYPE>(in_n, NV, Warps<TYPE, NV>::CW);
     static bool attr_set[64] = {};
     static int sms[64] = {};
@@ -793,12 +797,12 @@ inline cudaError_t launch_nv(const CUtensorMap& tm, int out_n, int in_n, const f
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, matvec_tc_kernel<TYPE, NV>, tm, out_n, in_n, x, y);
+    return cudaLaunchKernelEx(&cfg, matvec_tc_kernel<TYPE, NV>, tm, out_n, in_n, x, y, (int)w_early);
 }
 
 template <int TYPE>
 inline cudaError_t launch(const uint8_t* W, size_t row_bytes, int out_n, int in_n, int n_vec, const float* x,
-                          float* y, cudaStream_t st) {
+                          float* y, cudaStream_t st, bool w_early = false) {
     alignas(64) CUtensorMap tm;
     if (make_w_map<TYPE>(&tm, W, row_bytes, out_n) != 0) return cudaErrorInvalidValue;
     // Vectors go in passes of as many as fit in shared memory.
@@ -809,14 +813,14 @@ inline cudaError_t launch(const uint8_t* W, size_t row_bytes, int out_n, int in_
         float* yv = y + (size_t)v0 * out_n;
         cudaError_t e = cudaSuccess;
         switch (nv) {
-            case 1: e = launch_nv<TYPE, 1>(tm, out_n, in_n, xv, yv, st); break;
-            case 2: e = launch_nv<TYPE, 2>(tm, out_n, in_n, xv, yv, st); break;
-            case 3: e = launch_nv<TYPE, 3>(tm, out_n, in_n, xv, yv, st); break;
-            case 4: e = launch_nv<TYPE, 4>(tm, out_n, in_n, xv, yv, st); break;
-            case 5: e = launch_nv<TYPE, 5>(tm, out_n, in_n, xv, yv, st); break;
-            case 6: e = launch_nv<TYPE, 6>(tm, out_n, in_n, xv, yv, st); break;
-            case 7: e = launch_nv<TYPE, 7>(tm, out_n, in_n, xv, yv, st); break;
-            default: e = launch_nv<TYPE, 8>(tm, out_n, in_n, xv, yv, st); break;
+            case 1: e = launch_nv<TYPE, 1>(tm, out_n, in_n, xv, yv, st, w_early); break;
+            case 2: e = launch_nv<TYPE, 2>(tm, out_n, in_n, xv, yv, st, w_early); break;
+            case 3: e = launch_nv<TYPE, 3>(tm, out_n, in_n, xv, yv, st, w_early); break;
+            case 4: e = launch_nv<TYPE, 4>(tm, out_n, in_n, xv, yv, st, w_early); break;
+            case 5: e = launch_nv<TYPE, 5>(tm, out_n, in_n, xv, yv, st, w_early); break;
+            case 6: e = launch_nv<TYPE, 6>(tm, out_n, in_n, xv, yv, st, w_early); break;
+            case 7: e = launch_nv<TYPE, 7>(tm, out_n, in_n, xv, yv, st, w_early); break;
+            default: e = launch_nv<TYPE, 8>(tm, out_n, in_n, xv, yv, st, w_early); break;
         }
         if (e != cudaSuccess) return e;
         v0 += nv;

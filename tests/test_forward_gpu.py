@@ -56,6 +56,20 @@ def test_generate_with_prompt_chunks(tiny_model, golden_e2e):
     m.close()
 
 
+def test_weights_on_device_unfused(tiny_model, golden_e2e):
+    """Weights given as separate device tensors (weights_on_device): no two
+    are back to back, so q, k, v and gate, up run as separate projections."""
+    from lestramanika_b200 import gguf
+    path, prompt = tiny_model
+    meta, t = gguf.read(path)
+    tensors = {n: (typ, torch.from_numpy(np.array(d)).to(DEV)) for n, (typ, dims, d) in t.items()}
+    m = PickleModel(tensors, gguf.arch_detect(meta, t), max_tokens=64)
+    ids, logits, pos = m.generate(prompt, 48)
+    m.close()
+    np.testing.assert_array_equal(ids, golden_e2e["ids"][:48])
+    assert pos == 16 + 48
+
+
 def test_forward_step_by_step(tiny, golden_e2e):
     """pickle_fast_forward's calling convention: the prompt, then one id at a time."""
     m, prompt = tiny
