@@ -832,6 +832,17 @@ def run_ours_single(args):
     except Exception as exc:  # reported, not hidden
         extras["prefill_layer"] = {"error": str(exc)[:200]}
     try:
+        fw = forward_line(device, max(min(args.steps, 5), 2), max(args.warmup, 2))
+        fw["decode_frac_of_measured_hbm"] = fw["decode_GBps"] / hbm
+        if not args.no_cpu_baseline:
+            fw["cpu_reference"] = forward_cpu()
+            if "decode_ms_per_token" in fw["cpu_reference"]:
+                fw["decode_speedup_vs_reference"] = (fw["cpu_reference"]["decode_ms_per_token"] /
+                                                     fw["decode_ms_per_token"])
+        extras["forward"] = fw
+    except Exception as exc:  # reported, not hidden
+        extras["forward"] = {"error": str(exc)[:200]}
+    try:
         from lestramanika_b200 import PREFILL_BF16
         pf = prefill_line(C3, device, max(5, min(args.steps, 10)), max(args.warmup, 3), PREFILL_BF16)
         pf["frac_of_measured_bf16"] = pf["TFLOPs"] / bf16

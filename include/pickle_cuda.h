@@ -5,6 +5,9 @@
  * host forward pass (lee-muriithi-kingori/lestramanika,
  * src/pickle_fast.c:1910-2109): RoPE (NeoX half-split) on q and k, the
  * KV-cache append, and causal softmax attention over positions [0, pos].
+ * Around it: the weight projections (pickle_fast_matmul_dispatch, per
+ * token and for whole prompts) and the whole forward pass with the greedy
+ * decode loop (pickle_cuda_model_*, at the end of this header).
  *
  * Everything here is plain C: pointers, sizes and int status codes.
  * Status codes are pickle's own (src/pickle.h:52-60) plus
