@@ -313,8 +313,9 @@ typedef struct {
     int   weights_on_device;  /* 0: data are host pointers, copied into one device allocation at load;
                                  1: data are 16-byte aligned device pointers used in place (the caller
                                  keeps them alive until pickle_cuda_model_free) */
-    pickle_cuda_tensor_t token_embd;   /* "token_embd.weight", F32 or F16 [vocab][hidden] (the reference
-                                          dequantizes other types to F32 at state init, :1551-1584) */
+    pickle_cuda_tensor_t token_embd;   /* "token_embd.weight" [vocab][hidden]: F32 or F16 rows are looked
+                                          up as they are; Q4_0, Q8_0, Q4_K, Q6_K are dequantized to an
+                                          F32 table at load, as pickle_fast_state_init does (:1551-1584) */
     pickle_cuda_tensor_t output_norm;  /* "output_norm.weight", F32 [hidden]; NULL = no final norm */
     pickle_cuda_tensor_t output;       /* "output.weight" [vocab][hidden]; NULL = token_embd (tied) */
     const pickle_cuda_tensor_t* layers; /* [n_layers][PICKLE_CUDA_LAYER_TENSORS] */
@@ -351,6 +352,16 @@ PICKLE_CUDA_API int  pickle_cuda_model_sync(pickle_cuda_model_t* m, void* stream
  * larger one finds it (so 0 when logits[0] is NaN, other NaNs never win).
  * logits [n] and out (one int32) are device buffers; asynchronous. */
 PICKLE_CUDA_API int  pickle_cuda_argmax_dev(const float* logits, int n, int32_t* out, void* stream);
+/* pickle_fast_sample_temp (src/pickle_fast.c:2204-2276) on the device, one
+ * CTA: temp <= 0 is the argmax; otherwise softmax(logits / temp) (logits is
+ * overwritten with the unnormalized exponentials, as the reference does),
+ * one xorshift32 draw from seed (0 -> 0x12345678), and top-p (nucleus)
+ * sampling when 0 < top_p < 1, else plain temperature sampling. The sums
+ * are fixed-order trees, not the reference's one running float sum: a draw
+ * within float rounding of a probability boundary may pick the neighbouring
+ * id. Ties in probability go to the lower index. Asynchronous. */
+PICKLE_CUDA_API int  pickle_cuda_sample_dev(float* logits, int n, float temp, float top_p, uint32_t seed,
+                                            int32_t* out, void* stream);
 /* Greedy generation as pickle_chat_loop runs it with temp <= 0: forward the
  * prompt, then n_gen times take the argmax id, stop after eos_id (>= 0;
  * -1 = none) or when the cache is full, else forward that id. The ids stay
@@ -360,6 +371,14 @@ PICKLE_CUDA_API int  pickle_cuda_argmax_dev(const float* logits, int n, int32_t*
 PICKLE_CUDA_API int  pickle_cuda_generate(pickle_cuda_model_t* m, const int32_t* prompt, size_t n_prompt,
                                           int n_gen, int eos_id, int32_t* out_ids, int* n_out,
                                           float* last_logits, size_t* kv_pos);
+/* The same loop with pickle_chat_loop's sampler: id i is
+ * pickle_fast_sample_temp(logits, vocab, temp, top_p, seed + i) (greedy when
+ * temp <= 0), run on the device (pickle_cuda_sample_dev). The sampler
+ * leaves the logits it sampled from as expf(logits / temp - max), as the
+ * reference's does. */
+PICKLE_CUDA_API int  pickle_cuda_generate_sampled(pickle_cuda_model_t* m, const int32_t* prompt, size_t n_prompt,
+                                                  int n_gen, int eos_id, float temp, float top_p, uint32_t seed,
+                                                  int32_t* out_ids, int* n_out, float* last_logits, size_t* kv_pos);
 
 /* ---- Peer exchange of the sharded decodes (one process per GPU) ----
  * No counterpart in the reference, which runs on one host: this replaces an

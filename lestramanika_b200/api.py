@@ -102,6 +102,9 @@ SIGNATURES = {
     "pickle_cuda_forward_dev": ([_vp, _vp, _sz, _sz, _vp, _vp, _vp], _i),
     "pickle_cuda_model_sync": ([_vp, _vp], _i),
     "pickle_cuda_argmax_dev": ([_vp, _i, _vp, _vp], _i),
+    "pickle_cuda_sample_dev": ([_vp, _i, ctypes.c_float, ctypes.c_float, ctypes.c_uint32, _vp, _vp], _i),
+    "pickle_cuda_generate_sampled": ([_vp, _i32p, _sz, _i, _i, ctypes.c_float, ctypes.c_float, ctypes.c_uint32,
+                                      _i32p, ctypes.POINTER(_i), _fp, ctypes.POINTER(_sz)], _i),
     "pickle_cuda_generate": ([_vp, _i32p, _sz, _i, _i, _i32p, ctypes.POINTER(_i), _fp, ctypes.POINTER(_sz)], _i),
     "pickle_cuda_xchg_create": ([_i, _i, _sz, _i, ctypes.POINTER(_vp)], _i),
     "pickle_cuda_xchg_handle": ([_vp, _vp], _i),
@@ -363,6 +366,15 @@ def argmax_dev(logits, out, stream=None):
     rc = lib().pickle_cuda_argmax_dev(_ptr(logits), logits.numel(), _ptr(out), _stream(stream))
     if rc != PICKLE_OK:
         raise PickleError(rc, "pickle_cuda_argmax_dev")
+
+
+def sample_dev(logits, out, temp, top_p=0.0, seed=0, stream=None):
+    """pickle_fast_sample_temp on a device f32 vector (overwritten with the
+    exponentials when temp > 0) into a device int32 (asynchronous)."""
+    rc = lib().pickle_cuda_sample_dev(_ptr(logits), logits.numel(), float(temp), float(top_p), int(seed) & 0xFFFFFFFF,
+                                      _ptr(out), _stream(stream))
+    if rc != PICKLE_OK:
+        raise PickleError(rc, "pickle_cuda_sample_dev")
 
 
 def abi_version():

@@ -192,6 +192,290 @@ __global__ void swiglu_kernel(const float* __restrict__ gate, long long up_off, 
     }
 }
 
+// ---- Sampling: pickle_fast_sample_temp (src/pickle_fast.c:2204-2276) ----
+// One CTA of kSampleThreads. The reference, for temp > 0:
+//   logits /= temp; e = expf(logits - max); sum = sum(e);  (0 if sum == 0)
+//   r = (xorshift32(seed) & 0xFFFFFF) / (float)0xFFFFFF
+//   0 < top_p < 1: the fewest largest p = e / sum whose running sum cum
+//     reaches top_p (a selection sort), then the first of them, largest
+//     first, at which the running sum reaches r * cum (else the largest);
+//   otherwise the first index at which the running sum of p reaches r
+//     (else n - 1).
+// Here the sums are fixed-order trees instead of one running float sum, so
+// a draw within float rounding of a boundary may pick the neighbour; the
+// nucleus is found without sorting, by binary searches over the bit
+// patterns of e (non-negative floats order like their bits); among equal
+// values the lower index comes first. logits are left holding e, as the
+// reference leaves them.
+constexpr int kSampleThreads = 1024;
+
+template <int NT>
+__device__ float block_sum_n(float v, float* part) {
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) part[w] = v;
+    __syncthreads();
+    float t = l < NT / 32 ? part[l] : 0.0f;
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    return t;
+}
+
+template <int NT>
+__device__ float block_max_n(float v, float* part) {
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) part[w] = v;
+    __syncthreads();
+    float t = l < NT / 32 ? part[l] : -INFINITY;
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, o));
+    return t;
+}
+
+template <int NT>
+__device__ int block_min_i(int v, int* part) {
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) part[w] = v;
+    __syncthreads();
+    int t = l < NT / 32 ? part[l] : INT32_MAX;
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t = min(t, __shfl_xor_sync(0xffffffffu, t, o));
+    return t;
+}
+
+// Exclusive scan in thread order (one value per thread); every thread gets its prefix.
+template <int NT, typename T>
+__device__ T block_excl_scan(T v, T* part) {
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    T inc = v;
+    #pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const T t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (l >= o) inc += t;
+    }
+    __syncthreads();
+    if (l == 31) part[w] = inc;
+    __syncthreads();
+    T base = 0;
+    for (int j = 0; j < w; ++j) base += part[j];
+    return base + inc - v;
+}
+
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(float* __restrict__ lg, int n, float temp,
+                                                                float top_p, uint32_t seed, int32_t* __restrict__ out) {
+    griddep_launch_dependents();
+    griddep_wait();
+    constexpr int NT = kSampleThreads;
+    __shared__ float fpart[NT / 32];
+    __shared__ int ipart[NT / 32];
+    const int tid = threadIdx.x;
+    float mx = -INFINITY;
+    for (int i = tid; i < n; i += NT) {
+        const float l = lg[i] / temp;
+        lg[i] = l;
+        mx = fmaxf(mx, l);
+    }
+    mx = block_max_n<NT>(mx, fpart);
+    float s = 0.0f;
+    for (int i = tid; i < n; i += NT) {
+        const float e = expf(lg[i] - mx);
+        lg[i] = e;
+        s += e;
+    }
+    const float sum = block_sum_n<NT>(s, fpart);
+    uint32_t x = seed ? seed : 0x12345678u;   // g_rng_state, then one xorshift32 step
+    x ^= x << 13;
+    x ^= x >> 17;
+    x ^= x << 5;
+    const float r = (float)(x & 0xFFFFFFu) / (float)0xFFFFFF;
+    if (sum == 0.0f) {
+        if (tid == 0) *out = 0;
+        return;
+    }
+    // Each thread's contiguous run of indices, for the scans in index order.
+    const int C = (n + NT - 1) / NT;
+    const int i0 = min(n, tid * C), i1 = min(n, i0 + C);
+    if (top_p > 0.0f && top_p < 1.0f) {
+        // sum of p over the elements whose e has bits >= b
+        auto sum_ge = [&](uint32_t b) {
+            float a = 0.0f;
+            for (int i = tid; i < n; i += NT) {
+                const float e = lg[i];
+                if (__float_as_uint(e) >= b) a += e / sum;
+            }
+            return block_sum_n<NT>(a, fpart);
+        };
+        auto count_eq = [&](uint32_t b) {
+            float c = 0.0f;
+            for (int i = tid; i < n; i += NT) c += __float_as_uint(lg[i]) == b ? 1.0f : 0.0f;
+            return (int)block_sum_n<NT>(c, fpart);
+        };
+        // Largest bits b with sum_ge(b) >= v (lo0 when none qualifies); at most 31 steps.
+        auto search = [&](uint32_t lo0, float v) {
+            uint32_t lo = lo0, hi = 0x3F800001u;            // e <= 1 = expf(0)
+            while (hi - lo > 1) {
+                const uint32_t mid = lo + (hi - lo) / 2;
+                if (sum_ge(mid) >= v) lo = mid; else hi = mid;
+            }
+            return lo;
+        };
+        // The nucleus: every e above bk, then equal ones until cum >= top_p.
+        const uint32_t bk = search(0u, top_p);
+        const float pk = __uint_as_float(bk) / sum;
+        float cum = sum_ge(bk + 1);
+        const int eq_k = count_eq(bk);
+        int take_k = 0;
+        while (take_k < eq_k && cum < top_p) {
+            cum += pk;
+            ++take_k;
+        }
+        if (take_k == 0) take_k = eq_k;   // nothing reaches top_p: all of them
+        const float R = r * cum;
+        // The chosen value: largest bits bc >= bk with sum_ge(bc) >= R; then
+        // the m-th equal element (by index) at which the running sum gets there.
+        const uint32_t bc = search(bk, R);
+        const float pc = __uint_as_float(bc) / sum;
+        float acc = sum_ge(bc + 1);
+        const int eq_c = bc == bk ? take_k : count_eq(bc);
+        int m = 0;
+        while (m < eq_c && acc < R) {
+            acc += pc;
+            ++m;
+        }
+        int chosen = INT32_MAX;
+        if (acc >= R && m >= 1) {
+            // the m-th element in index order whose e has bits bc
+            int own = 0;
+            for (int i = i0; i < i1; ++i) own += __float_as_uint(lg[i]) == bc;
+            const int before = block_excl_scan<NT, int>(own, ipart);
+            int hit = INT32_MAX;
+            if (before < m && m <= before + own) {
+                int c = before;
+                for (int i = i0; i < i1; ++i)
+                    if (__float_as_uint(lg[i]) == bc && ++c == m) {
+                        hit = i;
+                        break;
+                    }
+            }
+            chosen = block_min_i<NT>(hit, ipart);
+        } else {
+            // no element reached R: the reference keeps idx[0], the largest e
+            // (e = expf(0) = 1), the lowest index among equal largest ones
+            int best = INT32_MAX;
+            for (int i = tid; i < n; i += NT)
+                if (lg[i] == 1.0f && i < best) best = i;
+            chosen = block_min_i<NT>(best, ipart);
+        }
+        if (tid == 0) *out = chosen == INT32_MAX ? 0 : chosen;
+        return;
+    }
+    // Plain temperature sampling: the first index whose running sum of p
+    // reaches r; the runs' sums are scanned across the CTA in index order.
+    float own = 0.0f;
+    for (int i = i0; i < i1; ++i) own += lg[i] / sum;
+    float acc = block_excl_scan<NT, float>(own, fpart);
+    int hit = INT32_MAX;
+    for (int i = i0; i < i1; ++i) {
+        acc += lg[i] / sum;
+        if (acc >= r) {
+            hit = i;
+            break;
+        }
+    }
+    hit = block_min_i<NT>(hit, ipart);
+    if (tid == 0) *out = hit == INT32_MAX ? n - 1 : hit;
+}
+
+// Token embeddings of a quantized type become an F32 table at load, as
+// pickle_fast_state_init does with pickle_dequant_stream
+// (src/pickle_fast.c:1551-1584, src/pickle.c:661-870), with that
+// function's expressions, each product and difference rounded once:
+//   Q8_0  d * q                  Q4_0  d * (q - 8)
+//   Q6_K  d * (sc * q)           Q4_K  (d * sc) * q - dmin * m
+// One thread per 32-element block (Q8_0, Q4_0), one warp per 256-element
+// block (Q4_K, Q6_K: lane l writes elements l, l + 32, ... of the block).
+__device__ __forceinline__ float h2f(const unsigned char* p) {
+    return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+}
+
+__global__ void dequant32_kernel(const unsigned char* __restrict__ w, int type, size_t n_blocks, float* __restrict__ out) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x; b < n_blocks; b += stride) {
+        float* o = out + b * 32;
+        if (type == T_Q8_0) {
+            const unsigned char* blk = w + b * 34;
+            const float d = h2f(blk);
+            for (int i = 0; i < 32; ++i) o[i] = __fmul_rn(d, (float)(int)(signed char)blk[2 + i]);
+        } else {
+            const unsigned char* blk = w + b * 18;
+            const float d = h2f(blk);
+            for (int i = 0; i < 16; ++i) {
+                o[i] = __fmul_rn(d, (float)((blk[2 + i] & 0x0F) - 8));
+                o[16 + i] = __fmul_rn(d, (float)((blk[2 + i] >> 4) - 8));
+            }
+        }
+    }
+}
+
+__global__ void dequant256_kernel(const unsigned char* __restrict__ w, int type, size_t n_blocks,
+                                  float* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const size_t warps = (size_t)gridDim.x * (blockDim.x >> 5);
+    for (size_t b = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < n_blocks; b += warps) {
+        float* o = out + b * 256;
+        if (type == T_Q4_K) {
+            // d, dmin, scales[12], qs[128]; element 64c + l (l < 32) is the low
+            // nibble of qs[32c + l] with sub-block 2c, 64c + 32 + l the high
+            // nibble with sub-block 2c + 1.
+            const unsigned char* blk = w + b * 144;
+            const float d = h2f(blk), dmin = h2f(blk + 2);
+            const unsigned char* sc = blk + 4;
+            const unsigned char* qs = blk + 16;
+            for (int c = 0; c < 4; ++c) {
+                for (int half = 0; half < 2; ++half) {
+                    const int j = 2 * c + half;
+                    int s, m;
+                    if (j < 4) {
+                        s = sc[j] & 63;
+                        m = sc[j + 4] & 63;
+                    } else {
+                        s = (sc[j + 4] & 0x0F) | ((sc[j - 4] >> 6) << 4);
+                        m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+                    }
+                    const float d1 = __fmul_rn(d, (float)s), m1 = __fmul_rn(dmin, (float)m);
+                    const int q = half ? qs[32 * c + lane] >> 4 : qs[32 * c + lane] & 0x0F;
+                    o[64 * c + 32 * half + lane] = __fsub_rn(__fmul_rn(d1, (float)q), m1);
+                }
+            }
+        } else {
+            // ql[128], qh[64], int8 scales[16], d; element 128n + 32u + l is
+            // (ql nibble | 2 bits of qh) - 32, times scales[(128n + 32u + l) / 16].
+            const unsigned char* blk = w + b * 210;
+            const unsigned char* ql = blk;
+            const unsigned char* qh = blk + 128;
+            const signed char* scales = reinterpret_cast<const signed char*>(blk + 192);
+            const float d = h2f(blk + 208);
+            for (int n = 0; n < 2; ++n) {
+                for (int u = 0; u < 4; ++u) {
+                    const unsigned char lb = ql[64 * n + lane + 32 * (u & 1)];
+                    const int lo = u < 2 ? (lb & 0x0F) : (lb >> 4);
+                    const int q = (lo | (((qh[32 * n + lane] >> (2 * u)) & 3) << 4)) - 32;
+                    const int i = 128 * n + 32 * u + lane;
+                    o[i] = __fmul_rn(d, (float)((int)scales[i / 16] * q));
+                }
+            }
+        }
+    }
+}
+
 // Launch with programmatic stream serialization: the kernel may be
 // scheduled before the previous one in the stream ends, and waits for it
 // with griddepcontrol.wait before it reads anything.
@@ -312,6 +596,7 @@ struct pickle_cuda_model {
     float eps = 0;
     pickle_cuda_t* attn = nullptr;
     void* blob = nullptr;            // the uploaded weights (null: caller-owned device pointers)
+    float* embd_f32 = nullptr;       // a quantized token_embd, dequantized at load
     DevTensor embd, out_norm, out;   // out.d == embd.d when tied
     std::vector<DevTensor> lt;       // [NL][9]
     // Per layer: how many of q, k, v (1..3) form one matrix (same type, rows
@@ -346,11 +631,23 @@ int mm(pickle_cuda_model* m, const DevTensor& w, const float* x, float* y, int o
     return pcu_matmul_ex(w.type, w.d, out_n, in_n, T, x, y, m->ws, m->ws_bytes, st, true);
 }
 
+// How the next id is taken from the last row's logits: pickle_fast_argmax
+// when temp <= 0, else pickle_fast_sample_temp with (temp, top_p, seed).
+struct Pick {
+    float temp = 0.0f, top_p = 0.0f;
+    uint32_t seed = 0;
+};
+
+cudaError_t launch_pick(const Pick& pk, float* logits, int n, int32_t* out, cudaStream_t st) {
+    if (!(pk.temp > 0.0f)) return launch_pdl(argmax_kernel, 1, kArgmaxThreads, st, (const float*)logits, n, out);
+    return launch_pdl(sample_kernel, 1, kSampleThreads, st, logits, n, pk.temp, pk.top_p, pk.seed, out);
+}
+
 // T tokens (device ids at tok_dev) at positions [pos0, pos0 + T), T <= max_tok,
 // all layers; when with_logits, the last row's logits go to logits_dev and
 // its argmax to next_dev (when non-null). Asynchronous on st.
 int run_chunk(pickle_cuda_model* m, const int32_t* tok_dev, int T, size_t pos0, bool with_logits, float* logits_dev,
-              int32_t* next_dev, cudaStream_t st) {
+              int32_t* next_dev, cudaStream_t st, const Pick& pk = Pick()) {
     const int HD = m->HD, ID = m->ID, qd = m->H * m->D, kd = m->HK * m->D;
     const DevTensor* L0 = &m->lt[0];
     if (launch_embed_rmsnorm(T, tok_dev, m->embd.d, m->embd.type == T_F16, m->VS,
@@ -420,9 +717,8 @@ int run_chunk(pickle_cuda_model* m, const int32_t* tok_dev, int T, size_t pos0, 
         return fail(m, PICKLE_ERR_DEVICE, "norm launch failed");
     if ((rc = mm(m, m->out, m->xn + last, logits_dev, m->VS, HD, 1, st)) != PICKLE_OK)
         return fail(m, rc, "output projection (lm_head)");
-    if (next_dev && launch_pdl(argmax_kernel, 1, kArgmaxThreads, st, (const float*)logits_dev, m->VS, next_dev) !=
-                        cudaSuccess)
-        return fail(m, PICKLE_ERR_DEVICE, "argmax launch failed");
+    if (next_dev && launch_pick(pk, logits_dev, m->VS, next_dev, st) != cudaSuccess)
+        return fail(m, PICKLE_ERR_DEVICE, "argmax / sampler launch failed");
     return PICKLE_OK;
 }
 
@@ -464,6 +760,7 @@ void free_model(pickle_cuda_model* m) {
     cudaSetDevice(m->device);
     if (m->attn) pickle_cuda_free(m->attn);
     cudaFree(m->blob);
+    cudaFree(m->embd_f32);
     cudaFree(m->act_blob);
     cudaFree(m->ws);
     if (m->ids_host) cudaFreeHost(m->ids_host);
@@ -510,8 +807,12 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_model_load(const pickle_cuda_model_pa
     // Shapes and types, as pickle_fast_state_init finds them (src/pickle_fast.c:1530-1633).
     const pickle_cuda_tensor_t& E = p->token_embd;
     if (!E.data) return PICKLE_ERR_ARCH;
-    if (E.type != T_F32 && E.type != T_F16) return PICKLE_ERR_TYPE;
-    if (E.nbytes != (size_t)p->vocab_size * HD * (E.type == T_F32 ? 4 : 2)) return PICKLE_ERR_ARG;
+    if (E.type != T_F32 && E.type != T_F16 && E.type != T_Q4_0 && E.type != T_Q8_0 && E.type != T_Q4_K &&
+        E.type != T_Q6_K)
+        return PICKLE_ERR_TYPE;
+    const bool e_quant = E.type != T_F32 && E.type != T_F16;
+    if (row_bytes_of(E.type, HD) == 0 || E.nbytes != (size_t)p->vocab_size * row_bytes_of(E.type, HD))
+        return PICKLE_ERR_ARG;
     int rc;
     if (p->output_norm.data && (rc = check_vector(p->output_norm, HD, on_dev)) != PICKLE_OK) return rc;
     if (p->output.data && (rc = check_matrix(p->output, p->vocab_size, HD, on_dev)) != PICKLE_OK) return rc;
@@ -550,7 +851,7 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_model_load(const pickle_cuda_model_pa
     // multiple of 16 bytes): such a run is one [rows][in] matrix, and a
     // decode step projects it in one launch.
     std::vector<const pickle_cuda_tensor_t*> all;
-    all.push_back(&p->token_embd);
+    if (!e_quant) all.push_back(&p->token_embd);
     if (p->output_norm.data) all.push_back(&p->output_norm);
     if (p->output.data) all.push_back(&p->output);
     const size_t lbase = all.size();
@@ -583,7 +884,32 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_model_load(const pickle_cuda_model_pa
         }
     }
     size_t wi = 0;
-    m->embd = {E.type, where[wi++], E.nbytes};
+    if (!e_quant) {
+        m->embd = {E.type, where[wi++], E.nbytes};
+    } else {
+        // The F32 table the reference builds at state init; the raw bytes
+        // are only needed until it is built.
+        const void* raw = E.data;
+        void* tmp = nullptr;
+        const size_t n_el = (size_t)p->vocab_size * HD;
+        bool ok = cudaMalloc((void**)&m->embd_f32, n_el * 4) == cudaSuccess;
+        if (ok && !on_dev) {
+            ok = cudaMalloc(&tmp, E.nbytes) == cudaSuccess &&
+                 cudaMemcpy(tmp, E.data, E.nbytes, cudaMemcpyHostToDevice) == cudaSuccess;
+            raw = tmp;
+        }
+        if (ok) {
+            const unsigned char* w = static_cast<const unsigned char*>(raw);
+            if (E.type == T_Q8_0 || E.type == T_Q4_0)
+                dequant32_kernel<<<148 * 8, 256>>>(w, E.type, n_el / 32, m->embd_f32);
+            else
+                dequant256_kernel<<<148 * 8, 256>>>(w, E.type, n_el / 256, m->embd_f32);
+            ok = cudaGetLastError() == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+        }
+        cudaFree(tmp);
+        if (!ok) { free_model(m); return PICKLE_ERR_DEVICE; }
+        m->embd = {T_F32, m->embd_f32, n_el * 4};
+    }
     m->out_norm = p->output_norm.data ? DevTensor{T_F32, where[wi++], p->output_norm.nbytes} : DevTensor{};
     // A model without output.weight (or with tied embeddings) projects with
     // token_embd (src/pickle_fast.c:2142-2166).
@@ -696,9 +1022,10 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_model_sync(pickle_cuda_model_t* m, vo
     return finish(m, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" PICKLE_CUDA_API int pickle_cuda_generate(pickle_cuda_model_t* m, const int32_t* prompt, size_t n_prompt,
-                                                    int n_gen, int eos_id, int32_t* out_ids, int* n_out,
-                                                    float* last_logits, size_t* kv_pos) {
+extern "C" PICKLE_CUDA_API int pickle_cuda_generate_sampled(pickle_cuda_model_t* m, const int32_t* prompt,
+                                                            size_t n_prompt, int n_gen, int eos_id, float temp,
+                                                            float top_p, uint32_t seed, int32_t* out_ids, int* n_out,
+                                                            float* last_logits, size_t* kv_pos) {
     if (!m || !prompt || n_prompt == 0 || n_gen < 0 || (n_gen > 0 && !out_ids) || !n_out || !kv_pos)
         return PICKLE_ERR_ARG;
     *n_out = 0;
@@ -714,14 +1041,19 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_generate(pickle_cuda_model_t* m, cons
         if (cudaMemcpyAsync(m->tok, prompt + c0, T * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
             return fail(m, PICKLE_ERR_DEVICE, "token upload failed");
         const bool last = c0 + T == n_prompt;
-        const int rc = run_chunk(m, m->tok, (int)T, pos + c0, last, m->logits, m->ids, st);
+        Pick pk;
+        pk.temp = temp;
+        pk.top_p = top_p;
+        pk.seed = seed;                         // the chat loop's seed + i, i = 0
+        const int rc = run_chunk(m, m->tok, (int)T, pos + c0, last, m->logits, m->ids, st, pk);
         if (rc != PICKLE_OK) return rc;
         if (!last && cudaStreamSynchronize(st) != cudaSuccess)   // m->tok is reused by the next chunk
             return fail(m, PICKLE_ERR_DEVICE, "stream synchronize failed");
     }
     pos += n_prompt;
-    // The greedy decode loop of pickle_chat_loop (src/pickle_host.c:489-521):
-    // id i is the argmax of the current logits; the loop stops after an id
+    // The decode loop of pickle_chat_loop (src/pickle_host.c:489-521): id i
+    // is the argmax of the current logits (temp <= 0) or their sample with
+    // seed + i; the loop stops after an id
     // equal to eos_id, or when the cache is full, and otherwise forwards id i
     // at the next position, whose argmax is id i + 1. The ids stay on the
     // device (ids[i] feeds the next embedding lookup). Without an eos_id the
@@ -740,7 +1072,11 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_generate(pickle_cuda_model_t* m, cons
         const bool full = pos >= (size_t)m->max_seq;
         const int nxt = eos ? cur ^ 1 : cur;
         if (!full) {
-            const int rc = run_chunk(m, m->ids + i, 1, pos, true, lbuf[nxt], m->ids + i + 1, st);
+            Pick pk;
+            pk.temp = temp;
+            pk.top_p = top_p;
+            pk.seed = seed + (uint32_t)(i + 1);
+            const int rc = run_chunk(m, m->ids + i, 1, pos, true, lbuf[nxt], m->ids + i + 1, st, pk);
             if (rc != PICKLE_OK) return rc;
         }
         done = i + 1;
@@ -762,4 +1098,22 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_generate(pickle_cuda_model_t* m, cons
     *n_out = done;
     *kv_pos = pos;
     return PICKLE_OK;
+}
+
+extern "C" PICKLE_CUDA_API int pickle_cuda_generate(pickle_cuda_model_t* m, const int32_t* prompt, size_t n_prompt,
+                                                    int n_gen, int eos_id, int32_t* out_ids, int* n_out,
+                                                    float* last_logits, size_t* kv_pos) {
+    return pickle_cuda_generate_sampled(m, prompt, n_prompt, n_gen, eos_id, 0.0f, 0.0f, 0u, out_ids, n_out,
+                                        last_logits, kv_pos);
+}
+
+extern "C" PICKLE_CUDA_API int pickle_cuda_sample_dev(float* logits, int n, float temp, float top_p, uint32_t seed,
+                                                      int32_t* out, void* stream) {
+    if (!logits || !out || n < 1) return PICKLE_ERR_ARG;
+    Pick pk;
+    pk.temp = temp;
+    pk.top_p = top_p;
+    pk.seed = seed;
+    return launch_pick(pk, logits, n, out, static_cast<cudaStream_t>(stream)) == cudaSuccess ? PICKLE_OK
+                                                                                              : PICKLE_ERR_DEVICE;
 }

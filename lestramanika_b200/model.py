@@ -6,9 +6,8 @@ src/pickle_fast.c:1497-1662, 1822-2184; src/pickle_host.c:473-521) over the
 C ABI's pickle_cuda_model_* entry points. Tensors are found by the names the
 reference looks up (src/pickle_fast.c:1530-1633); missing ones raise
 PICKLE_ERR_ARCH like the reference. Every weight goes to the device in its
-raw GGML blocks. The token embedding must be F32 or F16: the reference
-dequantizes any other type to F32 at state init (:1551-1584), which this
-loader does not do (PICKLE_ERR_TYPE).
+raw GGML blocks; a quantized token embedding becomes an F32 table on the
+device at load, as pickle_fast_state_init makes one (:1551-1584).
 """
 import ctypes
 
@@ -127,15 +126,17 @@ class PickleModel:
     def sync(self, stream=None):
         self._check(api.lib().pickle_cuda_model_sync(self._h, api._stream(stream)), "pickle_cuda_model_sync")
 
-    def generate(self, prompt, n_gen, eos_id=-1, kv_pos=0, want_logits=True):
-        """Greedy decode as pickle_chat_loop with temp <= 0 -> (ids, last logits, kv_pos)."""
+    def generate(self, prompt, n_gen, eos_id=-1, kv_pos=0, want_logits=True, temp=0.0, top_p=0.0, seed=0):
+        """The decode loop of pickle_chat_loop -> (ids, last logits, kv_pos):
+        greedy when temp <= 0, else pickle_fast_sample_temp with seed + i."""
         tok = np.ascontiguousarray(prompt, np.int32)
         ids = np.zeros(max(n_gen, 1), np.int32)
         n_out = ctypes.c_int(0)
         logits = np.empty(self.VS, np.float32) if want_logits else None
         pos = ctypes.c_size_t(int(kv_pos))
-        self._check(api.lib().pickle_cuda_generate(
-            self._h, tok.ctypes.data_as(api._i32p), tok.size, int(n_gen), int(eos_id),
-            ids.ctypes.data_as(api._i32p), ctypes.byref(n_out),
-            logits.ctypes.data_as(api._fp) if logits is not None else None, ctypes.byref(pos)), "pickle_cuda_generate")
+        self._check(api.lib().pickle_cuda_generate_sampled(
+            self._h, tok.ctypes.data_as(api._i32p), tok.size, int(n_gen), int(eos_id), float(temp), float(top_p),
+            int(seed) & 0xFFFFFFFF, ids.ctypes.data_as(api._i32p), ctypes.byref(n_out),
+            logits.ctypes.data_as(api._fp) if logits is not None else None, ctypes.byref(pos)),
+            "pickle_cuda_generate_sampled")
         return ids[:n_out.value].copy(), logits, pos.value

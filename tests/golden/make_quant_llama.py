@@ -52,11 +52,14 @@ def weight_bytes(t, out_n, in_n, rng):
     return b.tobytes()
 
 
-def write_model(path, mix="q4_k_m", seed=0, shape=None, tied=False, output_norm=True):
+def write_model(path, mix="q4_k_m", seed=0, shape=None, tied=False, output_norm=True, embd=None):
     """tied: no output.weight (the lm_head is token_embd, which the reference
-    then reads as F32); output_norm=False: no output_norm.weight."""
+    then reads as F32); output_norm=False: no output_norm.weight; embd: the
+    GGML type of token_embd instead of the mix's."""
     s = dict(SHAPE, **(shape or {}))
-    m = MIXES[mix]
+    m = dict(MIXES[mix])
+    if embd is not None:
+        m["embd"] = embd
     rng = np.random.Generator(np.random.Philox(1000 + seed))
     H, HK, D, HD, ID, VS = s["n_heads"], s["n_kv_heads"], s["head_dim"], s["hidden"], s["ffn"], s["vocab"]
     norm = lambda: (1.0 + 0.1 * rng.standard_normal(HD)).astype(np.float32).tobytes()  # noqa: E731

@@ -8,7 +8,8 @@ against the reference's own forward.
   step-by-step pickle_cuda_forward calls, and with the prompt split into
   chunks.
 * Small Llamas with quantized projections (tests/golden/make_quant_llama.py:
-  a Q4_K_M-like mix, Q8_0, Q4_0, F16; tied embeddings; no final norm): the
+  a Q4_K_M-like mix, Q8_0, Q4_0, F16; tied embeddings; no final norm;
+  quantized token embeddings, tied and untied): the
   reference's own forward (oracle/_ref/pickle_e2e_ref, the unmodified
   src/pickle_fast.c) run on the same GGUF file.
 
@@ -176,12 +177,16 @@ def quant_dir(tmp_path_factory):
 
 
 @pytest.mark.parametrize("mix,opts", [("q4_k_m", {}), ("q8_0", {}), ("q4_0", {}), ("f16", {}),
-                                      ("q8_0", {"tied": True}), ("q4_k_m", {"output_norm": False})])
+                                      ("q8_0", {"tied": True}), ("q4_k_m", {"output_norm": False}),
+                                      # quantized token_embd: an F32 table at load, as the reference's state init
+                                      ("q4_k_m", {"embd": mq.Q6_K}), ("q4_k_m", {"embd": mq.Q4_K}),
+                                      ("q8_0", {"tied": True, "embd": mq.Q8_0}),
+                                      ("q4_0", {"tied": True, "embd": mq.Q4_0})])
 def test_quantized_models_match_reference(quant_dir, mix, opts):
     exe = oracle.e2e_binary("ref")
     if not os.path.exists(exe):
         pytest.fail(f"{exe} is not built (python -m lestramanika_b200.build --all)")
-    tag = mix + "".join(f"_{k}" for k in opts)
+    tag = mix + "".join(f"_{k}{v}" for k, v in opts.items())
     path = str(quant_dir / f"{tag}.gguf")
     prompt = mq.write_model(path, mix, **opts)
     ref = oracle.e2e_run("ref", path, str(quant_dir / f"{tag}.bin"), 48, prompt)
