@@ -684,6 +684,45 @@ def forward_decode_line(device, steps, warmup):
             "tokens_per_s": 1e3 / ms, "weight_bytes": wbytes}
 
 
+def forward_batch_line(device, steps, warmup, batches=(8, 32)):
+    """Continuous-batching decode through the whole model (Llama-3-8B shape,
+    Q4_K_M-like weights): one step decodes B sequences, each in its own
+    cache slot at context 2048+ (the slots hold zeros: a step reads the same
+    bytes whatever they hold), all B rows sharing each pass over the weights
+    (pickle_cuda_forward_batch_dev with argmax ids). Tokens/s = B / step."""
+    torch = _torch()
+    from lestramanika_b200.model import PickleModel
+    c = FW_SHAPE
+    dev = torch.device("cuda", device)
+    tensors, arch, wbytes = _fw_model(device, c)
+    out = {"workload": "llama3-8b batched decode at context %d, Q4_K_M-like weights, B sequences per step"
+                       % c["prompt"], "batches": {}}
+    for B in batches:
+        m = PickleModel(tensors, arch, device=device, max_tokens=16, n_seqs=B)
+        logits = torch.empty((B, c["vocab"]), device=dev)
+        nxt = torch.full((B,), 7, dtype=torch.int32, device=dev)
+        slots = torch.arange(B, dtype=torch.int32, device=dev)
+        st = torch.cuda.Stream(device=dev)
+        P = c["prompt"]
+        pos = [torch.full((B,), P + i, dtype=torch.int32, device=dev) for i in range(warmup + steps)]
+        torch.cuda.synchronize()
+        for i in range(warmup):
+            m.forward_batch_dev(nxt, pos[i], slots, P + i, logits, nxt, stream=st)
+        m.sync(stream=st)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for i in range(warmup, warmup + steps):
+            m.forward_batch_dev(nxt, pos[i], slots, P + i, logits, nxt, stream=st)
+        e1.record(st)
+        m.sync(stream=st)
+        ms = e0.elapsed_time(e1) / steps
+        m.close()
+        kv = 2 * c["n_layers"] * c["HK"] * c["D"] * 4 * (P + warmup + steps / 2) * B
+        out["batches"][str(B)] = {"ms_per_step": round(ms, 4), "tokens_per_s": B / (ms * 1e-3),
+                                  "GBps": (wbytes + kv) / (ms * 1e-3) / 1e9}
+    return out
+
+
 def forward_cpu(seconds=8.0):
     """The reference's own per-token cost of the same forward on the host
     cores: its matvec kernels (oracle/_ref) for every projection shape and
@@ -843,6 +882,13 @@ def run_ours_single(args):
     except Exception as exc:  # reported, not hidden
         extras["forward"] = {"error": str(exc)[:200]}
     try:
+        fb = forward_batch_line(device, max(min(args.steps, 10), 3), max(args.warmup, 2))
+        for r in fb["batches"].values():
+            r["frac_of_measured_hbm"] = r["GBps"] / hbm
+        extras["forward_batch"] = fb
+    except Exception as exc:  # reported, not hidden
+        extras["forward_batch"] = {"error": str(exc)[:200]}
+    try:
         from lestramanika_b200 import PREFILL_BF16
         pf = prefill_line(C3, device, max(5, min(args.steps, 10)), max(args.warmup, 3), PREFILL_BF16)
         pf["frac_of_measured_bf16"] = pf["TFLOPs"] / bf16
@@ -924,7 +970,8 @@ def run_ours_multi(args, rank, world, local_rank):
 C4_SMALL = Decode("llama3-70b decode B=2 ctx=32768 (profiling size)", 2, 64, 8, 128, 32768, 500000.0)
 ONLY = {"c2b1": (C2_B1, True), "c2b8": (C2_B8, False), "c2b64": (C2_B64, False), "c4": (C4, False),
         "c4s": (C4_SMALL, False), "c5": (C5, False), "c3": (C3, None), "mv": (None, None), "mm": (None, None),
-        "pl": (None, None), "fw": (None, None), "fwd": (None, None)}
+        "pl": (None, None), "fw": (None, None), "fwd": (None, None), "fwb": (None, None),
+        "fwb32": (None, None)}
 
 
 def run_only(args):
@@ -948,6 +995,10 @@ def run_only(args):
             line["decode_speedup_vs_reference"] = ref["decode_ms_per_token"] / line["decode_ms_per_token"]
     elif args.only == "fwd":
         line = forward_decode_line(0, args.steps, args.warmup)
+    elif args.only == "fwb":
+        line = forward_batch_line(0, args.steps, args.warmup)
+    elif args.only == "fwb32":
+        line = forward_batch_line(0, args.steps, args.warmup, batches=(32,))
     elif args.only == "mm":
         line = matmul_line(0, args.steps, args.warmup)
         line["cpu_reference"] = matmul_cpu_baseline()

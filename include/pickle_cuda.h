@@ -319,6 +319,7 @@ typedef struct {
     pickle_cuda_tensor_t output_norm;  /* "output_norm.weight", F32 [hidden]; NULL = no final norm */
     pickle_cuda_tensor_t output;       /* "output.weight" [vocab][hidden]; NULL = token_embd (tied) */
     const pickle_cuda_tensor_t* layers; /* [n_layers][PICKLE_CUDA_LAYER_TENSORS] */
+    int   n_seqs;             /* sequence slots in the device KV cache (0 or 1: one, as the reference) */
 } pickle_cuda_model_params_t;
 
 /* Uploads the weights and allocates the device KV cache (one sequence),
@@ -339,6 +340,23 @@ PICKLE_CUDA_API const char* pickle_cuda_model_last_error(pickle_cuda_model_t* m)
  * (nothing is computed and *kv_pos is kept, as the reference keeps it). */
 PICKLE_CUDA_API int  pickle_cuda_forward(pickle_cuda_model_t* m, const int32_t* tokens, size_t n_tokens,
                                          float* out_logits, size_t* kv_pos);
+/* pickle_cuda_forward for the sequence in cache slot `slot` (0 <= slot <
+ * n_seqs; no counterpart in the reference, which serves one conversation
+ * per KV cache): the prompt of a request admitted into a free slot, or one
+ * of its tokens. PICKLE_ERR_RANGE for a slot outside the model's. */
+PICKLE_CUDA_API int  pickle_cuda_forward_slot(pickle_cuda_model_t* m, int slot, const int32_t* tokens,
+                                              size_t n_tokens, float* out_logits, size_t* kv_pos);
+/* One decode step of n sequences together (continuous batching; no
+ * counterpart in the reference): sequence i feeds token tokens_dev[i] at
+ * position pos_dev[i] of cache slot slot_dev[i] (device int arrays; slots
+ * distinct, positions <= max_pos < max_seq). All n rows go through each
+ * projection in one pass over the weights. logits_dev [n][vocab] gets every
+ * row's logits (vocab a multiple of 4 when n > 1), next_dev [n] (optional)
+ * their pickle_fast_argmax ids. Asynchronous on `stream`; a position or slot
+ * out of range is a device error reported by pickle_cuda_model_sync. */
+PICKLE_CUDA_API int  pickle_cuda_forward_batch_dev(pickle_cuda_model_t* m, int n, const int32_t* tokens_dev,
+                                                   const int* pos_dev, const int* slot_dev, size_t max_pos,
+                                                   float* logits_dev, int32_t* next_dev, void* stream);
 /* The same on device buffers, asynchronous on `stream`: tokens_dev [n_tokens]
  * at positions pos0.., logits_dev [vocab] (last token), and, when next_dev is
  * not NULL, its pickle_fast_argmax id in *next_dev. Device-side errors (a token

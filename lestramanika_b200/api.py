@@ -65,6 +65,7 @@ class ModelParams(ctypes.Structure):
         ("max_tokens", _i), ("prefill_precision", _i), ("weights_on_device", _i),
         ("token_embd", Tensor), ("output_norm", Tensor), ("output", Tensor),
         ("layers", ctypes.POINTER(Tensor)),
+        ("n_seqs", _i),
     ]
 
 SIGNATURES = {
@@ -100,6 +101,8 @@ SIGNATURES = {
     "pickle_cuda_model_last_error": ([_vp], ctypes.c_char_p),
     "pickle_cuda_forward": ([_vp, _i32p, _sz, _fp, ctypes.POINTER(_sz)], _i),
     "pickle_cuda_forward_dev": ([_vp, _vp, _sz, _sz, _vp, _vp, _vp], _i),
+    "pickle_cuda_forward_slot": ([_vp, _i, _i32p, _sz, _fp, ctypes.POINTER(_sz)], _i),
+    "pickle_cuda_forward_batch_dev": ([_vp, _i, _vp, _vp, _vp, _sz, _vp, _vp, _vp], _i),
     "pickle_cuda_model_sync": ([_vp, _vp], _i),
     "pickle_cuda_argmax_dev": ([_vp, _i, _vp, _vp], _i),
     "pickle_cuda_sample_dev": ([_vp, _i, ctypes.c_float, ctypes.c_float, ctypes.c_uint32, _vp, _vp], _i),

@@ -527,12 +527,14 @@ cudaError_t launch_embed_rmsnorm(int T, const int32_t* tok, const void* emb, int
 // keeps the first strictly larger value. Equivalent parallel form: 0 when
 // logits[0] is NaN (nothing compares greater than it); otherwise the first
 // index of the largest non-NaN value, and 0 when no value exceeds -inf.
-// One CTA; each thread scans its strided indices in increasing order, then
-// the CTA keeps the larger value, ties going to the lower index.
+// One CTA per row; each thread scans its strided indices in increasing
+// order, then the CTA keeps the larger value, ties going to the lower index.
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ logits, int n,
                                                                 int32_t* __restrict__ out) {
     griddep_launch_dependents();
     griddep_wait();
+    logits += (size_t)blockIdx.x * n;   // one CTA per row of [rows][n]
+    out += blockIdx.x;
     __shared__ float sv[kArgmaxThreads / 32];
     __shared__ int si[kArgmaxThreads / 32];
     float best = -INFINITY;
@@ -583,6 +585,7 @@ struct DevTensor {
     int type = -1;
     const void* d = nullptr;
     size_t nbytes = 0;
+    const float* rowsc = nullptr;   // the GEMM's row scales, computed at load (quantized types)
 };
 
 }  // namespace
@@ -593,10 +596,13 @@ enum { R_ATTN_NORM, R_Q, R_K, R_V, R_O, R_FFN_NORM, R_GATE, R_UP, R_DOWN };
 struct pickle_cuda_model {
     int device = 0;
     int NL = 0, HD = 0, ID = 0, H = 0, HK = 0, D = 0, VS = 0, max_seq = 0, max_tok = 0, precision = 0;
+    int S = 1;        // cache slots (sequences)
+    int rows = 0;     // activation rows: max(max_tok, S)
     float eps = 0;
     pickle_cuda_t* attn = nullptr;
     void* blob = nullptr;            // the uploaded weights (null: caller-owned device pointers)
     float* embd_f32 = nullptr;       // a quantized token_embd, dequantized at load
+    float* rowsc = nullptr;          // the GEMM row scales of the quantized matrices
     DevTensor embd, out_norm, out;   // out.d == embd.d when tied
     std::vector<DevTensor> lt;       // [NL][9]
     // Per layer: how many of q, k, v (1..3) form one matrix (same type, rows
@@ -628,7 +634,7 @@ int fail(pickle_cuda_model* m, int rc, const char* what) {
 // A projection with the model's own (constant) weights.
 int mm(pickle_cuda_model* m, const DevTensor& w, const float* x, float* y, int out_n, int in_n, int T,
        cudaStream_t st) {
-    return pcu_matmul_ex(w.type, w.d, out_n, in_n, T, x, y, m->ws, m->ws_bytes, st, true);
+    return pcu_matmul_ex(w.type, w.d, out_n, in_n, T, x, y, m->ws, m->ws_bytes, st, true, w.rowsc);
 }
 
 // How the next id is taken from the last row's logits: pickle_fast_argmax
@@ -643,11 +649,26 @@ cudaError_t launch_pick(const Pick& pk, float* logits, int n, int32_t* out, cuda
     return launch_pdl(sample_kernel, 1, kSampleThreads, st, logits, n, pk.temp, pk.top_p, pk.seed, out);
 }
 
+// Where the attention of a pass reads and writes the cache:
+//   n == 0: T tokens of cache slot `slot` at positions [pos0, pos0 + T)
+//           (slot 0: pickle_cuda_prefill_dev / pickle_cuda_decode_batch_dev,
+//           other slots: pickle_cuda_prefill_slot_dev);
+//   n > 0:  one token of each of n sequences, sequence i at position
+//           pos_dev[i] of slot slot_dev[i] (pickle_cuda_decode_ragged_dev);
+//           every row then gets logits and an argmax.
+struct Attn {
+    int slot = 0;
+    int n = 0;
+    const int* pos_dev = nullptr;
+    const int* slot_dev = nullptr;
+    size_t max_pos = 0;
+};
+
 // T tokens (device ids at tok_dev) at positions [pos0, pos0 + T), T <= max_tok,
 // all layers; when with_logits, the last row's logits go to logits_dev and
 // its argmax to next_dev (when non-null). Asynchronous on st.
 int run_chunk(pickle_cuda_model* m, const int32_t* tok_dev, int T, size_t pos0, bool with_logits, float* logits_dev,
-              int32_t* next_dev, cudaStream_t st, const Pick& pk = Pick()) {
+              int32_t* next_dev, cudaStream_t st, const Pick& pk = Pick(), const Attn& at = Attn()) {
     const int HD = m->HD, ID = m->ID, qd = m->H * m->D, kd = m->HK * m->D;
     const DevTensor* L0 = &m->lt[0];
     if (launch_embed_rmsnorm(T, tok_dev, m->embd.d, m->embd.type == T_F16, m->VS,
@@ -680,8 +701,15 @@ int run_chunk(pickle_cuda_model* m, const int32_t* tok_dev, int T, size_t pos0, 
             if ((rc = mm(m, W[R_K], m->xn, k, kd, HD, T, st)) != PICKLE_OK) return fail(m, rc, "k projection");
             if ((rc = mm(m, W[R_V], m->xn, v, kd, HD, T, st)) != PICKLE_OK) return fail(m, rc, "v projection");
         }
-        rc = T == 1 ? pickle_cuda_decode_batch_dev(m->attn, L, 1, pos0, q, k, v, m->ao, st)
-                    : pickle_cuda_prefill_dev(m->attn, L, 1, pos0, (size_t)T, q, k, v, m->ao, m->precision, st);
+        if (at.n > 0)
+            rc = pickle_cuda_decode_ragged_dev(m->attn, L, at.n, at.pos_dev, at.slot_dev, at.max_pos, q, k, v, m->ao,
+                                               st);
+        else if (at.slot == 0)
+            rc = T == 1 ? pickle_cuda_decode_batch_dev(m->attn, L, 1, pos0, q, k, v, m->ao, st)
+                        : pickle_cuda_prefill_dev(m->attn, L, 1, pos0, (size_t)T, q, k, v, m->ao, m->precision, st);
+        else
+            rc = pickle_cuda_prefill_slot_dev(m->attn, L, at.slot, pos0, (size_t)T, q, k, v, m->ao,
+                                              T == 1 ? PICKLE_CUDA_PREFILL_F32 : m->precision, st);
         if (rc != PICKLE_OK) return fail(m, rc, pickle_cuda_last_error(m->attn));
         if ((rc = mm(m, W[R_O], m->ao, m->proj, HD, qd, T, st)) != PICKLE_OK) return fail(m, rc, "output projection");
         if (launch_add_rmsnorm(T, m->x, m->proj, static_cast<const float*>(W[R_FFN_NORM].d), m->xn, HD, m->eps,
@@ -710,6 +738,18 @@ int run_chunk(pickle_cuda_model* m, const int32_t* tok_dev, int T, size_t pos0, 
     }
     // A chunk before the last one leaves only its cache rows behind.
     if (!with_logits) return PICKLE_OK;
+    if (at.n > 0) {
+        // One token of each sequence: every row's logits and argmax.
+        if (launch_add_rmsnorm(T, m->x, m->proj, static_cast<const float*>(m->out_norm.d), m->xn, HD, m->eps, st) !=
+            cudaSuccess)
+            return fail(m, PICKLE_ERR_DEVICE, "norm launch failed");
+        if ((rc = mm(m, m->out, m->xn, logits_dev, m->VS, HD, T, st)) != PICKLE_OK)
+            return fail(m, rc, "output projection (lm_head)");
+        if (next_dev && launch_pdl(argmax_kernel, (unsigned)T, kArgmaxThreads, st, (const float*)logits_dev, m->VS,
+                                   next_dev) != cudaSuccess)
+            return fail(m, PICKLE_ERR_DEVICE, "argmax launch failed");
+        return PICKLE_OK;
+    }
     // Last token only: x += down; xn = rmsnorm(x, output_norm); logits.
     const size_t last = (size_t)(T - 1) * HD;
     if (launch_add_rmsnorm(1, m->x + last, m->proj + last, static_cast<const float*>(m->out_norm.d), m->xn + last, HD,
@@ -761,6 +801,7 @@ void free_model(pickle_cuda_model* m) {
     if (m->attn) pickle_cuda_free(m->attn);
     cudaFree(m->blob);
     cudaFree(m->embd_f32);
+    cudaFree(m->rowsc);
     cudaFree(m->act_blob);
     cudaFree(m->ws);
     if (m->ids_host) cudaFreeHost(m->ids_host);
@@ -797,7 +838,7 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_model_load(const pickle_cuda_model_pa
     if (p->n_layers < 1 || p->hidden_dim < 4 || p->hidden_dim % 4 || p->intermediate_dim < 4 ||
         p->intermediate_dim % 4 || p->n_heads < 1 || p->n_kv_heads < 1 || p->n_heads % p->n_kv_heads ||
         p->head_dim < 4 || p->head_dim % 4 || p->vocab_size < 1 || p->max_seq < 1 || p->max_tokens < 1 ||
-        p->hidden_dim > 4 * kMaxNormVec * kNormThreads ||
+        p->hidden_dim > 4 * kMaxNormVec * kNormThreads || p->n_seqs < 0 || p->n_seqs > 4096 ||
         !(p->rms_eps >= 0.0f) || !p->layers ||
         (p->prefill_precision != PICKLE_CUDA_PREFILL_F32 && p->prefill_precision != PICKLE_CUDA_PREFILL_BF16))
         return PICKLE_ERR_ARG;
@@ -835,6 +876,8 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_model_load(const pickle_cuda_model_pa
     m->device = device;
     m->NL = p->n_layers; m->HD = HD; m->ID = ID; m->H = p->n_heads; m->HK = p->n_kv_heads; m->D = p->head_dim;
     m->VS = p->vocab_size; m->max_seq = p->max_seq; m->max_tok = p->max_tokens; m->precision = p->prefill_precision;
+    m->S = p->n_seqs > 0 ? p->n_seqs : 1;
+    m->rows = m->max_tok > m->S ? m->max_tok : m->S;
     m->eps = p->rms_eps;
     if (cudaSetDevice(device) != cudaSuccess) { free_model(m); return PICKLE_ERR_DEVICE; }
 
@@ -842,7 +885,7 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_model_load(const pickle_cuda_model_pa
     pickle_cuda_params_t ap{};
     ap.n_layers = p->n_layers; ap.n_heads = p->n_heads; ap.n_kv_heads = p->n_kv_heads; ap.head_dim = p->head_dim;
     ap.max_seq = p->max_seq; ap.half = p->head_dim / 2 < 64 ? p->head_dim / 2 : 64;
-    ap.rope_inv_freq = p->rope_inv_freq; ap.rope_theta = p->rope_theta; ap.n_seqs = 1; ap.rope_len = 0;
+    ap.rope_inv_freq = p->rope_inv_freq; ap.rope_theta = p->rope_theta; ap.n_seqs = m->S; ap.rope_len = 0;
     if ((rc = pickle_cuda_init(&ap, device, &m->attn)) != PICKLE_OK) { free_model(m); return rc; }
 
     // Weights: one allocation, uploaded once, every tensor 256-byte aligned
@@ -919,6 +962,37 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_model_load(const pickle_cuda_model_pa
     auto follows = [](const DevTensor& a, const DevTensor& b) {   // b continues matrix a
         return a.type == b.type && static_cast<const char*>(a.d) + a.nbytes == static_cast<const char*>(b.d);
     };
+    // The GEMM's per-row weight scales, once: the weights never change. One
+    // array, each tensor's rows after the previous one's, so that a fused
+    // gate|up matrix finds its rows' scales back to back too.
+    {
+        struct Job { DevTensor* t; int rows, in; };
+        std::vector<Job> jobs;
+        const int rows_of[kLayerTensors] = {0, qd, kd, kd, HD, 0, ID, ID, HD};
+        const int in_of[kLayerTensors] = {0, HD, HD, HD, qd, 0, HD, HD, ID};
+        auto quant = [](int t) { return t == T_Q4_0 || t == T_Q8_0 || t == T_Q4_K || t == T_Q6_K; };
+        for (int L = 0; L < p->n_layers; ++L)
+            for (int r = 0; r < kLayerTensors; ++r) {
+                DevTensor* t = &m->lt[(size_t)L * kLayerTensors + r];
+                if (rows_of[r] && quant(t->type)) jobs.push_back({t, rows_of[r], in_of[r]});
+            }
+        if (p->output.data && quant(m->out.type)) jobs.push_back({&m->out, p->vocab_size, HD});
+        size_t total = 0;
+        for (auto& e : jobs) total += (size_t)e.rows;
+        if (total > 0) {
+            if (cudaMalloc((void**)&m->rowsc, total * 4) != cudaSuccess) { free_model(m); return PICKLE_ERR_MEMORY; }
+            size_t off = 0;
+            for (auto& e : jobs) {
+                if (pcu_matmul_rowscale(e.t->type, e.t->d, e.rows, e.in, m->rowsc + off, nullptr) != PICKLE_OK) {
+                    free_model(m);
+                    return PICKLE_ERR_DEVICE;
+                }
+                e.t->rowsc = m->rowsc + off;
+                off += (size_t)e.rows;
+            }
+            if (cudaDeviceSynchronize() != cudaSuccess) { free_model(m); return PICKLE_ERR_DEVICE; }
+        }
+    }
     m->qkv_run.assign(p->n_layers, 1);
     m->gu_fused.assign(p->n_layers, 0);
     for (int L = 0; L < p->n_layers; ++L) {
@@ -928,7 +1002,7 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_model_load(const pickle_cuda_model_pa
     }
 
     // Activations for max_tok rows.
-    const size_t T = (size_t)m->max_tok;
+    const size_t T = (size_t)m->rows;
     const size_t sizes[] = {T * HD * 4, T * HD * 4, T * qd * 4, T * kd * 4, T * kd * 4, T * qd * 4, T * HD * 4,
                             2 * T * ID * 4, T * ID * 4, (size_t)m->VS * 4, (size_t)m->VS * 4, T * 4,
                             ((size_t)m->max_seq + 1) * 4, 256, (size_t)(qd + 2 * kd) * 4};
@@ -944,11 +1018,15 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_model_load(const pickle_cuda_model_pa
         a += align256(sizes[i]);
     }
     if (cudaMemset(m->err, 0, sizeof(int)) != cudaSuccess) { free_model(m); return PICKLE_ERR_DEVICE; }
-    const int shapes[][2] = {{qd, HD}, {kd, HD}, {HD, qd}, {ID, HD}, {2 * ID, HD}, {HD, ID}};
-    for (auto& s : shapes) {
-        const size_t b = pickle_cuda_matmul_workspace(s[0], s[1], m->max_tok);
-        if (b > m->ws_bytes) m->ws_bytes = b;
-    }
+    const int shapes[][2] = {{qd, HD}, {kd, HD}, {HD, qd}, {ID, HD}, {2 * ID, HD}, {HD, ID}, {p->vocab_size, HD}};
+    // Every row count a pass can have: the split-K partials do not grow with it.
+    const int counts[] = {m->rows, 128, 64, 32, 8, 2};
+    for (auto& s : shapes)
+        for (int c : counts) {
+            if (c > m->rows) continue;
+            const size_t b = pickle_cuda_matmul_workspace(s[0], s[1], c);
+            if (b > m->ws_bytes) m->ws_bytes = b;
+        }
     if (cudaMalloc(&m->ws, m->ws_bytes) != cudaSuccess) { free_model(m); return PICKLE_ERR_MEMORY; }
     if (cudaHostAlloc((void**)&m->ids_host, ((size_t)m->max_seq + 1) * 4, cudaHostAllocDefault) != cudaSuccess ||
         cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess ||
@@ -970,9 +1048,12 @@ extern "C" PICKLE_CUDA_API const char* pickle_cuda_model_last_error(pickle_cuda_
     return m ? m->last_error.c_str() : "null model";
 }
 
-extern "C" PICKLE_CUDA_API int pickle_cuda_forward(pickle_cuda_model_t* m, const int32_t* tokens, size_t n_tokens,
-                                                   float* out_logits, size_t* kv_pos) {
+extern "C" PICKLE_CUDA_API int pickle_cuda_forward_slot(pickle_cuda_model_t* m, int slot, const int32_t* tokens,
+                                                        size_t n_tokens, float* out_logits, size_t* kv_pos) {
     if (!m || !tokens || !out_logits || !kv_pos || n_tokens == 0) return PICKLE_ERR_ARG;
+    if (slot < 0 || slot >= m->S) return fail(m, PICKLE_ERR_RANGE, "cache slot outside [0, n_seqs)");
+    Attn at;
+    at.slot = slot;
     if (cudaSetDevice(m->device) != cudaSuccess) return PICKLE_ERR_DEVICE;
     const size_t pos0 = *kv_pos;
     // The reference stops at the first token outside [0, vocab) or at a
@@ -987,7 +1068,7 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_forward(pickle_cuda_model_t* m, const
         if (cudaMemcpyAsync(m->tok, tokens + c0, T * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
             return fail(m, PICKLE_ERR_DEVICE, "token upload failed");
         const bool last = c0 + T == n_tokens;
-        const int rc = run_chunk(m, m->tok, (int)T, pos0 + c0, last, m->logits, nullptr, st);
+        const int rc = run_chunk(m, m->tok, (int)T, pos0 + c0, last, m->logits, nullptr, st, Pick(), at);
         if (rc != PICKLE_OK) return rc;
         if (!last && cudaStreamSynchronize(st) != cudaSuccess)   // m->tok is reused by the next chunk
             return fail(m, PICKLE_ERR_DEVICE, "stream synchronize failed");
@@ -998,6 +1079,27 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_forward(pickle_cuda_model_t* m, const
     if (rc != PICKLE_OK) return rc;
     *kv_pos = pos0 + n_tokens;
     return PICKLE_OK;
+}
+
+extern "C" PICKLE_CUDA_API int pickle_cuda_forward(pickle_cuda_model_t* m, const int32_t* tokens, size_t n_tokens,
+                                                   float* out_logits, size_t* kv_pos) {
+    return pickle_cuda_forward_slot(m, 0, tokens, n_tokens, out_logits, kv_pos);
+}
+
+extern "C" PICKLE_CUDA_API int pickle_cuda_forward_batch_dev(pickle_cuda_model_t* m, int n, const int32_t* tokens_dev,
+                                                             const int* pos_dev, const int* slot_dev, size_t max_pos,
+                                                             float* logits_dev, int32_t* next_dev, void* stream) {
+    if (!m || !tokens_dev || !pos_dev || !slot_dev || !logits_dev || n < 1) return PICKLE_ERR_ARG;
+    if (n > m->S) return fail(m, PICKLE_ERR_RANGE, "more sequences than cache slots");
+    if ((uintptr_t)logits_dev % 16 || (n > 1 && m->VS % 4)) return fail(m, PICKLE_ERR_ARG, "logits rows unaligned");
+    if (max_pos >= (size_t)m->max_seq) return fail(m, PICKLE_ERR_RANGE, "position >= max_seq");
+    if (cudaSetDevice(m->device) != cudaSuccess) return PICKLE_ERR_DEVICE;
+    Attn at;
+    at.n = n;
+    at.pos_dev = pos_dev;
+    at.slot_dev = slot_dev;
+    at.max_pos = max_pos;
+    return run_chunk(m, tokens_dev, n, 0, true, logits_dev, next_dev, static_cast<cudaStream_t>(stream), Pick(), at);
 }
 
 extern "C" PICKLE_CUDA_API int pickle_cuda_forward_dev(pickle_cuda_model_t* m, const int32_t* tokens_dev,

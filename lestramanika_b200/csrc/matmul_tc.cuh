@@ -41,11 +41,14 @@ using mvtc::F_Q4_K;
 using mvtc::F_Q6_K;
 using mvtc::F_Q8_0;
 
+// BN, the token tile (the MMA's N), is 128 for prompts and 32 or 64 for
+// small decode batches, whose one token tile would leave most of a
+// 128-wide MMA on zero rows.
 constexpr int BM = 128, BN = 128, BK = 64, KB = 256;
 constexpr int A_STAGES = 2, X_STAGES = 3, RAW_STAGES = 2;
-constexpr int TILE = 128 * 128;                       // bytes of one 128 x 64 f16 tile
+constexpr int TILE = 128 * 128;                       // bytes of one 128 x 64 f16 weight tile
 constexpr int THREADS = 320;
-constexpr int TMEM_COLS = BN;
+inline int bn_for(int n_tok) { return n_tok <= 32 ? 32 : n_tok <= 64 ? 64 : 128; }
 
 // Raw weight bytes of one 256-element K-block per row (the TMA box width).
 template <int TYPE> struct Raw;
@@ -66,9 +69,10 @@ PCU_DEV int raw_x(int kb) {
 
 constexpr int OFF_A = 0;                                  // [A_STAGES][hi, lo] tiles
 constexpr int OFF_X = OFF_A + A_STAGES * 2 * TILE;        // [XS][hi, lo] tiles
-template <int TYPE> struct Lay {
-    static constexpr int XS = Raw<TYPE>::B > 240 ? 2 : X_STAGES;     // x ring depth that fits
-    static constexpr int OFF_RAW = OFF_X + XS * 2 * TILE;            // [RAW_STAGES][BM][Raw::B]
+template <int TYPE, int BNT> struct Lay {
+    static constexpr int XT = BNT * 128;                             // bytes of one BNT x 64 f16 x tile
+    static constexpr int XS = Raw<TYPE>::B > 240 && BNT == 128 ? 2 : X_STAGES;   // x ring depth that fits
+    static constexpr int OFF_RAW = OFF_X + XS * 2 * XT;              // [RAW_STAGES][BM][Raw::B]
     static constexpr int OFF_BAR = OFF_RAW + RAW_STAGES * BM * Raw<TYPE>::B;
     // RAW_FULL[2], RAW_EMPTY[2], A_FULL[2], A_EMPTY[2], X_FULL[XS], X_EMPTY[XS], D_FULL
     static constexpr int N_BARS = 2 * RAW_STAGES + 2 * A_STAGES + 2 * XS + 1;
@@ -78,8 +82,9 @@ template <int TYPE> struct Lay {
 };
 
 // tcgen05 instruction descriptor, kind::f16 with F16 A and B, F32
-// accumulate, both K-major, M = 128, N = BN.
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// accumulate, both K-major, M = 128, N = BNT.
+template <int BNT>
+__host__ __device__ constexpr uint32_t idesc() { return (1u << 4) | ((uint32_t)(BNT >> 3) << 17) | ((uint32_t)(BM >> 4) << 24); }
 
 // Shared-memory matrix descriptor: 128-byte swizzle, 8-row atoms 1024 bytes apart.
 PCU_DEV uint64_t sdesc(uint32_t saddr) {
@@ -92,11 +97,11 @@ PCU_DEV uint64_t sdesc(uint32_t saddr) {
     return d;
 }
 
-PCU_DEV void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+PCU_DEV void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc, uint32_t id) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(d_tmem), "l"(a), "l"(b), "r"(kIdesc), "r"(acc)
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(id), "r"(acc)
         : "memory");
 }
 
@@ -316,12 +321,15 @@ PCU_DEV void dequant_kstep(uint32_t rw, int kb, int ks, float rsc, float (&w)[64
 
 // ------------------------------------------------------------------- kernel
 
-template <int TYPE>
+template <int TYPE, int BNT>
 __global__ void __launch_bounds__(THREADS, 1)
     matmul_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xh,
                      const __grid_constant__ CUtensorMap tm_xl, int out_n, int in_n, int n_tok,
-                     const float* __restrict__ xinv, const float* __restrict__ rowsc, float* __restrict__ y) {
-    using L = Lay<TYPE>;
+                     const float* __restrict__ xinv, const float* __restrict__ rowsc, float* __restrict__ y,
+                     float* __restrict__ part) {
+    using L = Lay<TYPE, BNT>;
+    constexpr int XT = L::XT, TMEM_COLS = BNT;
+    constexpr uint32_t ID = idesc<BNT>();
     constexpr bool QUANT = TYPE != F_F16;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -332,8 +340,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                    X_EMPTY = X_FULL + 8 * L::XS, D_FULL = X_EMPTY + 8 * L::XS;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_TMEM);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
-    const int nkb = in_n / KB, nks = nkb * (KB / BK);
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BNT;
+    // Split K: this CTA takes K-blocks [kb0, kb0 + nkb) of slice blockIdx.z
+    // (the host makes every slice non-empty); stages are numbered within it.
+    const int nkb_all = in_n / KB;
+    const int kb0 = (int)blockIdx.z * nkb_all / (int)gridDim.z;
+    const int nkb = ((int)blockIdx.z + 1) * nkb_all / (int)gridDim.z - kb0, nks = nkb * (KB / BK);
 
     if (threadIdx.x == 0) {
         uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
@@ -366,23 +378,24 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ---------------------------------------------------------- producer
         if (lane == 0) {
             #pragma unroll 1
-            for (int kb = 0; kb < nkb; ++kb) {
+            for (int kl = 0; kl < nkb; ++kl) {
+                const int kb = kb0 + kl;
                 if constexpr (QUANT) {
-                    const int rs = kb % RAW_STAGES;
-                    if (kb >= RAW_STAGES)
-                        mvtc::wait_or_flag(RAW_EMPTY + 8 * rs, ((kb / RAW_STAGES) - 1) & 1, PCU_DEVERR_EMPTY_WAIT);
+                    const int rs = kl % RAW_STAGES;
+                    if (kl >= RAW_STAGES)
+                        mvtc::wait_or_flag(RAW_EMPTY + 8 * rs, ((kl / RAW_STAGES) - 1) & 1, PCU_DEVERR_EMPTY_WAIT);
                     mbar_expect(RAW_FULL + 8 * rs, BM * Raw<TYPE>::B);
                     tma2d(base + L::OFF_RAW + rs * BM * Raw<TYPE>::B, &tm_w, raw_x<TYPE>(kb), m0, RAW_FULL + 8 * rs);
                 }
                 #pragma unroll 1
                 for (int ks = 0; ks < KB / BK; ++ks) {
-                    const int s = kb * (KB / BK) + ks, k = kb * KB + ks * BK;
+                    const int s = kl * (KB / BK) + ks, k = kb * KB + ks * BK;
                     const int xs = s % L::XS;
                     if (s >= L::XS)
                         mvtc::wait_or_flag(X_EMPTY + 8 * xs, ((s / L::XS) - 1) & 1, PCU_DEVERR_EMPTY_WAIT);
-                    mbar_expect(X_FULL + 8 * xs, 2 * TILE);
-                    tma2d(base + OFF_X + (2 * xs) * TILE, &tm_xh, k, n0, X_FULL + 8 * xs);
-                    tma2d(base + OFF_X + (2 * xs + 1) * TILE, &tm_xl, k, n0, X_FULL + 8 * xs);
+                    mbar_expect(X_FULL + 8 * xs, 2 * XT);
+                    tma2d(base + OFF_X + (2 * xs) * XT, &tm_xh, k, n0, X_FULL + 8 * xs);
+                    tma2d(base + OFF_X + (2 * xs + 1) * XT, &tm_xl, k, n0, X_FULL + 8 * xs);
                     if constexpr (!QUANT) {
                         const int as = s % A_STAGES;
                         if (s >= A_STAGES)
@@ -403,13 +416,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                 mvtc::wait_or_flag(X_FULL + 8 * xs, (s / L::XS) & 1, PCU_DEVERR_FULL_WAIT);
                 tc_after();
                 const uint32_t ah = base + OFF_A + (2 * as) * TILE, al = ah + TILE;
-                const uint32_t xh = base + OFF_X + (2 * xs) * TILE, xl = xh + TILE;
+                const uint32_t xh = base + OFF_X + (2 * xs) * XT, xl = xh + XT;
                 #pragma unroll
                 for (int k = 0; k < BK / 16; ++k) {
                     const uint32_t o = 32 * k;        // 16 f16 of a 128-byte swizzled row
-                    umma(tmem, sdesc(ah + o), sdesc(xh + o), (s | k) != 0);
-                    umma(tmem, sdesc(ah + o), sdesc(xl + o), 1);
-                    if constexpr (QUANT) umma(tmem, sdesc(al + o), sdesc(xh + o), 1);
+                    umma(tmem, sdesc(ah + o), sdesc(xh + o), (s | k) != 0, ID);
+                    umma(tmem, sdesc(ah + o), sdesc(xl + o), 1, ID);
+                    if constexpr (QUANT) umma(tmem, sdesc(al + o), sdesc(xh + o), 1, ID);
                 }
                 umma_commit(A_EMPTY + 8 * as);
                 umma_commit(X_EMPTY + 8 * xs);
@@ -422,13 +435,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int r = threadIdx.x - 64;                 // weight row within the tile
             const float rsc = (m0 + r < out_n) ? __ldg(rowsc + m0 + r) : 1.f;
             #pragma unroll 1
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int rs = kb % RAW_STAGES;
-                mvtc::wait_or_flag(RAW_FULL + 8 * rs, (kb / RAW_STAGES) & 1, PCU_DEVERR_FULL_WAIT);
+            for (int kl = 0; kl < nkb; ++kl) {
+                const int kb = kb0 + kl;
+                const int rs = kl % RAW_STAGES;
+                mvtc::wait_or_flag(RAW_FULL + 8 * rs, (kl / RAW_STAGES) & 1, PCU_DEVERR_FULL_WAIT);
                 const uint32_t rw = base + L::OFF_RAW + rs * BM * Raw<TYPE>::B + r * Raw<TYPE>::B;
                 #pragma unroll 1
                 for (int ks = 0; ks < KB / BK; ++ks) {
-                    const int s = kb * (KB / BK) + ks, as = s % A_STAGES;
+                    const int s = kl * (KB / BK) + ks, as = s % A_STAGES;
                     if (s >= A_STAGES)
                         mvtc::wait_or_flag(A_EMPTY + 8 * as, ((s / A_STAGES) - 1) & 1, PCU_DEVERR_EMPTY_WAIT);
                     float w[64];                              // the K-step's 64 weights of row r, scaled
@@ -462,13 +476,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_after();
         const float rinv = (QUANT && m < out_n) ? 1.f / __ldg(rowsc + m) : 1.f;
         #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = 0; c < BNT / 32; ++c) {
             float v[32];
             tmem_ld32x(tmem + ((uint32_t)(32 * q) << 16) + 32 * c, v);
             #pragma unroll
             for (int j = 0; j < 32; ++j) {
                 const int n = n0 + 32 * c + j;
-                if (m < out_n && n < n_tok) y[(size_t)n * out_n + m] = v[j] * rinv * __ldg(xinv + n);
+                if (m < out_n && n < n_tok) {
+                    const float o = v[j] * rinv * __ldg(xinv + n);
+                    if (part) part[((size_t)blockIdx.z * n_tok + n) * out_n + m] = o;
+                    else y[(size_t)n * out_n + m] = o;
+                }
             }
         }
     }
@@ -476,6 +494,17 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+}
+
+// Sum of the split-K slices' partial outputs, in slice order:
+// y[i] = part[0][i] + part[1][i] + ... (i over n_tok * out_n).
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int ks, size_t total, float* __restrict__ y) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        float a = part[i];
+        for (int z = 1; z < ks; ++z) a += part[(size_t)z * total + i];
+        y[i] = a;
+    }
 }
 
 // ---------------------------------------------------------------- host side
@@ -519,9 +548,26 @@ inline bool map_raw(CUtensorMap* m, const void* W, size_t row_bytes, int out_n, 
 
 inline size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 
-// Workspace: x hi, x lo [n_tok][in_n] f16, xinv [n_tok], rowsc [out_n].
+// K slices: when the output tiles do not fill the 148 SMs (a decode batch:
+// one token tile), each tile's K-blocks are split over up to 16 CTAs.
+constexpr int kSms = 148;
+inline int split_k(int out_n, int in_n, int n_tok) {
+    const int bn = bn_for(n_tok);
+    const long long tiles = (long long)((out_n + BM - 1) / BM) * ((n_tok + bn - 1) / bn);
+    const int nkb = in_n / KB;
+    if (tiles >= kSms || nkb < 2) return 1;
+    int ks = (int)(kSms / tiles);
+    if (ks > 16) ks = 16;
+    if (ks > nkb) ks = nkb;
+    return ks < 1 ? 1 : ks;
+}
+
+// Workspace: x hi, x lo [n_tok][in_n] f16, xinv [n_tok], rowsc [out_n],
+// and the split-K partials [ks][n_tok][out_n] when ks > 1.
 inline size_t workspace_bytes(int out_n, int in_n, int n_tok) {
-    return 2 * align256((size_t)n_tok * in_n * 2) + align256((size_t)n_tok * 4) + align256((size_t)out_n * 4);
+    const int ks = split_k(out_n, in_n, n_tok);
+    return 2 * align256((size_t)n_tok * in_n * 2) + align256((size_t)n_tok * 4) + align256((size_t)out_n * 4) +
+           (ks > 1 ? align256((size_t)ks * n_tok * out_n * 4) : 0);
 }
 
 // Rows that are 16-byte multiples (TMA) and whole 256-element K-blocks.
@@ -529,21 +575,28 @@ inline bool supported(const void* W, size_t row_bytes, int in_n) {
     return reinterpret_cast<uintptr_t>(W) % 16 == 0 && row_bytes % 16 == 0 && in_n % KB == 0;
 }
 
-template <int TYPE>
-inline cudaError_t launch(const uint8_t* W, size_t row_bytes, int out_n, int in_n, int n_tok, const float* x,
-                          float* y, void* ws, cudaStream_t st) {
+template <int TYPE, int BNT>
+inline cudaError_t launch_bn(const uint8_t* W, size_t row_bytes, int out_n, int in_n, int n_tok, const float* x,
+                          float* y, void* ws, cudaStream_t st, const float* rowsc_pre = nullptr) {
     uint8_t* p = static_cast<uint8_t*>(ws);
     const size_t plane = align256((size_t)n_tok * in_n * 2);
     __half* xh = reinterpret_cast<__half*>(p);
     __half* xl = reinterpret_cast<__half*>(p + plane);
     float* xinv = reinterpret_cast<float*>(p + 2 * plane);
     float* rowsc = reinterpret_cast<float*>(p + 2 * plane + align256((size_t)n_tok * 4));
+    const int ks = split_k(out_n, in_n, n_tok);
+    float* part = ks > 1 ? reinterpret_cast<float*>(p + 2 * plane + align256((size_t)n_tok * 4) +
+                                                    align256((size_t)out_n * 4))
+                         : nullptr;
     xsplit_kernel<<<n_tok, 256, 0, st>>>(x, in_n, xh, xl, xinv);
-    if constexpr (TYPE != F_F16)
-        rowscale_kernel<TYPE><<<(out_n + 7) / 8, 256, 0, st>>>(W, row_bytes, out_n, in_n, rowsc);
+    if constexpr (TYPE != F_F16) {
+        // the row scales of constant weights may come precomputed
+        if (rowsc_pre) rowsc = const_cast<float*>(rowsc_pre);
+        else rowscale_kernel<TYPE><<<(out_n + 7) / 8, 256, 0, st>>>(W, row_bytes, out_n, in_n, rowsc);
+    }
     alignas(64) CUtensorMap tw, th, tl;
     const bool ok = (TYPE == F_F16 ? map_f16(&tw, W, in_n, out_n, BM) : map_raw(&tw, W, row_bytes, out_n, Raw<TYPE>::B)) &&
-                    map_f16(&th, xh, in_n, n_tok, BN) && map_f16(&tl, xl, in_n, n_tok, BN);
+                    map_f16(&th, xh, in_n, n_tok, BNT) && map_f16(&tl, xl, in_n, n_tok, BNT);
     if (!ok) return cudaErrorInvalidValue;
     static bool attr[64] = {};
     int dev = 0;
@@ -551,12 +604,37 @@ inline cudaError_t launch(const uint8_t* W, size_t row_bytes, int out_n, int in_
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!attr[dev]) {
         cudaError_t e =
-            cudaFuncSetAttribute(matmul_tc_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay<TYPE>::BYTES);
+            cudaFuncSetAttribute(matmul_tc_kernel<TYPE, BNT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Lay<TYPE, BNT>::BYTES);
         if (e != cudaSuccess) return e;
         attr[dev] = true;
     }
-    const dim3 grid((unsigned)((out_n + BM - 1) / BM), (unsigned)((n_tok + BN - 1) / BN));
-    matmul_tc_kernel<TYPE><<<grid, THREADS, Lay<TYPE>::BYTES, st>>>(tw, th, tl, out_n, in_n, n_tok, xinv, rowsc, y);
+    const dim3 grid((unsigned)((out_n + BM - 1) / BM), (unsigned)((n_tok + BNT - 1) / BNT), (unsigned)ks);
+    matmul_tc_kernel<TYPE, BNT><<<grid, THREADS, Lay<TYPE, BNT>::BYTES, st>>>(tw, th, tl, out_n, in_n, n_tok, xinv,
+                                                                              rowsc, y, part);
+    if (ks > 1) {
+        const size_t total = (size_t)n_tok * out_n;
+        const unsigned blocks = (unsigned)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
+        splitk_reduce_kernel<<<blocks, 256, 0, st>>>(part, ks, total, y);
+    }
+    return cudaGetLastError();
+}
+
+template <int TYPE>
+inline cudaError_t launch(const uint8_t* W, size_t row_bytes, int out_n, int in_n, int n_tok, const float* x,
+                          float* y, void* ws, cudaStream_t st, const float* rowsc_pre = nullptr) {
+    switch (bn_for(n_tok)) {
+        case 32: return launch_bn<TYPE, 32>(W, row_bytes, out_n, in_n, n_tok, x, y, ws, st, rowsc_pre);
+        case 64: return launch_bn<TYPE, 64>(W, row_bytes, out_n, in_n, n_tok, x, y, ws, st, rowsc_pre);
+        default: return launch_bn<TYPE, 128>(W, row_bytes, out_n, in_n, n_tok, x, y, ws, st, rowsc_pre);
+    }
+}
+
+// The per-row power-of-two weight scales the GEMM uses, computed once for
+// weights that do not change (rowsc [out_n]).
+template <int TYPE>
+inline cudaError_t rowscale(const uint8_t* W, size_t row_bytes, int out_n, int in_n, float* rowsc, cudaStream_t st) {
+    if constexpr (TYPE != F_F16) rowscale_kernel<TYPE><<<(out_n + 7) / 8, 256, 0, st>>>(W, row_bytes, out_n, in_n, rowsc);
     return cudaGetLastError();
 }
 

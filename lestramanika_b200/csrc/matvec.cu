@@ -289,7 +289,7 @@ extern "C" PICKLE_CUDA_API size_t pickle_cuda_matmul_workspace(int out_n, int in
 }
 
 int pcu_matmul_ex(int type, const void* W, int out_n, int in_n, int n_tok, const float* x, float* y,
-                  void* workspace, size_t ws_bytes, void* stream, bool w_static) {
+                  void* workspace, size_t ws_bytes, void* stream, bool w_static, const float* rowsc) {
     if (!W || !x || !y || out_n < 1 || in_n < 1 || n_tok < 1) return PICKLE_ERR_ARG;
     if (((uintptr_t)W | (uintptr_t)x | (uintptr_t)y) % 16) return PICKLE_ERR_ARG;
     if (type != T_F32 && type != T_F16 && type != T_Q4_0 && type != T_Q8_0 && type != T_Q4_K && type != T_Q6_K)
@@ -300,14 +300,28 @@ int pcu_matmul_ex(int type, const void* W, int out_n, int in_n, int n_tok, const
     const unsigned char* w = static_cast<const unsigned char*>(W);
     const bool ws_ok = workspace && (uintptr_t)workspace % 256 == 0 &&
                        ws_bytes >= mmtc::workspace_bytes(out_n, in_n, n_tok);
-    if (n_tok > PICKLE_CUDA_MATVEC_MAX_VEC && ws_ok && type != T_F32 && mmtc::supported(w, row_bytes, in_n)) {
+    // A few rows of a model's constant weights (a decode batch) stay on the
+    // matvec unless it would need more than three passes over W, because
+    // not enough of the rows fit in its shared memory at once.
+    int fit = PICKLE_CUDA_MATVEC_MAX_VEC;
+    if (w_static && n_tok > 1) {
+        switch (type) {
+            case T_F16: fit = mvtc::fit_nv<T_F16>(in_n); break;
+            case T_Q4_0: fit = mvtc::fit_nv<T_Q4_0>(in_n); break;
+            case T_Q8_0: fit = mvtc::fit_nv<T_Q8_0>(in_n); break;
+            case T_Q4_K: fit = mvtc::fit_nv<T_Q4_K>(in_n); break;
+            case T_Q6_K: fit = mvtc::fit_nv<T_Q6_K>(in_n); break;
+        }
+    }
+    const bool gemm = n_tok > PICKLE_CUDA_MATVEC_MAX_VEC || (w_static && (n_tok + fit - 1) / fit > 3);
+    if (gemm && ws_ok && type != T_F32 && mmtc::supported(w, row_bytes, in_n)) {
         cudaError_t e = cudaErrorInvalidValue;
         switch (type) {
-            case T_F16: e = mmtc::launch<T_F16>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st); break;
-            case T_Q4_0: e = mmtc::launch<T_Q4_0>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st); break;
-            case T_Q8_0: e = mmtc::launch<T_Q8_0>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st); break;
-            case T_Q4_K: e = mmtc::launch<T_Q4_K>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st); break;
-            case T_Q6_K: e = mmtc::launch<T_Q6_K>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st); break;
+            case T_F16: e = mmtc::launch<T_F16>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st, rowsc); break;
+            case T_Q4_0: e = mmtc::launch<T_Q4_0>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st, rowsc); break;
+            case T_Q8_0: e = mmtc::launch<T_Q8_0>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st, rowsc); break;
+            case T_Q4_K: e = mmtc::launch<T_Q4_K>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st, rowsc); break;
+            case T_Q6_K: e = mmtc::launch<T_Q6_K>(w, row_bytes, out_n, in_n, n_tok, x, y, workspace, st, rowsc); break;
         }
         return e == cudaSuccess ? PICKLE_OK : PICKLE_ERR_DEVICE;
     }
@@ -324,5 +338,21 @@ int pcu_matmul_ex(int type, const void* W, int out_n, int in_n, int n_tok, const
 extern "C" PICKLE_CUDA_API int pickle_cuda_matmul_dev(int type, const void* W, int out_n, int in_n, int n_tok,
                                                       const float* x, float* y, void* workspace, size_t ws_bytes,
                                                       void* stream) {
-    return pcu_matmul_ex(type, W, out_n, in_n, n_tok, x, y, workspace, ws_bytes, stream, false);
+    return pcu_matmul_ex(type, W, out_n, in_n, n_tok, x, y, workspace, ws_bytes, stream, false, nullptr);
+}
+
+int pcu_matmul_rowscale(int type, const void* W, int out_n, int in_n, float* rowsc, void* stream) {
+    const size_t row_bytes = pickle_cuda_matvec_row_bytes(type, in_n);
+    if (!W || !rowsc || out_n < 1 || row_bytes == 0) return PICKLE_ERR_ARG;
+    const uint8_t* w = static_cast<const uint8_t*>(W);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSuccess;
+    switch (type) {
+        case T_Q4_0: e = mmtc::rowscale<T_Q4_0>(w, row_bytes, out_n, in_n, rowsc, st); break;
+        case T_Q8_0: e = mmtc::rowscale<T_Q8_0>(w, row_bytes, out_n, in_n, rowsc, st); break;
+        case T_Q4_K: e = mmtc::rowscale<T_Q4_K>(w, row_bytes, out_n, in_n, rowsc, st); break;
+        case T_Q6_K: e = mmtc::rowscale<T_Q6_K>(w, row_bytes, out_n, in_n, rowsc, st); break;
+        default: return PICKLE_ERR_TYPE;
+    }
+    return e == cudaSuccess ? PICKLE_OK : PICKLE_ERR_DEVICE;
 }

@@ -7,5 +7,9 @@
 
 int pcu_matvec_ex(int type, const void* W, int out_n, int in_n, int n_vec, const float* x, float* y, void* stream,
                   bool w_static);
+// rowsc: the GEMM's per-row weight scales, precomputed by
+// pcu_matmul_rowscale for constant weights (nullptr: computed per call).
 int pcu_matmul_ex(int type, const void* W, int out_n, int in_n, int n_tok, const float* x, float* y,
-                  void* workspace, size_t ws_bytes, void* stream, bool w_static);
+                  void* workspace, size_t ws_bytes, void* stream, bool w_static, const float* rowsc);
+// Those scales for W [out_n][in_n] of a quantized type (Q4_0, Q8_0, Q4_K, Q6_K).
+int pcu_matmul_rowscale(int type, const void* W, int out_n, int in_n, float* rowsc, void* stream);

@@ -769,6 +769,15 @@ inline bool tc_supported(const void* W, size_t row_bytes, int in_n) {
     return smem_layout<TYPE>(in_n, 1, Warps<TYPE, 1>::CW).bytes <= kSmemLimit;
 }
 
+// Vectors one pass over W can take: as many (up to 8) as fit in shared
+// memory beside a two-stage ring.
+template <int TYPE>
+inline int fit_nv(int in_n) {
+    int nv = 8;
+    while (nv > 1 && smem_layout<TYPE>(in_n, nv, consumer_warps(TYPE, nv)).bytes > kSmemLimit) --nv;
+    return nv;
+}
+
 template <int TYPE, int NV>
 inline cudaError_t launch_nv(const CUtensorMap& tm, int out_n, int in_n, const float* x, float* y, cudaStream_t st,
                              bool w_early) {

@@ -29,10 +29,12 @@ def _dev_tensor(typ, t):
 
 
 class PickleModel:
-    def __init__(self, tensors, arch, device=0, max_tokens=512, precision=api.PREFILL_F32, rope_inv_freq=None):
+    def __init__(self, tensors, arch, device=0, max_tokens=512, precision=api.PREFILL_F32, rope_inv_freq=None,
+                 n_seqs=1):
         """tensors: {gguf name: (ggml_type, data)} with data a numpy array of the
         raw bytes (host) or a torch CUDA tensor (used in place, kept alive by
-        this object); arch: the dict gguf.arch_detect returns."""
+        this object); arch: the dict gguf.arch_detect returns; n_seqs: cache
+        slots, for generate_batch / forward_batch_dev."""
         self.arch = dict(arch)
         self.VS, self.max_seq = arch["vocab_size"], arch["max_seq"]
         keep = []
@@ -75,6 +77,8 @@ class PickleModel:
                 layers[L * api.LAYER_TENSORS + j] = tensor(f"blk.{L}.{n}.weight")
         p.layers = layers
         p.weights_on_device = 1 if on_dev else 0
+        p.n_seqs = int(n_seqs)
+        self.n_seqs = max(1, int(n_seqs))
         h = ctypes.c_void_p()
         rc = api.lib().pickle_cuda_model_load(ctypes.byref(p), int(device), ctypes.byref(h))
         if rc != 0:
@@ -116,6 +120,79 @@ class PickleModel:
                                                   logits.ctypes.data_as(api._fp), ctypes.byref(pos)),
                     "pickle_cuda_forward")
         return logits, pos.value
+
+    def forward_slot(self, slot, tokens, kv_pos):
+        """pickle_fast_forward for the sequence in cache slot `slot`."""
+        tok = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty(self.VS, np.float32)
+        pos = ctypes.c_size_t(int(kv_pos))
+        self._check(api.lib().pickle_cuda_forward_slot(self._h, int(slot), tok.ctypes.data_as(api._i32p), tok.size,
+                                                       logits.ctypes.data_as(api._fp), ctypes.byref(pos)),
+                    "pickle_cuda_forward_slot")
+        return logits, pos.value
+
+    def forward_batch_dev(self, tokens_dev, pos_dev, slot_dev, max_pos, logits_dev, next_dev=None, stream=None):
+        """One decode step of n sequences (device int32 tokens / positions /
+        slots [n], f32 logits [n][vocab], optional int32 argmax ids [n])."""
+        self._check(api.lib().pickle_cuda_forward_batch_dev(self._h, tokens_dev.numel(), api._ptr(tokens_dev),
+                                                            api._ptr(pos_dev), api._ptr(slot_dev), int(max_pos),
+                                                            api._ptr(logits_dev), api._ptr(next_dev),
+                                                            api._stream(stream)), "pickle_cuda_forward_batch_dev")
+
+    def generate_batch(self, prompts, n_gen, eos_id=-1):
+        """Greedy generation of many requests with continuous batching: up to
+        n_seqs requests hold a cache slot each; every step decodes all of them
+        together (forward_batch_dev); a finished request frees its slot and
+        the next waiting prompt is admitted (its prompt runs into that slot,
+        forward_slot). Each request's ids are those generate(prompt, n_gen,
+        eos_id) gives. -> list of id arrays, in the order of prompts."""
+        import torch
+        dev = torch.device("cuda", self.device)
+        waiting = list(range(len(prompts)))[::-1]
+        free = list(range(self.n_seqs))[::-1]
+        ids = [[] for _ in prompts]
+        slot, pos, cur = {}, {}, {}
+        active = []
+
+        def done(r):
+            return (len(ids[r]) >= n_gen or (eos_id >= 0 and ids[r][-1] == eos_id) or pos[r] >= self.max_seq)
+
+        def admit():
+            while waiting and free:
+                r = waiting.pop()
+                if n_gen <= 0:
+                    continue
+                s = free.pop()
+                logits, p = self.forward_slot(s, prompts[r], 0)
+                slot[r], pos[r] = s, p
+                ids[r].append(int(np.argmax(logits)))
+                if done(r):
+                    free.append(s)
+                else:
+                    active.append(r)
+
+        logits_dev = torch.empty((self.n_seqs, self.VS), device=dev)
+        next_dev = torch.empty(self.n_seqs, dtype=torch.int32, device=dev)
+        admit()
+        while active:
+            n = len(active)
+            host = np.array([[ids[r][-1] for r in active], [pos[r] for r in active], [slot[r] for r in active]],
+                            np.int32)
+            d = torch.from_numpy(host).to(dev)
+            self.forward_batch_dev(d[0], d[1], d[2], int(host[1].max()), logits_dev[:n], next_dev[:n])
+            nxt = next_dev[:n].cpu().numpy()
+            self.sync()
+            still = []
+            for r, t in zip(active, nxt):
+                pos[r] += 1
+                ids[r].append(int(t))
+                if done(r):
+                    free.append(slot[r])
+                else:
+                    still.append(r)
+            active[:] = still
+            admit()
+        return [np.array(x, np.int32) for x in ids]
 
     def forward_dev(self, tokens_dev, pos0, logits_dev, next_dev=None, stream=None):
         """Asynchronous forward on device buffers (int32 tokens, f32 logits [vocab])."""

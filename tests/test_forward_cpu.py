@@ -78,7 +78,7 @@ def test_gguf_rejects_bad_files(tmp_path):
 def test_model_params_layout_matches_header(tmp_path):
     src = tmp_path / "layout.c"
     fields = ["rope_inv_freq", "max_tokens", "prefill_precision", "weights_on_device", "token_embd", "output_norm",
-              "output", "layers"]
+              "output", "layers", "n_seqs"]
     src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include <stdint.h>\n#include \"pickle_cuda.h\"\n"
                    "int main(void){printf(\"%zu %zu %zu\", sizeof(pickle_cuda_tensor_t),"
                    " offsetof(pickle_cuda_tensor_t, nbytes), sizeof(pickle_cuda_model_params_t));"

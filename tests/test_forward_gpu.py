@@ -13,6 +13,10 @@ against the reference's own forward.
   reference's own forward (oracle/_ref/pickle_e2e_ref, the unmodified
   src/pickle_fast.c) run on the same GGUF file.
 
+* Continuous batching through the model (n_seqs cache slots,
+  pickle_cuda_forward_slot / pickle_cuda_forward_batch_dev): each request's
+  ids and each row's logits against the single-sequence path.
+
 Bars: greedy ids identical; final logits within 1e-4 of the largest logit.
 """
 import os
@@ -212,3 +216,68 @@ def test_bf16_prefill_logits(quant_dir):
     m32.close()
     m16.close()
     assert_rel(l16, l32, tol=BF16_ABS_TOL, what="bf16 prompt logits")
+
+
+def _prompts(n, vocab, seed=11):
+    rng = np.random.default_rng(seed)
+    return [[int(t) for t in rng.integers(3, vocab, size=int(rng.integers(5, 21)))] for _ in range(n)]
+
+
+def test_generate_batch_matches_single(tiny, tiny_model, golden_e2e):
+    """Continuous batching through the whole model: 5 requests on 3 cache
+    slots (later prompts are admitted into the slots earlier ones free);
+    every request gets the ids that a single-sequence generate gives, and the
+    golden prompt gets the reference's."""
+    single, prompt = tiny
+    path, _ = tiny_model
+    prompts = [prompt] + _prompts(4, single.VS)
+    n_gen = [30, 30, 30, 30, 30]
+    mb = PickleModel.from_gguf(path, max_tokens=64, n_seqs=3)
+    got = mb.generate_batch(prompts, 30)
+    np.testing.assert_array_equal(got[0], golden_e2e["ids"][:30])
+    for i, p in enumerate(prompts):
+        want, _, _ = single.generate(p, n_gen[i])
+        np.testing.assert_array_equal(got[i], want, err_msg=f"request {i}")
+    # with an eos id: each request stops after its first occurrence
+    eos = int(golden_e2e["ids"][5])
+    got = mb.generate_batch(prompts, 30, eos_id=eos)
+    for i, p in enumerate(prompts):
+        want, _, _ = single.generate(p, 30, eos_id=eos)
+        np.testing.assert_array_equal(got[i], want, err_msg=f"request {i} with eos")
+    mb.close()
+
+
+def test_forward_batch_rows_match_single_steps(quant_dir):
+    """One batched decode step of 12 sequences (more than 8 rows: the
+    projections run as GEMMs) on a Q4_K_M-like model: each row's logits
+    equal that sequence's own step within the library's 1e-4 bar."""
+    path = str(quant_dir / "batch.gguf")
+    mq.write_model(path, "q4_k_m", seed=2)
+    n = 12
+    mb = PickleModel.from_gguf(path, max_tokens=32, n_seqs=n)
+    ms = PickleModel.from_gguf(path, max_tokens=32)
+    prompts = _prompts(n, mb.VS, seed=5)
+    toks = [int(t) for t in np.random.default_rng(6).integers(3, mb.VS, size=n)]
+    slots = list(range(n))[::-1]                       # slots in another order than the rows
+    for p, s in zip(prompts, slots):
+        mb.forward_slot(s, p, 0)
+    host = np.array([toks, [len(p) for p in prompts], slots], np.int32)
+    d = torch.from_numpy(host).to(DEV)
+    logits = torch.empty((n, mb.VS), device=DEV)
+    nxt = torch.empty(n, dtype=torch.int32, device=DEV)
+    mb.forward_batch_dev(d[0], d[1], d[2], int(host[1].max()), logits, nxt)
+    mb.sync()
+    got = logits.cpu().numpy()
+    for i, p in enumerate(prompts):
+        ms.forward(p, 0)
+        want, _ = ms.forward([toks[i]], len(p))
+        assert_rel(got[i], want, what=f"row {i}")
+        assert int(nxt[i].item()) == int(np.argmax(got[i]))
+    with pytest.raises(PickleError) as e:
+        mb.forward_slot(n, prompts[0], 0)
+    assert e.value.code == -7
+    with pytest.raises(PickleError) as e:
+        ms.forward_batch_dev(d[0], d[1], d[2], int(host[1].max()), logits, nxt)   # 12 rows, 1 slot
+    assert e.value.code == -7
+    mb.close()
+    ms.close()
