@@ -404,6 +404,43 @@ def matmul_line(device, steps, warmup, types=("Q4_K", "Q8_0", "F16")):
             "note": "per call: x hi/lo split + per-row weight scales (pre-passes) + GEMM"}
 
 
+def matmul_batch_line(device, steps, warmup, shape=(28672, 4096, 32)):
+    """The GEMM on a decode batch: Llama-3-8B gate|up (Q4_K) for 32 tokens,
+    two weight copies used in turn (132 MB, above L2): us per call and the
+    weight stream in GB/s."""
+    torch = _torch()
+    from lestramanika_b200 import api
+    out_n, in_n, n_tok = shape
+    dev = torch.device("cuda", device)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(13)
+    t = api.GGML_Q4_K
+    wbytes = api.matvec_row_bytes(t, in_n) * out_n
+    Ws = []
+    for _ in range(2):
+        W = torch.randint(0, 256, (wbytes,), device=dev, dtype=torch.uint8, generator=gen)
+        b = W.view(-1, 144)
+        for off in (0, 2):
+            sc = (torch.rand((b.shape[0],), device=dev, generator=gen) * 2e-4 + 1e-4).half()
+            b[:, off:off + 2] = sc.view(torch.uint8).view(-1, 2)
+        Ws.append(W)
+    x = torch.randn((n_tok, in_n), device=dev, generator=gen)
+    y = torch.empty((n_tok, out_n), device=dev)
+    ws = torch.empty(api.matmul_workspace(out_n, in_n, n_tok), dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream()
+    for i in range(warmup):
+        api.matmul_dev(t, Ws[i % 2], out_n, in_n, x, y, n_tok, workspace=ws, stream=st)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(steps):
+        api.matmul_dev(t, Ws[i % 2], out_n, in_n, x, y, n_tok, workspace=ws, stream=st)
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / steps * 1e3
+    return {"shape": f"{out_n}x{in_n} Q4_K, {n_tok} tokens", "us_per_call": us, "weight_GBps": wbytes / us / 1e3}
+
+
 def matmul_cpu_baseline(types=("Q4_K", "Q8_0", "F16"), seconds=2.0):
     """The reference's own per-token projection (oracle/_ref matvec kernels,
     OpenMP on the host cores) on the QKV shape: ms per token, a bounded
@@ -971,7 +1008,7 @@ C4_SMALL = Decode("llama3-70b decode B=2 ctx=32768 (profiling size)", 2, 64, 8, 
 ONLY = {"c2b1": (C2_B1, True), "c2b8": (C2_B8, False), "c2b64": (C2_B64, False), "c4": (C4, False),
         "c4s": (C4_SMALL, False), "c5": (C5, False), "c3": (C3, None), "mv": (None, None), "mm": (None, None),
         "pl": (None, None), "fw": (None, None), "fwd": (None, None), "fwb": (None, None),
-        "fwb32": (None, None)}
+        "fwb32": (None, None), "mmb": (None, None)}
 
 
 def run_only(args):
@@ -997,6 +1034,8 @@ def run_only(args):
         line = forward_decode_line(0, args.steps, args.warmup)
     elif args.only == "fwb":
         line = forward_batch_line(0, args.steps, args.warmup)
+    elif args.only == "mmb":
+        line = matmul_batch_line(0, args.steps, args.warmup)
     elif args.only == "fwb32":
         line = forward_batch_line(0, args.steps, args.warmup, batches=(32,))
     elif args.only == "mm":

@@ -49,6 +49,11 @@ constexpr int A_STAGES = 2, X_STAGES = 3, RAW_STAGES = 2;
 constexpr int TILE = 128 * 128;                       // bytes of one 128 x 64 f16 weight tile
 constexpr int THREADS = 320;
 inline int bn_for(int n_tok) { return n_tok <= 32 ? 32 : n_tok <= 64 ? 64 : 128; }
+// Warps: producer, MMA, DQW dequantizing (one thread per weight row), 4 epilogue.
+template <int BNT> struct Cfg {
+    static constexpr int DQW = 4;
+    static constexpr int THREADS = 32 * (2 + DQW + 4);
+};
 
 // Raw weight bytes of one 256-element K-block per row (the TMA box width).
 template <int TYPE> struct Raw;
@@ -67,15 +72,22 @@ PCU_DEV int raw_x(int kb) {
     else return kb * (Raw<TYPE>::B / 8);
 }
 
-constexpr int OFF_A = 0;                                  // [A_STAGES][hi, lo] tiles
-constexpr int OFF_X = OFF_A + A_STAGES * 2 * TILE;        // [XS][hi, lo] tiles
+constexpr int OFF_A = 0;                                  // [AS][hi, lo] weight tiles
 template <int TYPE, int BNT> struct Lay {
     static constexpr int XT = BNT * 128;                             // bytes of one BNT x 64 f16 x tile
     static constexpr int XS = Raw<TYPE>::B > 240 && BNT == 128 ? 2 : X_STAGES;   // x ring depth that fits
-    static constexpr int OFF_RAW = OFF_X + XS * 2 * XT;              // [RAW_STAGES][BM][Raw::B]
-    static constexpr int OFF_BAR = OFF_RAW + RAW_STAGES * BM * Raw<TYPE>::B;
+    static constexpr int AS = A_STAGES;                              // weight-tile (hi, lo) ring
+    // Raw weight ring (K-blocks in flight from HBM). A wide token tile has
+    // enough tensor work per K-block to hide the latency of two; a narrow
+    // one (a decode batch) streams weights and takes as many as fit, up to 6.
+    static constexpr int FIXED = XS * 2 * XT + AS * 2 * TILE + 2048;
+    static constexpr int RS_FIT = Raw<TYPE>::B ? (232448 - FIXED) / (BM * Raw<TYPE>::B) : RAW_STAGES;
+    static constexpr int RS = BNT == 128 || Raw<TYPE>::B == 0 ? RAW_STAGES : RS_FIT > 6 ? 6 : RS_FIT;
+    static constexpr int OFF_X = OFF_A + AS * 2 * TILE;              // [XS][hi, lo] x tiles
+    static constexpr int OFF_RAW = OFF_X + XS * 2 * XT;              // [RS][BM][Raw::B]
+    static constexpr int OFF_BAR = OFF_RAW + RS * BM * Raw<TYPE>::B;
     // RAW_FULL[2], RAW_EMPTY[2], A_FULL[2], A_EMPTY[2], X_FULL[XS], X_EMPTY[XS], D_FULL
-    static constexpr int N_BARS = 2 * RAW_STAGES + 2 * A_STAGES + 2 * XS + 1;
+    static constexpr int N_BARS = 2 * RS + 2 * AS + 2 * XS + 1;
     static constexpr int OFF_TMEM = OFF_BAR + N_BARS * 8;
     static constexpr int BYTES = OFF_TMEM + 16 + 1024;     // + alignment slack of the 1024-byte base
     static_assert(BYTES <= 232448, "dynamic shared memory of one CTA on sm_100");
@@ -322,7 +334,7 @@ PCU_DEV void dequant_kstep(uint32_t rw, int kb, int ks, float rsc, float (&w)[64
 // ------------------------------------------------------------------- kernel
 
 template <int TYPE, int BNT>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(Cfg<BNT>::THREADS, 1)
     matmul_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xh,
                      const __grid_constant__ CUtensorMap tm_xl, int out_n, int in_n, int n_tok,
                      const float* __restrict__ xinv, const float* __restrict__ rowsc, float* __restrict__ y,
@@ -331,6 +343,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     constexpr int XT = L::XT, TMEM_COLS = BNT;
     constexpr uint32_t ID = idesc<BNT>();
     constexpr bool QUANT = TYPE != F_F16;
+    constexpr int DQW = Cfg<BNT>::DQW;
+    constexpr int A_STAGES = L::AS, OFF_X = L::OFF_X, RAW_STAGES = L::RS;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     uint8_t* smem = smem_raw + (base - smem_u32(smem_raw));
@@ -351,10 +365,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
         for (int i = 0; i < RAW_STAGES; ++i) {
             mbar_init(&bars[i], 1);
-            mbar_init(&bars[RAW_STAGES + i], 128);
+            mbar_init(&bars[RAW_STAGES + i], DQW);
         }
         for (int i = 0; i < A_STAGES; ++i) {
-            mbar_init(&bars[2 * RAW_STAGES + i], QUANT ? 128 : 1);
+            mbar_init(&bars[2 * RAW_STAGES + i], QUANT ? DQW : 1);
             mbar_init(&bars[2 * RAW_STAGES + A_STAGES + i], 1);
         }
         for (int i = 0; i < L::XS; ++i) {
@@ -429,7 +443,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             umma_commit(D_FULL);
         }
-    } else if (warp < 6) {
+    } else if (warp < 2 + DQW) {
         // ----------------------------------------------------------- dequant
         if constexpr (QUANT) {
             const int r = threadIdx.x - 64;                 // weight row within the tile
@@ -445,27 +459,32 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const int s = kl * (KB / BK) + ks, as = s % A_STAGES;
                     if (s >= A_STAGES)
                         mvtc::wait_or_flag(A_EMPTY + 8 * as, ((s / A_STAGES) - 1) & 1, PCU_DEVERR_EMPTY_WAIT);
-                    float w[64];                              // the K-step's 64 weights of row r, scaled
-                    dequant_kstep<TYPE>(rw, kb, ks, rsc, w);
                     // hi / lo tiles, row r: 8 chunks of 8 f16, chunk c at (c ^ (r & 7)).
                     const uint32_t ah = base + OFF_A + (2 * as) * TILE + r * 128, al = ah + TILE;
-                    #pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        uint4 hv, lv;
-                        split2(w[8 * c + 0], w[8 * c + 1], hv.x, lv.x);
-                        split2(w[8 * c + 2], w[8 * c + 3], hv.y, lv.y);
-                        split2(w[8 * c + 4], w[8 * c + 5], hv.z, lv.z);
-                        split2(w[8 * c + 6], w[8 * c + 7], hv.w, lv.w);
+                    auto put = [&](const float* w, int c) {
+                        uint4 hv4, lv4;
+                        split2(w[0], w[1], hv4.x, lv4.x);
+                        split2(w[2], w[3], hv4.y, lv4.y);
+                        split2(w[4], w[5], hv4.z, lv4.z);
+                        split2(w[6], w[7], hv4.w, lv4.w);
                         const uint32_t off = (uint32_t)((c ^ (r & 7)) << 4);
                         asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};"
-                                     ::"r"(ah + off), "r"(hv.x), "r"(hv.y), "r"(hv.z), "r"(hv.w) : "memory");
+                                     ::"r"(ah + off), "r"(hv4.x), "r"(hv4.y), "r"(hv4.z), "r"(hv4.w) : "memory");
                         asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};"
-                                     ::"r"(al + off), "r"(lv.x), "r"(lv.y), "r"(lv.z), "r"(lv.w) : "memory");
-                    }
+                                     ::"r"(al + off), "r"(lv4.x), "r"(lv4.y), "r"(lv4.z), "r"(lv4.w) : "memory");
+                    };
+                    float w[64];                              // the K-step's 64 weights of row r, scaled
+                    dequant_kstep<TYPE>(rw, kb, ks, rsc, w);
+                    #pragma unroll
+                    for (int c = 0; c < 8; ++c) put(w + 8 * c, c);
+                    // each thread's tile writes are made visible to the tensor
+                    // core (async proxy); then one arrival per warp
                     fence_async_smem();
-                    mvtc::mbar_arrive_a(A_FULL + 8 * as);
+                    __syncwarp();
+                    if (lane == 0) mvtc::mbar_arrive_a(A_FULL + 8 * as);
                 }
-                mvtc::mbar_arrive_a(RAW_EMPTY + 8 * rs);
+                __syncwarp();
+                if (lane == 0) mvtc::mbar_arrive_a(RAW_EMPTY + 8 * rs);
             }
         }
     } else {
@@ -475,6 +494,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         mvtc::wait_or_flag(D_FULL, 0, PCU_DEVERR_MMA_WAIT);
         tc_after();
         const float rinv = (QUANT && m < out_n) ? 1.f / __ldg(rowsc + m) : 1.f;
+        // y, or this K slice's partial outputs [n_tok][out_n]
+        float* dst = part ? part + (size_t)blockIdx.z * n_tok * out_n : y;
         #pragma unroll 1
         for (int c = 0; c < BNT / 32; ++c) {
             float v[32];
@@ -482,11 +503,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             #pragma unroll
             for (int j = 0; j < 32; ++j) {
                 const int n = n0 + 32 * c + j;
-                if (m < out_n && n < n_tok) {
-                    const float o = v[j] * rinv * __ldg(xinv + n);
-                    if (part) part[((size_t)blockIdx.z * n_tok + n) * out_n + m] = o;
-                    else y[(size_t)n * out_n + m] = o;
-                }
+                if (m < out_n && n < n_tok) dst[(size_t)n * out_n + m] = v[j] * rinv * __ldg(xinv + n);
             }
         }
     }
@@ -610,7 +627,7 @@ inline cudaError_t launch_bn(const uint8_t* W, size_t row_bytes, int out_n, int 
         attr[dev] = true;
     }
     const dim3 grid((unsigned)((out_n + BM - 1) / BM), (unsigned)((n_tok + BNT - 1) / BNT), (unsigned)ks);
-    matmul_tc_kernel<TYPE, BNT><<<grid, THREADS, Lay<TYPE, BNT>::BYTES, st>>>(tw, th, tl, out_n, in_n, n_tok, xinv,
+    matmul_tc_kernel<TYPE, BNT><<<grid, Cfg<BNT>::THREADS, Lay<TYPE, BNT>::BYTES, st>>>(tw, th, tl, out_n, in_n, n_tok, xinv,
                                                                               rowsc, y, part);
     if (ks > 1) {
         const size_t total = (size_t)n_tok * out_n;
