@@ -169,6 +169,8 @@ PCU_DEV void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
 // s per token (its largest |x| just below 2^15); xinv[n] = 2^-s.
 __global__ void __launch_bounds__(256) xsplit_kernel(const float* __restrict__ x, int in_n, __half* __restrict__ xh,
                                                      __half* __restrict__ xl, float* __restrict__ xinv) {
+    griddep_launch_dependents();
+    griddep_wait();                       // x may come from the kernel before
     __shared__ float red[8];
     const int n = blockIdx.x, tid = threadIdx.x;
     const float* xr = x + (size_t)n * in_n;
@@ -387,6 +389,11 @@ __global__ void __launch_bounds__(Cfg<BNT>::THREADS, 1)
     __syncthreads();
     tc_after();
     const uint32_t tmem = *tmem_slot;
+    // Launched with programmatic stream serialization: the set-up above ran
+    // while the kernel before finished; x, its scales and the row scales may
+    // come from that kernel.
+    griddep_launch_dependents();
+    griddep_wait();
 
     if (warp == 0) {
         // ---------------------------------------------------------- producer
@@ -516,6 +523,8 @@ __global__ void __launch_bounds__(Cfg<BNT>::THREADS, 1)
 // Sum of the split-K slices' partial outputs, in slice order:
 // y[i] = part[0][i] + part[1][i] + ... (i over n_tok * out_n).
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int ks, size_t total, float* __restrict__ y) {
+    griddep_launch_dependents();
+    griddep_wait();
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
         float a = part[i];
@@ -525,6 +534,24 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int ks, siz
 }
 
 // ---------------------------------------------------------------- host side
+
+// Launch with programmatic stream serialization (the kernels above wait
+// with griddepcontrol.wait before they read their inputs).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
 
 inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
@@ -605,7 +632,8 @@ inline cudaError_t launch_bn(const uint8_t* W, size_t row_bytes, int out_n, int 
     float* part = ks > 1 ? reinterpret_cast<float*>(p + 2 * plane + align256((size_t)n_tok * 4) +
                                                     align256((size_t)out_n * 4))
                          : nullptr;
-    xsplit_kernel<<<n_tok, 256, 0, st>>>(x, in_n, xh, xl, xinv);
+    if (launch_pdl(xsplit_kernel, dim3(n_tok), dim3(256), 0, st, x, in_n, xh, xl, xinv) != cudaSuccess)
+        return cudaGetLastError();
     if constexpr (TYPE != F_F16) {
         // the row scales of constant weights may come precomputed
         if (rowsc_pre) rowsc = const_cast<float*>(rowsc_pre);
@@ -627,12 +655,14 @@ inline cudaError_t launch_bn(const uint8_t* W, size_t row_bytes, int out_n, int 
         attr[dev] = true;
     }
     const dim3 grid((unsigned)((out_n + BM - 1) / BM), (unsigned)((n_tok + BNT - 1) / BNT), (unsigned)ks);
-    matmul_tc_kernel<TYPE, BNT><<<grid, Cfg<BNT>::THREADS, Lay<TYPE, BNT>::BYTES, st>>>(tw, th, tl, out_n, in_n, n_tok, xinv,
-                                                                              rowsc, y, part);
+    cudaError_t e = launch_pdl(matmul_tc_kernel<TYPE, BNT>, grid, dim3(Cfg<BNT>::THREADS), (size_t)Lay<TYPE, BNT>::BYTES,
+                               st, tw, th, tl, out_n, in_n, n_tok, (const float*)xinv, (const float*)rowsc, y, part);
+    if (e != cudaSuccess) return e;
     if (ks > 1) {
         const size_t total = (size_t)n_tok * out_n;
         const unsigned blocks = (unsigned)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
-        splitk_reduce_kernel<<<blocks, 256, 0, st>>>(part, ks, total, y);
+        e = launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, st, (const float*)part, ks, total, y);
+        if (e != cudaSuccess) return e;
     }
     return cudaGetLastError();
 }
