@@ -20,10 +20,12 @@
 // each projection as one GEMM (pickle_cuda_matmul_dev) and through the
 // attention block as one causal prefill (pickle_cuda_prefill_dev); a decode
 // step (T = 1) uses the matvec and the split-KV decode. The elementwise work
-// of the reference's loop is fused into four small kernels below (norm with
-// the residual add before it, embedding with the first norm, SwiGLU, argmax).
-// The greedy loop feeds each argmax id back on the device, so a generation
-// of n tokens needs no host round trip per token.
+// of the reference's loop is fused into small kernels below (norm with the
+// residual add before it, embedding with the first norm, SwiGLU, argmax,
+// the temperature / top-p sampler). The decode loop feeds each chosen id
+// back on the device, so a generation of n tokens needs no host round trip
+// per token. With n_seqs cache slots, one step can also decode many
+// sequences together, each at its own position (continuous batching).
 #include "pickle_cuda.h"
 
 #include <cuda_fp16.h>
@@ -31,7 +33,6 @@
 
 #include <cmath>
 #include <cstdint>
-#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <new>

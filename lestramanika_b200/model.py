@@ -147,7 +147,7 @@ class PickleModel:
         forward_slot). Each request's ids are those generate(prompt, n_gen,
         eos_id) gives. -> list of id arrays, in the order of prompts."""
         import torch
-        dev = torch.device("cuda", self.device)
+        dev = self._torch_device()
         waiting = list(range(len(prompts)))[::-1]
         free = list(range(self.n_seqs))[::-1]
         ids = [[] for _ in prompts]
@@ -193,6 +193,10 @@ class PickleModel:
             active[:] = still
             admit()
         return [np.array(x, np.int32) for x in ids]
+
+    def _torch_device(self):
+        import torch
+        return torch.device("cuda", self.device)
 
     def forward_dev(self, tokens_dev, pos0, logits_dev, next_dev=None, stream=None):
         """Asynchronous forward on device buffers (int32 tokens, f32 logits [vocab])."""
