@@ -814,10 +814,15 @@ inline cudaError_t launch(const uint8_t* W, size_t row_bytes, int out_n, int in_
                           float* y, cudaStream_t st, bool w_early = false) {
     alignas(64) CUtensorMap tm;
     if (make_w_map<TYPE>(&tm, W, row_bytes, out_n) != 0) return cudaErrorInvalidValue;
-    // Vectors go in passes of as many as fit in shared memory.
+    // Vectors go in passes of at most as many as fit in shared memory, the
+    // same number in each pass (8 that fit 7 at a time go as 4 + 4, not
+    // 7 + 1): as many passes over W, and narrower passes keep more
+    // consumer warps.
+    const int fit = fit_nv<TYPE>(in_n);
+    const int passes = (n_vec + fit - 1) / fit;
+    const int per = (n_vec + passes - 1) / passes;
     for (int v0 = 0; v0 < n_vec;) {
-        int nv = n_vec - v0 < 8 ? n_vec - v0 : 8;
-        while (nv > 1 && smem_layout<TYPE>(in_n, nv, consumer_warps(TYPE, nv)).bytes > kSmemLimit) --nv;
+        const int nv = n_vec - v0 < per ? n_vec - v0 : per;
         const float* xv = x + (size_t)v0 * in_n;
         float* yv = y + (size_t)v0 * out_n;
         cudaError_t e = cudaSuccess;
