@@ -35,7 +35,10 @@ class _Reader:
         self.buf, self.off = buf, 0
 
     def take(self, fmt):
-        v = struct.unpack_from(fmt, self.buf, self.off)[0]
+        try:
+            v = struct.unpack_from(fmt, self.buf, self.off)[0]
+        except struct.error as e:
+            raise GGUFError(f"file ends inside the header ({e})") from None
         self.off += struct.calcsize(fmt)
         return v
 

@@ -74,6 +74,16 @@ def test_gguf_rejects_bad_files(tmp_path):
         gguf.read(str(p))
 
 
+def test_gguf_rejects_truncated_files(tmp_path, tiny_model):
+    path, _ = tiny_model
+    data = open(path, "rb").read()
+    for cut in (10, 200, 3000, len(data) - 100):     # in the header, the tensor infos, the data
+        p = tmp_path / f"cut{cut}.gguf"
+        p.write_bytes(data[:cut])
+        with pytest.raises(gguf.GGUFError):
+            gguf.read(str(p))
+
+
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="needs gcc")
 def test_model_params_layout_matches_header(tmp_path):
     src = tmp_path / "layout.c"
