@@ -507,10 +507,21 @@ __global__ void __launch_bounds__(Cfg<BNT>::THREADS, 1)
         for (int c = 0; c < BNT / 32; ++c) {
             float v[32];
             tmem_ld32x(tmem + ((uint32_t)(32 * q) << 16) + 32 * c, v);
-            #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int n = n0 + 32 * c + j;
-                if (m < out_n && n < n_tok) dst[(size_t)n * out_n + m] = v[j] * rinv * __ldg(xinv + n);
+            // the chunk's 32 token scales: one load per lane, shared by shuffles
+            const int nl = n0 + 32 * c + lane;
+            const float xs = nl < n_tok ? __ldg(xinv + nl) : 0.f;
+            float* d = dst + (size_t)(n0 + 32 * c) * out_n + m;
+            // warp-uniform test: all 32 rows and all 32 tokens in range
+            if (m0 + 32 * q + 32 <= out_n && n0 + 32 * c + 32 <= n_tok) {
+                #pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    d[(size_t)j * out_n] = v[j] * rinv * __shfl_sync(0xffffffffu, xs, j);
+            } else {
+                #pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float sj = __shfl_sync(0xffffffffu, xs, j);
+                    if (m < out_n && n0 + 32 * c + j < n_tok) d[(size_t)j * out_n] = v[j] * rinv * sj;
+                }
             }
         }
     }
