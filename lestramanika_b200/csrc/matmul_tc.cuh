@@ -86,8 +86,9 @@ template <int TYPE, int BNT> struct Lay {
     static constexpr int OFF_X = OFF_A + AS * 2 * TILE;              // [XS][hi, lo] x tiles
     static constexpr int OFF_RAW = OFF_X + XS * 2 * XT;              // [RS][BM][Raw::B]
     static constexpr int OFF_BAR = OFF_RAW + RS * BM * Raw<TYPE>::B;
-    // RAW_FULL[2], RAW_EMPTY[2], A_FULL[2], A_EMPTY[2], X_FULL[XS], X_EMPTY[XS], D_FULL
-    static constexpr int N_BARS = 2 * RS + 2 * AS + 2 * XS + 1;
+    // RAW_FULL[RS], RAW_EMPTY[RS], A_FULL[AS], A_EMPTY[AS], X_FULL[XS], X_EMPTY[XS],
+    // D_FULL[2], ACC_EMPTY[2] (the two TMEM accumulators)
+    static constexpr int N_BARS = 2 * RS + 2 * AS + 2 * XS + 4;
     static constexpr int OFF_TMEM = OFF_BAR + N_BARS * 8;
     static constexpr int BYTES = OFF_TMEM + 16 + 1024;     // + alignment slack of the 1024-byte base
     static_assert(BYTES <= 232448, "dynamic shared memory of one CTA on sm_100");
@@ -342,7 +343,7 @@ __global__ void __launch_bounds__(Cfg<BNT>::THREADS, 1)
                      const float* __restrict__ xinv, const float* __restrict__ rowsc, float* __restrict__ y,
                      float* __restrict__ part) {
     using L = Lay<TYPE, BNT>;
-    constexpr int XT = L::XT, TMEM_COLS = BNT;
+    constexpr int XT = L::XT, TMEM_COLS = 2 * BNT;   // two accumulators: tile i+1 while tile i drains
     constexpr uint32_t ID = idesc<BNT>();
     constexpr bool QUANT = TYPE != F_F16;
     constexpr int DQW = Cfg<BNT>::DQW;
@@ -353,12 +354,17 @@ __global__ void __launch_bounds__(Cfg<BNT>::THREADS, 1)
     const uint32_t bar0 = base + L::OFF_BAR;
     const uint32_t RAW_FULL = bar0, RAW_EMPTY = bar0 + 8 * RAW_STAGES, A_FULL = RAW_EMPTY + 8 * RAW_STAGES,
                    A_EMPTY = A_FULL + 8 * A_STAGES, X_FULL = A_EMPTY + 8 * A_STAGES,
-                   X_EMPTY = X_FULL + 8 * L::XS, D_FULL = X_EMPTY + 8 * L::XS;
+                   X_EMPTY = X_FULL + 8 * L::XS, D_FULL = X_EMPTY + 8 * L::XS, ACC_EMPTY = D_FULL + 16;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_TMEM);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BNT;
+    // Output tiles: a CTA takes tiles blockIdx.x, blockIdx.x + gridDim.x, ...
+    // (tile t: weight rows (t % n_mt) * BM, tokens (t / n_mt) * BNT), so the
+    // epilogue of one tile overlaps the main loop of the next. Every ring
+    // counts its stages on across the tiles.
+    const int n_mt = (out_n + BM - 1) / BM;
+    const int total = n_mt * ((n_tok + BNT - 1) / BNT);
     // Split K: this CTA takes K-blocks [kb0, kb0 + nkb) of slice blockIdx.z
-    // (the host makes every slice non-empty); stages are numbered within it.
+    // (the host makes every slice non-empty and then gives each CTA one tile).
     const int nkb_all = in_n / KB;
     const int kb0 = (int)blockIdx.z * nkb_all / (int)gridDim.z;
     const int nkb = ((int)blockIdx.z + 1) * nkb_all / (int)gridDim.z - kb0, nks = nkb * (KB / BK);
@@ -377,7 +383,10 @@ __global__ void __launch_bounds__(Cfg<BNT>::THREADS, 1)
             mbar_init(&bars[2 * RAW_STAGES + 2 * A_STAGES + i], 1);
             mbar_init(&bars[2 * RAW_STAGES + 2 * A_STAGES + L::XS + i], 1);
         }
-        mbar_init(&bars[L::N_BARS - 1], 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bars[L::N_BARS - 4 + i], 1);   // D_FULL: the MMAs of a tile are done
+            mbar_init(&bars[L::N_BARS - 2 + i], 4);   // ACC_EMPTY: the 4 epilogue warps read it out
+        }
         mbar_fence_init();
     }
     if (warp == 1) {
@@ -399,8 +408,11 @@ __global__ void __launch_bounds__(Cfg<BNT>::THREADS, 1)
         // ---------------------------------------------------------- producer
         if (lane == 0) {
             #pragma unroll 1
-            for (int kl = 0; kl < nkb; ++kl) {
-                const int kb = kb0 + kl;
+            for (int t = blockIdx.x, it = 0; t < total; t += gridDim.x, ++it) {
+            const int m0 = (t % n_mt) * BM, n0 = (t / n_mt) * BNT;
+            #pragma unroll 1
+            for (int kl0 = 0; kl0 < nkb; ++kl0) {
+                const int kb = kb0 + kl0, kl = it * nkb + kl0;   // kl: K-block count across tiles
                 if constexpr (QUANT) {
                     const int rs = kl % RAW_STAGES;
                     if (kl >= RAW_STAGES)
@@ -426,12 +438,24 @@ __global__ void __launch_bounds__(Cfg<BNT>::THREADS, 1)
                     }
                 }
             }
+            }
         }
     } else if (warp == 1) {
         // --------------------------------------------------------------- MMA
         if (lane == 0) {
             #pragma unroll 1
-            for (int s = 0; s < nks; ++s) {
+            for (int t = blockIdx.x, it = 0; t < total; t += gridDim.x, ++it) {
+            // accumulator it & 1; before reusing it, the epilogue must have
+            // read out the tile two before this one
+            const int buf = it & 1;
+            const uint32_t acc = tmem + (uint32_t)(buf * BNT);
+            if (it >= 2) {
+                mvtc::wait_or_flag(ACC_EMPTY + 8 * buf, ((it >> 1) - 1) & 1, PCU_DEVERR_EMPTY_WAIT);
+                tc_after();
+            }
+            #pragma unroll 1
+            for (int s0 = 0; s0 < nks; ++s0) {
+                const int s = it * nks + s0;                // step count across tiles
                 const int as = s % A_STAGES, xs = s % L::XS;
                 mvtc::wait_or_flag(A_FULL + 8 * as, (s / A_STAGES) & 1, PCU_DEVERR_FULL_WAIT);
                 mvtc::wait_or_flag(X_FULL + 8 * xs, (s / L::XS) & 1, PCU_DEVERR_FULL_WAIT);
@@ -441,23 +465,27 @@ __global__ void __launch_bounds__(Cfg<BNT>::THREADS, 1)
                 #pragma unroll
                 for (int k = 0; k < BK / 16; ++k) {
                     const uint32_t o = 32 * k;        // 16 f16 of a 128-byte swizzled row
-                    umma(tmem, sdesc(ah + o), sdesc(xh + o), (s | k) != 0, ID);
-                    umma(tmem, sdesc(ah + o), sdesc(xl + o), 1, ID);
-                    if constexpr (QUANT) umma(tmem, sdesc(al + o), sdesc(xh + o), 1, ID);
+                    umma(acc, sdesc(ah + o), sdesc(xh + o), (s0 | k) != 0, ID);
+                    umma(acc, sdesc(ah + o), sdesc(xl + o), 1, ID);
+                    if constexpr (QUANT) umma(acc, sdesc(al + o), sdesc(xh + o), 1, ID);
                 }
                 umma_commit(A_EMPTY + 8 * as);
                 umma_commit(X_EMPTY + 8 * xs);
             }
-            umma_commit(D_FULL);
+            umma_commit(D_FULL + 8 * buf);
+            }
         }
     } else if (warp < 2 + DQW) {
         // ----------------------------------------------------------- dequant
         if constexpr (QUANT) {
             const int r = threadIdx.x - 64;                 // weight row within the tile
+            #pragma unroll 1
+            for (int t = blockIdx.x, it = 0; t < total; t += gridDim.x, ++it) {
+            const int m0 = (t % n_mt) * BM;
             const float rsc = (m0 + r < out_n) ? __ldg(rowsc + m0 + r) : 1.f;
             #pragma unroll 1
-            for (int kl = 0; kl < nkb; ++kl) {
-                const int kb = kb0 + kl;
+            for (int kl0 = 0; kl0 < nkb; ++kl0) {
+                const int kb = kb0 + kl0, kl = it * nkb + kl0;
                 const int rs = kl % RAW_STAGES;
                 mvtc::wait_or_flag(RAW_FULL + 8 * rs, (kl / RAW_STAGES) & 1, PCU_DEVERR_FULL_WAIT);
                 const uint32_t rw = base + L::OFF_RAW + rs * BM * Raw<TYPE>::B + r * Raw<TYPE>::B;
@@ -493,36 +521,46 @@ __global__ void __launch_bounds__(Cfg<BNT>::THREADS, 1)
                 __syncwarp();
                 if (lane == 0) mvtc::mbar_arrive_a(RAW_EMPTY + 8 * rs);
             }
+            }
         }
     } else {
         // ---------------------------------------------------------- epilogue
         const int q = warp & 3;                             // TMEM lanes 32q .. 32q + 31
-        const int m = m0 + 32 * q + lane;
-        mvtc::wait_or_flag(D_FULL, 0, PCU_DEVERR_MMA_WAIT);
-        tc_after();
-        const float rinv = (QUANT && m < out_n) ? 1.f / __ldg(rowsc + m) : 1.f;
         // y, or this K slice's partial outputs [n_tok][out_n]
         float* dst = part ? part + (size_t)blockIdx.z * n_tok * out_n : y;
         #pragma unroll 1
-        for (int c = 0; c < BNT / 32; ++c) {
-            float v[32];
-            tmem_ld32x(tmem + ((uint32_t)(32 * q) << 16) + 32 * c, v);
-            // the chunk's 32 token scales: one load per lane, shared by shuffles
-            const int nl = n0 + 32 * c + lane;
-            const float xs = nl < n_tok ? __ldg(xinv + nl) : 0.f;
-            float* d = dst + (size_t)(n0 + 32 * c) * out_n + m;
-            // warp-uniform test: all 32 rows and all 32 tokens in range
-            if (m0 + 32 * q + 32 <= out_n && n0 + 32 * c + 32 <= n_tok) {
-                #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    d[(size_t)j * out_n] = v[j] * rinv * __shfl_sync(0xffffffffu, xs, j);
-            } else {
-                #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float sj = __shfl_sync(0xffffffffu, xs, j);
-                    if (m < out_n && n0 + 32 * c + j < n_tok) d[(size_t)j * out_n] = v[j] * rinv * sj;
+        for (int t = blockIdx.x, it = 0; t < total; t += gridDim.x, ++it) {
+            const int m0 = (t % n_mt) * BM, n0 = (t / n_mt) * BNT, buf = it & 1;
+            const int m = m0 + 32 * q + lane;
+            mvtc::wait_or_flag(D_FULL + 8 * buf, (it >> 1) & 1, PCU_DEVERR_MMA_WAIT);
+            tc_after();
+            const float rinv = (QUANT && m < out_n) ? 1.f / __ldg(rowsc + m) : 1.f;
+            #pragma unroll 1
+            for (int c = 0; c < BNT / 32; ++c) {
+                float v[32];
+                tmem_ld32x(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * BNT + 32 * c), v);
+                // the chunk's 32 token scales: one load per lane, shared by shuffles
+                const int nl = n0 + 32 * c + lane;
+                const float xs = nl < n_tok ? __ldg(xinv + nl) : 0.f;
+                float* d = dst + (size_t)(n0 + 32 * c) * out_n + m;
+                // warp-uniform test: all 32 rows and all 32 tokens in range
+                if (m0 + 32 * q + 32 <= out_n && n0 + 32 * c + 32 <= n_tok) {
+                    #pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        d[(size_t)j * out_n] = v[j] * rinv * __shfl_sync(0xffffffffu, xs, j);
+                } else {
+                    #pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float sj = __shfl_sync(0xffffffffu, xs, j);
+                        if (m < out_n && n0 + 32 * c + j < n_tok) d[(size_t)j * out_n] = v[j] * rinv * sj;
+                    }
                 }
             }
+            // this warp has read its lanes of the accumulator out: the MMA
+            // may reuse it for the tile after next
+            tc_before();
+            __syncwarp();
+            if (lane == 0) mvtc::mbar_arrive_a(ACC_EMPTY + 8 * buf);
         }
     }
     tc_before();
@@ -665,7 +703,10 @@ inline cudaError_t launch_bn(const uint8_t* W, size_t row_bytes, int out_n, int 
         if (e != cudaSuccess) return e;
         attr[dev] = true;
     }
-    const dim3 grid((unsigned)((out_n + BM - 1) / BM), (unsigned)((n_tok + BNT - 1) / BNT), (unsigned)ks);
+    // Persistent: at most one CTA per SM, each walking its output tiles
+    // (one tile per CTA when K is split).
+    const int total = ((out_n + BM - 1) / BM) * ((n_tok + BNT - 1) / BNT);
+    const dim3 grid((unsigned)(ks > 1 || total < kSms ? total : kSms), 1u, (unsigned)ks);
     cudaError_t e = launch_pdl(matmul_tc_kernel<TYPE, BNT>, grid, dim3(Cfg<BNT>::THREADS), (size_t)Lay<TYPE, BNT>::BYTES,
                                st, tw, th, tl, out_n, in_n, n_tok, (const float*)xinv, (const float*)rowsc, y, part);
     if (e != cudaSuccess) return e;
