@@ -18,16 +18,20 @@
 //     term is below f32 rounding); the epilogue removes both powers of two.
 //     F16 weights are exact in f16 and need only hi.hi + hi.lo.
 //
-// CTA = 128 weight rows x 128 tokens, one tile per CTA:
+// Tile = 128 weight rows x BN tokens (BN 128 for prompts, 32 / 64 for decode
+// batches). The grid is persistent: at most one CTA per SM, each walking its
+// tiles (one tile per CTA when K is split over CTAs):
 //   warp 0     one lane streams the raw weight blocks of each 256-element
 //              K-block (2-D TMA, 128-row box) and the x hi / lo tiles of each
 //              64-element K-step (2-D TMA, 128-byte swizzle); for F16 it loads
 //              the weight tile itself the same way;
 //   warps 2-5  thread r dequantizes row r of each K-step into the A hi / lo
 //              tiles, in the 128-byte-swizzled K-major layout the MMA reads;
-//   warp 1     allocates 128 TMEM columns; one lane issues tcgen05.mma
-//              (M = 128, N = 128, K = 16, f16 in, f32 accumulate);
-//   warps 6-9  read the accumulator rows out of TMEM and store y.
+//   warp 1     allocates two BN-column TMEM accumulators; one lane issues
+//              tcgen05.mma (M = 128, N = BN, K = 16, f16 in, f32 accumulate)
+//              into tile i's accumulator while tile i - 1's drains;
+//   warps 6-9  read the accumulator rows out of TMEM, store y, and hand the
+//              accumulator back to the MMA.
 // Every mbarrier wait is bounded (a timeout records an error in g_mv_err and
 // the kernel runs on to its end, freeing TMEM). No multicast.
 #pragma once
