@@ -327,11 +327,15 @@ PCU_DEV void dequant_kstep(uint32_t rw, int kb, int ks, float rsc, float (&w)[64
             for (int uu = 0; uu < 2; ++uu) {
                 const int u = 2 * (ks & 1) + uu;
                 const uint32_t ql = ld4(bp + 64 * n + 32 * uu + 4 * i);
+                // the four 6-bit quants of bytes 0..3 at once
+                const uint32_t q4 = ((ql >> hs) & 0x0F0F0F0Fu) | (((qh >> (2 * u)) & 0x03030303u) << 4);
                 #pragma unroll
                 for (int b = 0; b < 4; ++b) {
                     const int l = 4 * i + b;
-                    const int q = ((byte_of(ql, b) >> hs) & 15) | (((byte_of(qh, b) >> (2 * u)) & 3) << 4);
-                    w[32 * uu + l] = ds[uu][l >> 4] * (float)(q - 32);
+                    // quant byte b under the exponent of 2^23: 2^23 + q exactly,
+                    // so (2^23 + q) - (2^23 + 32) is (float)(q - 32) exactly
+                    const float f = __uint_as_float(__byte_perm(q4, 0x4B000000u, 0x7540u + b));
+                    w[32 * uu + l] = ds[uu][l >> 4] * (f - 8388640.0f);
                 }
             }
         }
