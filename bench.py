@@ -3,23 +3,25 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N = 1: headline = Llama-3-8B-shaped decode, B=64, ctx 4096 (KV cache
-       2.15 GB > L2, so no flush between steps), plus B=1 / B=8, the
-       70B-shaped and long-context decodes on one GPU, and causal prefill
-       (TFLOP/s) as extras. A workload whose cache fits in L2 (B=1: 34 MB)
-       steps through enough layer caches that the set is twice L2, as a
-       model's decode step does; its L2-write-flushed time is reported too.
-N > 1: headline = Llama-3-70B-shaped decode sharded by KV-head group
-       (B=16, ctx 32768), head outputs exchanged over NVLink by the
-       library's peer exchange (the NCCL all-gather time is reported
-       beside it); extra = long-context decode sharded by sequence chunk
-       (ctx 131072), partial (m, l, acc) triples exchanged and merged by
-       log-sum-exp. Steps replayed from a captured CUDA graph.
-       Strong scaling: total work fixed. Time = max over ranks.
+Headline at every N: Llama-3-70B-shaped decode attention, B=16, ctx 32768
+(4.3 GB of F32 KV cache, larger than L2, so no flush between steps).
+  N = 1: the whole cache on one GPU (split-KV decode kernel + merge).
+  N > 1: KV heads sharded N ways (1/N of the cache per GPU); the head
+         outputs are exchanged over NVLink inside the decode's merge launch
+         (plain peer stores, per-row flags). Strong scaling: total work
+         fixed, time = max over ranks; rank 0 also decodes the whole
+         problem on one GPU (parity reference and 1-GPU time).
+Series at every N: long-context decode, ctx 131072 (seq-chunk shard at
+N > 1: partial (m, l, acc) triples exchanged and merged by log-sum-exp in the
+same fused launch). N = 1 extras: Llama-3-8B-shaped decode B=1/8/64, causal
+prefill (TFLOP/s), the projection matvec/GEMM. Decode steps are replayed
+from a captured CUDA graph.
 
 One JSON line on rank 0. `--impl reference` times the reference's own
-OpenMP attention block (oracle/_ref, compiled from its sources) on the host
-cores on a bounded sample of the same workload.
+OpenMP attention block (oracle/_ref, compiled from its sources) on all host
+cores, on the same workload: a step is one reference call per sequence,
+cycling over distinct caches that total more than the host's L3. The
+`cpu_baseline` of this arm's line runs the same code.
 """
 import argparse
 import json
@@ -33,7 +35,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from lestramanika_b200.workloads import C2_B1, C2_B8, C2_B64, C3, C4, C5, Decode  # noqa: E402
+from lestramanika_b200.workloads import C2_B1, C2_B8, C2_B64, C3, C4, C4_SMALL, C5  # noqa: E402
 
 MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS = 6650.0, 1590.0
@@ -838,43 +840,103 @@ def matvec_cpu_baseline(types=("F16", "Q8_0", "Q6_K", "Q4_K", "Q4_0"), seconds=2
             "types": res}
 
 
-def cpu_baseline(seconds=10.0):
-    """The reference's OpenMP attention (oracle/_ref, compiled from its sources)
-    on the host cores, on whole sequences of the C2 workload (ctx 4096)."""
+REF_CACHE_BYTES = 1 << 30     # distinct host caches cycled through by the CPU reference: above the host's L3
+
+
+def config_of(w):
+    """The workload description both arms print (identical dicts)."""
+    return {"workload": w.name, "B": w.B, "H": w.H, "HK": w.HK, "D": w.D, "ctx": w.ctx,
+            "l2": "inputs larger than L2 (no flush)"}
+
+
+def ref_decode(w, steps, warmup):
+    """The reference's own OpenMP attention block (oracle/_ref/libref_attn_block.so,
+    compiled from its sources; the C restatement when that is not built) on
+    all host cores, on workload w: the reference has no batch dimension, so
+    a step is w.B calls, one per sequence at position ctx, each parallel over
+    heads (src/pickle_fast.c:1960). The block is made with R layers and call i
+    uses layer i % R, so the calls cycle over R distinct caches of
+    >= 1 GiB in all - more than the host's L3. The `--impl reference` arm
+    and the `cpu_baseline` of this arm's line both run this function."""
     ncores = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(ncores))
+    os.environ["OMP_NUM_THREADS"] = str(ncores)
     os.environ.setdefault("OMP_PROC_BIND", "close")
     import numpy as np
     import oracle
-    w = C2_B64
-    rng = np.random.Generator(np.random.Philox(5))
+    per_layer = 2 * (w.ctx + 1) * w.HK * w.D * 4
+    R = max(1, -(-REF_CACHE_BYTES // per_layer))
     if oracle.RefBlock.available():
-        blk, kind = oracle.RefBlock(1, w.H, w.HK, w.D, w.ctx + 1, w.theta), "reference"
-        lib = oracle.RefBlock.lib()
-        kptr, vptr = lib.ref_block_k_cache(blk._h), lib.ref_block_v_cache(blk._h)
+        blk, kind = oracle.RefBlock(R, w.H, w.HK, w.D, w.ctx + 1, w.theta), "reference"
     else:
-        blk, kind = oracle.OracleAttn(1, w.H, w.HK, w.D, w.ctx + 1, w.theta), "port"
-        lo = oracle.oracle_lib()
-        kptr, vptr = lo.oracle_attn_k_cache(blk._h), lo.oracle_attn_v_cache(blk._h)
-    n = (w.ctx + 1) * w.HK * w.D
-    kc = np.ctypeslib.as_array(kptr, shape=(n,))
-    vc = np.ctypeslib.as_array(vptr, shape=(n,))
-    kc[:w.ctx * w.HK * w.D] = rng.standard_normal(w.ctx * w.HK * w.D, dtype=np.float32)
-    vc[:w.ctx * w.HK * w.D] = rng.standard_normal(w.ctx * w.HK * w.D, dtype=np.float32)
+        blk, kind = oracle.OracleAttn(R, w.H, w.HK, w.D, w.ctx + 1, w.theta), "port"
+    rng = np.random.Generator(np.random.Philox(5))
+    k0, v0 = blk.cache(0)
+    k0[:w.ctx] = rng.standard_normal(k0[:w.ctx].shape, dtype=np.float32)
+    v0[:w.ctx] = rng.standard_normal(v0[:w.ctx].shape, dtype=np.float32)
+    for L in range(1, R):          # distinct memory, same distribution: rows rotated
+        kL, vL = blk.cache(L)
+        kL[:w.ctx] = np.roll(k0[:w.ctx], 97 * L, axis=0)
+        vL[:w.ctx] = np.roll(v0[:w.ctx], 97 * L, axis=0)
     q = rng.standard_normal(w.H * w.D, dtype=np.float32)
     k = rng.standard_normal(w.HK * w.D, dtype=np.float32)
     v = rng.standard_normal(w.HK * w.D, dtype=np.float32)
-    blk.decode(0, w.ctx, q, k, v)                 # warm-up (also fills the RoPE table)
-    seqs, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < seconds:
-        blk.decode(0, w.ctx, q, k, v)
-        seqs += 1
+    i = 0
+    for _ in range(warmup):
+        for _ in range(w.B):
+            blk.decode(i % R, w.ctx, q, k, v)
+            i += 1
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        for _ in range(w.B):
+            blk.decode(i % R, w.ctx, q, k, v)
+            i += 1
     dt = time.perf_counter() - t0
     blk.close()
-    per_seq = w.kv_bytes / w.B
-    return {"value": per_seq * seqs / dt / 1e9, "unit": "GB/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
-            "kind": kind, "sample": f"{seqs} sequences of {w.name} (one reference call each) in {dt:.1f} s",
-            "ms_per_sequence": dt / seqs * 1e3}
+    return {"value": w.kv_bytes * steps / dt / 1e9, "unit": "GB/s", "cores": ncores, "kind": kind,
+            "ms_per_step": dt / steps * 1e3,
+            "sample": f"{steps} whole steps of {w.name}: {w.B} calls each, one per sequence, cycling over "
+                      f"{R} distinct {per_layer / 1e6:.0f} MB caches ({R * per_layer / 1e9:.2f} GB)"}
+
+
+def prefill_cpu(w, n_pos=16):
+    """The reference's prefill of workload w on all host cores: it runs a
+    prompt token by token through its attention block (src/pickle_fast.c:1881),
+    so one layer's prefill of B prompts of T tokens is B * T block calls at
+    positions 0..T-1. Timed at n_pos positions spread over the prompt and
+    extrapolated (the call's cost grows linearly with the position)."""
+    os.environ["OMP_NUM_THREADS"] = str(os.cpu_count() or 1)
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    import numpy as np
+    import oracle
+    if oracle.RefBlock.available():
+        blk, kind = oracle.RefBlock(1, w.H, w.HK, w.D, w.T + 1, w.theta), "reference"
+    else:
+        blk, kind = oracle.OracleAttn(1, w.H, w.HK, w.D, w.T + 1, w.theta), "port"
+    rng = np.random.Generator(np.random.Philox(9))
+    kc, vc = blk.cache(0)
+    kc[:w.T] = rng.standard_normal(kc[:w.T].shape, dtype=np.float32)
+    vc[:w.T] = rng.standard_normal(vc[:w.T].shape, dtype=np.float32)
+    q = rng.standard_normal(w.H * w.D, dtype=np.float32)
+    k = rng.standard_normal(w.HK * w.D, dtype=np.float32)
+    v = rng.standard_normal(w.HK * w.D, dtype=np.float32)
+    pos = np.linspace(0, w.T - 1, n_pos).astype(int)
+    blk.decode(0, int(pos[-1]), q, k, v)
+    t0 = time.perf_counter()
+    for p in pos:
+        blk.decode(0, int(p), q, k, v)
+    per_call = (time.perf_counter() - t0) / n_pos
+    blk.close()
+    ms = per_call * w.B * w.T * 1e3
+    return {"value": w.flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "kind": kind,
+            "cores": int(os.environ["OMP_NUM_THREADS"]),
+            "sample": f"{n_pos} block calls at positions spread over the {w.T}-token prompt, "
+                      f"extrapolated to {w.B} x {w.T} calls"}
+
+
+def _decode_extra(w, device, steps, warmup, small, hbm):
+    line, _ = decode_line(w, device, steps, warmup, small)
+    line["frac_of_measured_hbm"] = line["GBps"] / hbm
+    return line
 
 
 def run_ours_single(args):
@@ -882,13 +944,28 @@ def run_ours_single(args):
     device = 0
     torch.cuda.set_device(device)
     hbm, bf16, bf16_sus, src = peaks()
+    w = C4
     with ClockSampler(device) as clk:
-        head, e2e = decode_line(C2_B64, device, args.steps, args.warmup, small=False)
+        head, e2e = decode_line(w, device, args.steps, args.warmup, small=False)
     extras = {}
-    for w, small in ((C2_B1, True), (C2_B8, False), (C4, False), (C5, False)):
-        line, _ = decode_line(w, device, max(args.steps, 5), args.warmup, small)
-        line["frac_of_measured_hbm"] = line["GBps"] / hbm
-        extras[w.name] = line
+    # The long-context series' 1-GPU point and the small-batch decodes.
+    c5 = _decode_extra(C5, device, max(args.steps, 5), args.warmup, False, hbm)
+    extras["c5_series"] = {"workload": C5.name, "n_gpus": 1, "ms": c5["ms"], "GBps": c5["GBps"],
+                           "roofline_frac_per_gpu": c5["frac_of_measured_hbm"], "splits": c5["splits"]}
+    for wx, small in ((C2_B64, False), (C2_B8, False), (C2_B1, True), (C4_SMALL, False)):
+        extras[wx.name] = _decode_extra(wx, device, max(args.steps, 5), args.warmup, small, hbm)
+    try:
+        from lestramanika_b200 import PREFILL_BF16
+        pf = prefill_line(C3, device, max(5, min(args.steps, 10)), max(args.warmup, 3), PREFILL_BF16)
+        pf["roofline"] = {"bound": "tensor", "achieved": pf["TFLOPs"], "peak": bf16, "unit": "TFLOP/s",
+                          "frac": pf["TFLOPs"] / bf16, "peak_source": f"{src} (bf16_tflops, cuBLAS burst)"}
+        pf["attn_roofline"] = {"bound": "tensor", "achieved": pf["attn_TFLOPs"], "peak": bf16, "unit": "TFLOP/s",
+                               "frac": pf["attn_TFLOPs"] / bf16}
+        if not args.no_cpu_baseline:
+            pf["cpu_baseline"] = prefill_cpu(C3)
+        extras["prefill"] = pf
+    except Exception as exc:  # reported, not hidden
+        extras["prefill"] = {"error": str(exc)[:200]}
     try:
         mvl = matvec_line(device, max(args.steps, 20), max(args.warmup, 3))
         for r in mvl["types"].values():
@@ -907,53 +984,28 @@ def run_ours_single(args):
         extras["prefill_layer"] = prefill_layer_line(device, max(min(args.steps, 10), 3), max(args.warmup, 3))
     except Exception as exc:  # reported, not hidden
         extras["prefill_layer"] = {"error": str(exc)[:200]}
-    try:
-        fw = forward_line(device, max(min(args.steps, 5), 2), max(args.warmup, 2))
-        fw["decode_frac_of_measured_hbm"] = fw["decode_GBps"] / hbm
-        if not args.no_cpu_baseline:
-            fw["cpu_reference"] = forward_cpu()
-            if "decode_ms_per_token" in fw["cpu_reference"]:
-                fw["decode_speedup_vs_reference"] = (fw["cpu_reference"]["decode_ms_per_token"] /
-                                                     fw["decode_ms_per_token"])
-        extras["forward"] = fw
-    except Exception as exc:  # reported, not hidden
-        extras["forward"] = {"error": str(exc)[:200]}
-    try:
-        fb = forward_batch_line(device, max(min(args.steps, 10), 3), max(args.warmup, 2))
-        for r in fb["batches"].values():
-            r["frac_of_measured_hbm"] = r["GBps"] / hbm
-        extras["forward_batch"] = fb
-    except Exception as exc:  # reported, not hidden
-        extras["forward_batch"] = {"error": str(exc)[:200]}
-    try:
-        from lestramanika_b200 import PREFILL_BF16
-        pf = prefill_line(C3, device, max(5, min(args.steps, 10)), max(args.warmup, 3), PREFILL_BF16)
-        pf["frac_of_measured_bf16"] = pf["TFLOPs"] / bf16
-        pf["attn_frac_of_measured_bf16"] = pf["attn_TFLOPs"] / bf16
-        extras["prefill"] = pf
-    except Exception as exc:  # reported, not hidden
-        extras["prefill"] = {"error": str(exc)[:200]}
     gbps = head["GBps"]
     e2e_ms, h2d, d2h = e2e
     out = {
         "metric": "decode-attn KV GB/s", "value": gbps, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": head["ms"], "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) cache and q/k/v, seeded",
-        "config": {"workload": C2_B64.name, "B": 64, "H": 32, "HK": 8, "D": 128, "ctx": 4096,
-                   "l2": head["l2"], "splits": head["splits"], "parallelism": "single GPU"},
+        "config": config_of(w),
+        "parallelism": "single GPU", "splits": head["splits"],
         "frac_of_8TBps": gbps / 8000.0,
         "roofline": {"bound": "hbm", "achieved": gbps, "peak": hbm, "unit": "GB/s", "frac": gbps / hbm,
                      "peak_source": f"{src} (hbm_gbs, copy burst)",
-                     "traffic": profile_traffic("decode_splitkv C2 B=64"),
-                     "algorithmic_bytes_per_launch": C2_B64.kv_bytes},
-        "e2e": {"value": C2_B64.kv_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                     "traffic": profile_traffic("decode_splitkv C4 B=16"),
+                     "algorithmic_bytes_per_launch": w.kv_bytes},
+        "e2e": {"value": w.kv_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
         "gpu_launches": args.steps * (2 if head["splits"] > 1 else 1),   # split kernel (+ merge kernel)
         "clocks": clk.summary(),
         "extras": extras,
     }
     if not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+        # The reference arm's code on a shorter run (whole steps of the same workload).
+        out["cpu_baseline"] = ref_decode(w, min(args.steps, 8), 1)
     print(json.dumps(out), flush=True)
 
 
@@ -966,45 +1018,55 @@ def run_ours_multi(args, rank, world, local_rank):
                             device_id=torch.device("cuda", local_rank))
     from lestramanika_b200 import dist as pdist
     hbm, _, _, src = peaks()
+    w = C4
     clk = ClockSampler(local_rank) if rank == 0 else None
     if clk:
         clk.__enter__()
     try:
-        res = pdist.bench_head_sharded(C4, rank, world, local_rank, args.steps, args.warmup)
+        res = pdist.bench_head_sharded(w, rank, world, local_rank, args.steps, args.warmup)
     finally:
         if clk:
             clk.__exit__(None, None, None)
     res_seq = pdist.bench_seq_sharded(C5, rank, world, local_rank, args.steps, args.warmup)
     if rank == 0:
-        gbps = C4.kv_bytes / (res["ms"] * 1e-3) / 1e9
+        gbps = w.kv_bytes / (res["ms"] * 1e-3) / 1e9
+        one = res["one_gpu"]
+        one5 = res_seq["one_gpu"]
         out = {
             "metric": "decode-attn KV GB/s", "value": gbps, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": res["ms"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) cache and q/k/v, seeded",
-            "config": {"workload": C4.name, "B": C4.B, "H": C4.H, "HK": C4.HK, "D": C4.D, "ctx": C4.ctx,
-                       "l2": "inputs larger than L2", "parallelism": f"kv-head shard x{world} + NVLink peer exchange"},
+            "config": config_of(w),
+            "parallelism": f"kv-head shard x{world}, head outputs exchanged over NVLink inside the merge launch",
+            "splits": res["splits"],
             "frac_of_8TBps_per_gpu": gbps / world / 8000.0,
             "roofline": {"bound": "hbm", "achieved": res["kernel_GBps_per_gpu"], "peak": hbm, "unit": "GB/s",
                          "frac": res["kernel_GBps_per_gpu"] / hbm, "peak_source": f"{src} (hbm_gbs)",
-                         "traffic": None, "note": "per-GPU decode kernel, collective excluded"},
+                         "traffic": None, "note": "per-GPU split-KV decode kernel alone (its 1/N of the cache)"},
             "e2e": res["e2e"],
-            "gpu_launches": args.steps * res["launches_per_step"],   # per rank: split (+ merge); NCCL not counted
+            "gpu_launches": args.steps * res["launches_per_step"],   # per rank: split + fused merge/exchange
             "clocks": clk.summary() if clk else {"sm_mhz": None, "reasons": ["unsampled"]},
-            "extras": {"exchange": "NVLink peer stores (pickle_cuda_xchg_put_dev), output equal to NCCL's: "
-                                   f"{res['exchange_matches_nccl']}",
-                       "nccl_all_gather": {"ms": res["nccl_all_gather_ms"],
-                                           "GBps": C4.kv_bytes / (res["nccl_all_gather_ms"] * 1e-3) / 1e9},
-                       "seq_sharded": {"workload": C5.name, "ms": res_seq["ms"],
-                                       "GBps": C5.kv_bytes / (res_seq["ms"] * 1e-3) / 1e9,
-                                       "nccl_all_gather_ms": res_seq["nccl_all_gather_ms"],
-                                       "exchange_matches_nccl": res_seq["exchange_matches_nccl"]}},
+            "parity": {"max_rel_err_vs_one_gpu": one["max_rel_err_vs_one_gpu"], "bar": 1e-4,
+                       "reference": "the whole problem decoded on GPU 0 from the same seeded shards"},
+            "extras": {
+                "one_gpu_ms": one["one_gpu_ms"],
+                "builder_efficiency": one["one_gpu_ms"] / (world * res["ms"]),
+                "nccl_all_gather": {"ms": res["nccl_all_gather_ms"],
+                                    "GBps": w.kv_bytes / (res["nccl_all_gather_ms"] * 1e-3) / 1e9},
+                "c5_series": {"workload": C5.name, "n_gpus": world, "ms": res_seq["ms"],
+                              "GBps": C5.kv_bytes / (res_seq["ms"] * 1e-3) / 1e9,
+                              "roofline_frac_per_gpu": res_seq["kernel_GBps_per_gpu"] / hbm,
+                              "kernel_ms": res_seq["kernel_ms"],
+                              "nccl_all_gather_ms": res_seq["nccl_all_gather_ms"],
+                              "one_gpu_ms": one5["one_gpu_ms"],
+                              "builder_efficiency": one5["one_gpu_ms"] / (world * res_seq["ms"]),
+                              "max_rel_err_vs_one_gpu": one5["max_rel_err_vs_one_gpu"]}},
         }
         print(json.dumps(out), flush=True)
     dist.barrier()
     dist.destroy_process_group()
 
 
-C4_SMALL = Decode("llama3-70b decode B=2 ctx=32768 (profiling size)", 2, 64, 8, 128, 32768, 500000.0)
 ONLY = {"c2b1": (C2_B1, True), "c2b8": (C2_B8, False), "c2b64": (C2_B64, False), "c4": (C4, False),
         "c4s": (C4_SMALL, False), "c5": (C5, False), "c3": (C3, None), "mv": (None, None), "mm": (None, None),
         "pl": (None, None), "fw": (None, None), "fwd": (None, None), "fwb": (None, None),
@@ -1054,49 +1116,20 @@ def run_only(args):
 
 
 def run_reference(args, rank):
+    """The reference's own CPU attention block on the host cores (rank 0 only;
+    other ranks exit without work): the same workload, metric and config as
+    this arm's line at every N."""
     if rank != 0:
         return
-    import numpy as np  # noqa: F401
-    ncores = os.cpu_count() or 1
-    os.environ["OMP_NUM_THREADS"] = str(ncores)
-    os.environ.setdefault("OMP_PROC_BIND", "close")
-    import oracle
-    w = C2_B64 if args.gpus == 1 else C4
-    # Each step: a bounded sample of the workload's sequences, one reference call per sequence.
-    sample_seqs = 4 if args.gpus == 1 else 1
-    rng = np.random.Generator(np.random.Philox(5))
-    if not oracle.RefBlock.available():
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built from the reference sources"}))
-        return
-    blk = oracle.RefBlock(1, w.H, w.HK, w.D, w.ctx + 1, w.theta)
-    lib = oracle.RefBlock.lib()
-    n = (w.ctx + 1) * w.HK * w.D
-    kc = np.ctypeslib.as_array(lib.ref_block_k_cache(blk._h), shape=(n,))
-    vc = np.ctypeslib.as_array(lib.ref_block_v_cache(blk._h), shape=(n,))
-    kc[:] = rng.standard_normal(n, dtype=np.float32)
-    vc[:] = rng.standard_normal(n, dtype=np.float32)
-    q = rng.standard_normal(w.H * w.D, dtype=np.float32)
-    k = rng.standard_normal(w.HK * w.D, dtype=np.float32)
-    v = rng.standard_normal(w.HK * w.D, dtype=np.float32)
-    for _ in range(args.warmup):
-        blk.decode(0, w.ctx, q, k, v)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        for _ in range(sample_seqs):
-            blk.decode(0, w.ctx, q, k, v)
-    dt = time.perf_counter() - t0
-    blk.close()
-    per_seq = w.kv_bytes / w.B
-    gbps = per_seq * sample_seqs * args.steps / dt / 1e9
-    out = {"impl": "reference", "metric": "decode-attn KV GB/s", "value": gbps, "unit": "GB/s",
-           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-           "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
-           "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) cache and q/k/v, seeded",
-           "config": {"workload": w.name, "B": w.B, "H": w.H, "HK": w.HK, "D": w.D, "ctx": w.ctx},
-           "cpu_baseline": {"value": gbps, "unit": "GB/s", "cores": ncores, "kind": "reference",
-                            "sample": f"{sample_seqs} of {w.B} sequences per step (reference has no batch "
-                                      f"dimension: one pickle attention call per sequence, OpenMP over heads)"},
-           "e2e": {"value": gbps, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    w = C4
+    r = ref_decode(w, args.steps, args.warmup)
+    out = {"impl": "reference", "metric": "decode-attn KV GB/s", "value": r["value"], "unit": "GB/s",
+           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic N(0,1) cache and q/k/v, seeded", "config": config_of(w),
+           "cpu_baseline": {"value": r["value"], "unit": "GB/s", "cores": r["cores"], "kind": r["kind"],
+                            "sample": r["sample"]},
+           "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
 
@@ -1107,7 +1140,6 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--only", choices=sorted(ONLY), help="run one workload on one GPU (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -425,9 +425,62 @@ PICKLE_CUDA_API int  pickle_cuda_xchg_buffer(pickle_cuda_xchg_t* x, void** dev_p
 PICKLE_CUDA_API int  pickle_cuda_xchg_put_dev(pickle_cuda_xchg_t* x, const void* src, size_t rows,
                                               size_t row_bytes, size_t src_stride, size_t dst_offset,
                                               size_t dst_stride, void* stream);
+/* Reports a bounded wait of this rank's exchanging kernels that gave up
+ * (PICKLE_ERR_DEVICE). The exchange is then broken - the ranks' call
+ * counters no longer agree - and every later call on it returns
+ * PICKLE_ERR_DEVICE: free it and create a new one on every rank. */
 PICKLE_CUDA_API int  pickle_cuda_xchg_sync(pickle_cuda_xchg_t* x, void* stream);
 PICKLE_CUDA_API const char* pickle_cuda_xchg_last_error(pickle_cuda_xchg_t* x);
 PICKLE_CUDA_API void pickle_cuda_xchg_free(pickle_cuda_xchg_t* x);
+
+/* Ranks driven by one process (one exchange per rank, on its own GPU, or
+ * several on one GPU for tests) use each other's regions directly instead
+ * of through IPC handles: rank `peer`'s exchange `other` becomes x's peer.
+ * Devices must be able to reach each other (peer access is enabled). */
+PICKLE_CUDA_API int  pickle_cuda_xchg_attach(pickle_cuda_xchg_t* x, int peer, pickle_cuda_xchg_t* other);
+
+/* Bound of every flag wait of this exchange's kernels, in nanoseconds
+ * (default 1 s). */
+PICKLE_CUDA_API int  pickle_cuda_xchg_set_wait(pickle_cuda_xchg_t* x, unsigned long long wait_ns);
+
+/* ---- Sharded decodes with the exchange fused into the launch ----
+ * No counterpart in the reference (one host, OpenMP over heads,
+ * src/pickle_fast.c:1960). Each is two launches on `stream`: the split-KV
+ * decode of this rank's share, then one kernel that merges its splits and
+ * stores the result straight into every rank's exchange buffer with plain
+ * peer stores (no multicast), meeting the other ranks on per-row flags.
+ * All ranks make the same calls with the same n_seqs; q/k/v are this
+ * rank's inputs as for pickle_cuda_decode_batch_dev /
+ * pickle_cuda_decode_partial_dev. Decode errors are reported by
+ * pickle_cuda_sync(h), exchange waits that gave up by
+ * pickle_cuda_xchg_sync(x). n_seqs * n_heads (of this handle) <= 4096.
+ *
+ * KV-head shard: this handle holds this rank's KV heads and their
+ * n_heads query heads (kv_head = h * HK / H keeps them together,
+ * src/pickle_fast.c:1963). Output row (z, local head hl) lands at byte
+ * offset dst_offset + z * dst_row_stride + hl * head_dim * 4 of every
+ * rank's exchange buffer (16-byte multiples); with dst_offset = this
+ * rank's first head * head_dim * 4 and dst_row_stride = all heads *
+ * head_dim * 4 the buffer holds [n_seqs][all heads][head_dim] once the
+ * call completes on the stream. Before storing into a rank's buffer the
+ * call waits until that rank has started the same call, so consume the
+ * buffer on the stream that makes the next call. */
+PICKLE_CUDA_API int  pickle_cuda_decode_gather_dev(pickle_cuda_t* h, pickle_cuda_xchg_t* x, int layer, int n_seqs,
+                                                   size_t pos, const float* q, const float* k, const float* v,
+                                                   size_t dst_offset, size_t dst_row_stride, void* stream);
+
+/* Sequence-chunk shard: this handle holds this rank's n_local cache rows
+ * of every sequence (append != 0 on the rank that also stores the new
+ * token at local row n_local); queries rotate at absolute position pos.
+ * The triples (max, sum, acc) of every rank are exchanged and merged by
+ * log-sum-exp into out [n_seqs][n_heads][head_dim] (this rank's device
+ * memory). The exchange buffer must hold 2 * world * part bytes, part =
+ * n_seqs * n_heads * (head_dim + 2) * 4 rounded up to 16: calls alternate
+ * between its two halves. */
+PICKLE_CUDA_API int  pickle_cuda_decode_seqshard_dev(pickle_cuda_t* h, pickle_cuda_xchg_t* x, int layer,
+                                                     int n_seqs, size_t pos, size_t n_local, int append,
+                                                     const float* q, const float* k, const float* v, float* out,
+                                                     void* stream);
 
 #ifdef __cplusplus
 }

@@ -117,6 +117,10 @@ SIGNATURES = {
     "pickle_cuda_xchg_sync": ([_vp, _vp], _i),
     "pickle_cuda_xchg_last_error": ([_vp], ctypes.c_char_p),
     "pickle_cuda_xchg_free": ([_vp], None),
+    "pickle_cuda_xchg_attach": ([_vp, _i, _vp], _i),
+    "pickle_cuda_xchg_set_wait": ([_vp, ctypes.c_ulonglong], _i),
+    "pickle_cuda_decode_gather_dev": ([_vp, _vp, _i, _i, _sz, _vp, _vp, _vp, _sz, _sz, _vp], _i),
+    "pickle_cuda_decode_seqshard_dev": ([_vp, _vp, _i, _i, _sz, _sz, _i, _vp, _vp, _vp, _vp, _vp], _i),
 }
 
 IPC_HANDLE_BYTES = 64
@@ -267,6 +271,21 @@ class PickleCuda:
                                                          _ptr(q), _ptr(k), _ptr(v), _ptr(m), _ptr(l), _ptr(acc),
                                                          _stream(stream)),
                     "pickle_cuda_decode_partial_dev")
+
+    def decode_gather_dev(self, xchg, layer, n_seqs, pos, q, k, v, dst_offset, dst_row_stride, stream=None):
+        """pickle_cuda_decode_gather_dev: this rank's heads decoded and stored into every
+        rank's exchange buffer (bytes dst_offset + z * dst_row_stride + local head * D * 4)."""
+        self._check(lib().pickle_cuda_decode_gather_dev(self._h, xchg._x, layer, n_seqs, pos, _ptr(q), _ptr(k),
+                                                        _ptr(v), dst_offset, dst_row_stride, _stream(stream)),
+                    "pickle_cuda_decode_gather_dev")
+
+    def decode_seqshard_dev(self, xchg, layer, n_seqs, pos, n_local, append, q, k, v, out, stream=None):
+        """pickle_cuda_decode_seqshard_dev: partial over this rank's n_local cache rows,
+        triples exchanged with every rank and merged into out [n_seqs][H][D]."""
+        self._check(lib().pickle_cuda_decode_seqshard_dev(self._h, xchg._x, layer, n_seqs, pos, n_local,
+                                                          int(bool(append)), _ptr(q), _ptr(k), _ptr(v), _ptr(out),
+                                                          _stream(stream)),
+                    "pickle_cuda_decode_seqshard_dev")
 
     def sync(self, stream=None):
         self._check(lib().pickle_cuda_sync(self._h, _stream(stream)), "pickle_cuda_sync")
@@ -429,6 +448,20 @@ class PeerExchange:
 
     def sync(self, stream=None):
         self._check(lib().pickle_cuda_xchg_sync(self._x, _stream(stream)), "pickle_cuda_xchg_sync")
+
+    def attach(self, peer, other):
+        """Use rank `peer`'s exchange `other`, made by this process, as that peer."""
+        self._check(lib().pickle_cuda_xchg_attach(self._x, peer, other._x), "pickle_cuda_xchg_attach")
+
+    def set_wait(self, wait_ns):
+        """Bound of every flag wait of this exchange's kernels (ns)."""
+        self._check(lib().pickle_cuda_xchg_set_wait(self._x, int(wait_ns)), "pickle_cuda_xchg_set_wait")
+
+    @staticmethod
+    def seqshard_bytes(world, n_seqs, n_heads, head_dim):
+        """Buffer bytes pickle_cuda_decode_seqshard_dev needs: two halves of world parts."""
+        part = (n_seqs * n_heads * (head_dim + 2) * 4 + 15) // 16 * 16
+        return 2 * world * part
 
     def close(self):
         if self._x:

@@ -32,18 +32,31 @@ def _stale(target, deps):
     return any(os.path.getmtime(d) > t for d in deps)
 
 
+UNITS = ("pickle_cuda.cu", "decode_noalloc.cu", "peer_xchg.cu", "matvec.cu", "forward.cu")
+
+
 def build_lib(force=False, verbose=False):
+    """Compile each translation unit to an object (in parallel), then link
+    the shared library; objects go to a build folder next to the library."""
+    from concurrent.futures import ThreadPoolExecutor
     deps = _sources() + [os.path.join(ROOT, "include", "pickle_cuda.h"), __file__]
     if not force and not _stale(LIB, deps):
         return LIB
-    cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
-           "-Xcompiler", "-fvisibility=hidden", "-I" + os.path.join(ROOT, "include"), "-I" + CSRC,
-           "-DPICKLE_CUDA_BUILD", "-o", LIB + ".tmp", os.path.join(CSRC, "pickle_cuda.cu"),
-           os.path.join(CSRC, "decode_noalloc.cu"), os.path.join(CSRC, "peer_xchg.cu"), os.path.join(CSRC, "matvec.cu"),
-           os.path.join(CSRC, "forward.cu")]
+    objdir = os.path.join(HERE, "_build")
+    os.makedirs(objdir, exist_ok=True)
+    flags = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+             "-I" + os.path.join(ROOT, "include"), "-I" + CSRC, "-DPICKLE_CUDA_BUILD"]
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-    subprocess.run(cmd, check=True)
+        flags.insert(0, "-Xptxas=-v")
+
+    def compile_unit(unit):
+        obj = os.path.join(objdir, unit.replace(".cu", ".o"))
+        subprocess.run([NVCC, *flags, "-c", "-o", obj, os.path.join(CSRC, unit)], check=True)
+        return obj
+
+    with ThreadPoolExecutor(max_workers=len(UNITS)) as pool:
+        objs = list(pool.map(compile_unit, UNITS))
+    subprocess.run([NVCC, *ARCH, "-shared", "-o", LIB + ".tmp", *objs], check=True)
     os.replace(LIB + ".tmp", LIB)
     return LIB
 

@@ -19,10 +19,13 @@
 // kernel as its programmatic dependent) when it plans several splits.
 // The first call on each device looks up the array's device address with
 // cudaGetSymbolAddress (host code may not use the symbol itself as a
-// device pointer) and sets the kernel's shared-memory limit; make that
-// first call before any stream capture.
+// device pointer), and the first call with each head dim and GQA group
+// size sets that kernel's shared-memory limit and queries its occupancy;
+// make those first calls before any stream capture. Later calls reuse the
+// cached values without taking a lock.
 #include "pickle_cuda.h"
 
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -40,10 +43,16 @@ constexpr int kNoAllocMaxDevices = 64;
 // Layout: [partials: m rows, l rows, acc rows].
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
+constexpr int kNoAllocKernels = 5 * 4;                      // head dims x GQA group sizes
+
+// Set up once per device under the mutex; later calls read it without the
+// lock (ready and occ[] are published with release stores after the fields
+// they guard).
 struct NoAllocDevice {
-    bool ready = false;
+    std::atomic<bool> ready{false};
     unsigned char* scratch = nullptr;     // device address of g_noalloc_scratch
     int num_sms = 0;
+    std::atomic<int> occ[kNoAllocKernels] = {};   // resident CTAs per SM of each kernel; 0: not prepared
 };
 NoAllocDevice g_dev[kNoAllocMaxDevices];
 std::mutex g_dev_mutex;
@@ -53,12 +62,15 @@ struct NoAllocKernel {
     int threads;
     size_t smem;
     int tile_rows;
+    int index;                            // slot in NoAllocDevice::occ
 };
 
 template <int D, int G>
 NoAllocKernel noalloc_kernel() {
     using C = DecodeCfg<D, G>;
-    return {reinterpret_cast<const void*>(&decode_splitkv_kernel<D, G>), C::THREADS, C::SMEM, C::TP};
+    const int di = D == 48 ? 0 : D == 64 ? 1 : D == 96 ? 2 : D == 128 ? 3 : 4;
+    const int gi = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3;
+    return {reinterpret_cast<const void*>(&decode_splitkv_kernel<D, G>), C::THREADS, C::SMEM, C::TP, di * 4 + gi};
 }
 
 template <int D>
@@ -88,23 +100,34 @@ void report(const char* what, cudaError_t e) {
 }
 
 // Once per device, with that device current: the scratch address and the
-// SM count. Also raises the shared-memory limit of the kernel to be used.
-int noalloc_setup(int device, const NoAllocKernel& k, NoAllocDevice** out) {
+// SM count; once per (device, kernel): the kernel's shared-memory limit and
+// its occupancy. Later calls take the cached values without the lock.
+int noalloc_setup(int device, const NoAllocKernel& k, NoAllocDevice** out, int* occ_out) {
     if (device < 0 || device >= kNoAllocMaxDevices) return PICKLE_ERR_ARG;
-    std::lock_guard<std::mutex> lock(g_dev_mutex);
     NoAllocDevice& d = g_dev[device];
-    if (!d.ready) {
-        void* ptr = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-        if (e != cudaSuccess) { report("cudaGetSymbolAddress", e); return PICKLE_ERR_DEVICE; }
-        e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, device);
-        if (e != cudaSuccess) { report("cudaDeviceGetAttribute", e); return PICKLE_ERR_DEVICE; }
-        d.scratch = static_cast<unsigned char*>(ptr);
-        d.ready = true;
+    int occ = d.ready.load(std::memory_order_acquire) ? d.occ[k.index].load(std::memory_order_acquire) : 0;
+    if (occ < 1) {
+        std::lock_guard<std::mutex> lock(g_dev_mutex);
+        if (!d.ready.load(std::memory_order_relaxed)) {
+            void* ptr = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+            if (e != cudaSuccess) { report("cudaGetSymbolAddress", e); return PICKLE_ERR_DEVICE; }
+            e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, device);
+            if (e != cudaSuccess) { report("cudaDeviceGetAttribute", e); return PICKLE_ERR_DEVICE; }
+            d.scratch = static_cast<unsigned char*>(ptr);
+            d.ready.store(true, std::memory_order_release);
+        }
+        occ = d.occ[k.index].load(std::memory_order_relaxed);
+        if (occ < 1) {
+            cudaError_t e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)k.smem);
+            if (e != cudaSuccess) { report("cudaFuncSetAttribute", e); return PICKLE_ERR_DEVICE; }
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k.fn, k.threads, k.smem);
+            if (e != cudaSuccess || occ < 1) { report("occupancy", e); return PICKLE_ERR_DEVICE; }
+            d.occ[k.index].store(occ, std::memory_order_release);
+        }
     }
-    cudaError_t e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)k.smem);
-    if (e != cudaSuccess) { report("cudaFuncSetAttribute", e); return PICKLE_ERR_DEVICE; }
     *out = &d;
+    *occ_out = occ;
     return PICKLE_OK;
 }
 
@@ -137,11 +160,9 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_decode_noalloc(
     cudaError_t e = cudaGetDevice(&device);
     if (e != cudaSuccess) { report("cudaGetDevice", e); return PICKLE_ERR_DEVICE; }
     NoAllocDevice* dev = nullptr;
-    int rc = noalloc_setup(device, kern, &dev);
-    if (rc != PICKLE_OK) return rc;
     int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern.fn, kern.threads, kern.smem);
-    if (e != cudaSuccess || occ < 1) { report("occupancy", e); return PICKLE_ERR_DEVICE; }
+    int rc = noalloc_setup(device, kern, &dev, &occ);
+    if (rc != PICKLE_OK) return rc;
 
     // Split plan: fill the SMs, but never more partial rows than the array holds.
     const size_t row_bytes = (size_t)(head_dim + 2) * sizeof(float);
@@ -195,6 +216,7 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_decode_noalloc(
     a.hist_len0 = hist;
     a.hist_step = 0;
     a.n_splits = n_splits;
+    a.l2_ahead = kDefaultL2Ahead;
     a.chunk = hist > 0 ? (hist + n_splits - 1) / n_splits : 1;
     a.scale = 1.0f / sqrtf((float)head_dim);
     a.out_mode = 0;

@@ -16,6 +16,7 @@ enum : int {
     PCU_DEVERR_DRAIN_WAIT = 3,   // copies still in flight at exit after an abort
     PCU_DEVERR_MMA_WAIT = 4,     // tensor-core completion never arrived
     PCU_DEVERR_ARG = 5,          // a device-side argument (position, slot) out of range
+    PCU_DEVERR_PEER_WAIT = 6,    // another rank's flag never reached this call's epoch
 };
 
 // Every spin on an mbarrier gives up after this long and records an error
@@ -82,6 +83,14 @@ PCU_DEV void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
         ::"r"(smem_u32(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+// Bulk prefetch of `bytes` (multiple of 16, 16-byte aligned) from global
+// memory into L2 only: no shared memory, no barrier, nothing to wait for.
+// It lets a CTA keep more DRAM requests in flight than its shared-memory
+// ring holds; the later bulk copy of the same bytes then hits L2.
+PCU_DEV void bulk_prefetch_l2(const void* src_gmem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src_gmem), "r"(bytes) : "memory");
 }
 
 // Programmatic dependent launch: a dependent grid waits here until its

@@ -17,9 +17,14 @@
 //   3. it publishes done_p[rank] = e (system-scope release after a
 //      system-scope fence) and waits until done_rank[p] == e: rank p's rows
 //      have arrived here.
-// Each rank's region is one cudaMalloc: the receive buffer, then the ready,
-// done and epoch arrays. Every wait is bounded (1 s); giving up records an
-// error that pickle_cuda_xchg_sync reports.
+// Each rank's region is one cudaMalloc: the receive buffer, then the flag
+// arrays (xchg_internal.cuh). Every wait is bounded (1 s by default,
+// pickle_cuda_xchg_set_wait); giving up records an error that
+// pickle_cuda_xchg_sync reports, and the exchange is then broken: the ranks'
+// call counters no longer agree, so it must be recreated.
+// The fused decode exchanges (pickle_cuda_decode_gather_dev,
+// pickle_cuda_decode_seqshard_dev, in pickle_cuda.cu) use the same regions
+// with per-row flags.
 #include "pickle_cuda.h"
 
 #include <cstdint>
@@ -28,10 +33,11 @@
 #include <new>
 
 #include "pcu_common.cuh"
+#include "xchg_internal.cuh"
 
 namespace {
 
-constexpr int kMaxRanks = PICKLE_CUDA_XCHG_MAX_RANKS;
+constexpr int kMaxRanks = kXchgMaxRanks;
 constexpr int kPutThreads = 512;
 
 struct PutArgs {
@@ -40,23 +46,14 @@ struct PutArgs {
     const unsigned char* src;
     size_t rows, row_bytes, src_stride, dst_offset, dst_stride;
     int rank, world;
+    unsigned long long wait_ns;
     int* err;
 };
 
-PCU_DEV void st_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-PCU_DEV unsigned ld_acquire_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-PCU_DEV bool wait_flag(const unsigned* f, unsigned e) {
+PCU_DEV bool wait_flag(const unsigned* f, unsigned e, unsigned long long wait_ns) {
     const uint64_t t0 = global_timer_ns();
     while (ld_acquire_sys(f) != e)
-        if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+        if (global_timer_ns() - t0 > wait_ns) return false;
     return true;
 }
 
@@ -72,7 +69,7 @@ __global__ void __launch_bounds__(kPutThreads) xchg_put_kernel(const PutArgs a) 
         e = *slot + 1u;
         *slot = e;
         st_release_sys(reinterpret_cast<unsigned*>(theirs + a.ready_off) + a.rank, e);
-        s_ok = wait_flag(reinterpret_cast<const unsigned*>(mine + a.ready_off) + p, e);
+        s_ok = wait_flag(reinterpret_cast<const unsigned*>(mine + a.ready_off) + p, e, a.wait_ns);
         if (!s_ok) record_error(a.err, PCU_DEVERR_FULL_WAIT);
     }
     __syncthreads();
@@ -89,22 +86,12 @@ __global__ void __launch_bounds__(kPutThreads) xchg_put_kernel(const PutArgs a) 
     if (threadIdx.x == 0) {
         __threadfence_system();
         st_release_sys(reinterpret_cast<unsigned*>(theirs + a.done_off) + a.rank, e);
-        if (!wait_flag(reinterpret_cast<const unsigned*>(mine + a.done_off) + p, e))
+        if (!wait_flag(reinterpret_cast<const unsigned*>(mine + a.done_off) + p, e, a.wait_ns))
             record_error(a.err, PCU_DEVERR_FULL_WAIT);
     }
 }
 
 }  // namespace
-
-struct pickle_cuda_xchg {
-    int rank = 0, world = 0, device = 0;
-    size_t buf_bytes = 0, ready_off = 0, done_off = 0, epoch_off = 0, region_bytes = 0;
-    unsigned char* region = nullptr;                 // this rank's allocation
-    unsigned char* peer[kMaxRanks] = {};             // mapped regions (peer[rank] = region)
-    bool opened[kMaxRanks] = {};
-    int* err_dev = nullptr;
-    char last_error[256] = {0};
-};
 
 extern "C" {
 
@@ -123,7 +110,10 @@ PICKLE_CUDA_API int pickle_cuda_xchg_create(int rank, int world, size_t buf_byte
     x->ready_off = buf_bytes;
     x->done_off = x->ready_off + kMaxRanks * sizeof(unsigned);
     x->epoch_off = x->done_off + kMaxRanks * sizeof(unsigned);
-    x->region_bytes = buf_bytes + 256;
+    x->row_ready_off = (buf_bytes + 256 + 255) / 256 * 256;
+    x->row_done_off = x->row_ready_off + (size_t)kMaxRanks * kXchgMaxRows * sizeof(unsigned);
+    x->row_epoch_off = x->row_done_off + (size_t)kMaxRanks * kXchgMaxRows * sizeof(unsigned);
+    x->region_bytes = x->row_epoch_off + (size_t)kXchgMaxRows * sizeof(unsigned);
     if (cudaSetDevice(device) != cudaSuccess || cudaMalloc(&x->region, x->region_bytes) != cudaSuccess ||
         cudaMemset(x->region, 0, x->region_bytes) != cudaSuccess ||
         cudaMalloc(&x->err_dev, sizeof(int)) != cudaSuccess || cudaMemset(x->err_dev, 0, sizeof(int)) != cudaSuccess ||
@@ -165,6 +155,43 @@ PICKLE_CUDA_API int pickle_cuda_xchg_open(pickle_cuda_xchg_t* x, int peer, const
     }
     x->peer[peer] = static_cast<unsigned char*>(ptr);
     x->opened[peer] = true;
+    x->ipc_mapped[peer] = true;
+    return PICKLE_OK;
+}
+
+PICKLE_CUDA_API int pickle_cuda_xchg_attach(pickle_cuda_xchg_t* x, int peer, pickle_cuda_xchg_t* other) {
+    if (!x || !other || peer < 0 || peer >= x->world || peer == x->rank || other->rank != peer ||
+        other->world != x->world || other->buf_bytes != x->buf_bytes)
+        return PICKLE_ERR_ARG;
+    if (x->opened[peer]) return PICKLE_OK;
+    if (other->device != x->device) {
+        // Another GPU of this process: its memory must be reachable from ours.
+        int can = 0;
+        cudaError_t e = cudaDeviceCanAccessPeer(&can, x->device, other->device);
+        if (e != cudaSuccess || !can) {
+            snprintf(x->last_error, sizeof(x->last_error), "device %d cannot reach device %d", x->device,
+                     other->device);
+            return PICKLE_ERR_DEVICE;
+        }
+        e = cudaSetDevice(x->device);
+        if (e == cudaSuccess) e = cudaDeviceEnablePeerAccess(other->device, 0);
+        if (e == cudaErrorPeerAccessAlreadyEnabled) {
+            cudaGetLastError();
+            e = cudaSuccess;
+        }
+        if (e != cudaSuccess) {
+            snprintf(x->last_error, sizeof(x->last_error), "cudaDeviceEnablePeerAccess: %s", cudaGetErrorString(e));
+            return PICKLE_ERR_DEVICE;
+        }
+    }
+    x->peer[peer] = other->region;
+    x->opened[peer] = true;
+    return PICKLE_OK;
+}
+
+PICKLE_CUDA_API int pickle_cuda_xchg_set_wait(pickle_cuda_xchg_t* x, unsigned long long wait_ns) {
+    if (!x || wait_ns == 0) return PICKLE_ERR_ARG;
+    x->wait_ns = wait_ns;
     return PICKLE_OK;
 }
 
@@ -182,6 +209,10 @@ PICKLE_CUDA_API int pickle_cuda_xchg_put_dev(pickle_cuda_xchg_t* x, const void* 
         return PICKLE_ERR_ARG;
     if (rows > 1 && (src_stride < row_bytes || dst_stride < row_bytes)) return PICKLE_ERR_ARG;
     if (dst_offset + (rows - 1) * dst_stride + row_bytes > x->buf_bytes) return PICKLE_ERR_RANGE;
+    if (x->broken) {
+        snprintf(x->last_error, sizeof(x->last_error), "exchange broken by an earlier wait that gave up: recreate it");
+        return PICKLE_ERR_DEVICE;
+    }
     for (int p = 0; p < x->world; ++p)
         if (!x->opened[p]) {
             snprintf(x->last_error, sizeof(x->last_error), "peer %d's region is not open", p);
@@ -201,6 +232,7 @@ PICKLE_CUDA_API int pickle_cuda_xchg_put_dev(pickle_cuda_xchg_t* x, const void* 
     a.dst_stride = rows > 1 ? dst_stride : row_bytes;
     a.rank = x->rank;
     a.world = x->world;
+    a.wait_ns = x->wait_ns;
     a.err = x->err_dev;
     xchg_put_kernel<<<x->world, kPutThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
     cudaError_t e = cudaGetLastError();
@@ -219,7 +251,11 @@ PICKLE_CUDA_API int pickle_cuda_xchg_sync(pickle_cuda_xchg_t* x, void* stream) {
         cudaStreamSynchronize(st) != cudaSuccess)
         return PICKLE_ERR_DEVICE;
     if (err) {
-        snprintf(x->last_error, sizeof(x->last_error), "a peer's rows never arrived (bounded wait gave up)");
+        // The ranks' call counters no longer agree (this rank's moved on, a
+        // peer's did not): every later call would wait in vain too.
+        snprintf(x->last_error, sizeof(x->last_error),
+                 "a peer never arrived (bounded wait gave up); the exchange is broken: recreate it");
+        x->broken = true;
         cudaMemsetAsync(x->err_dev, 0, sizeof(int), st);
         cudaStreamSynchronize(st);
         return PICKLE_ERR_DEVICE;
@@ -236,7 +272,7 @@ PICKLE_CUDA_API void pickle_cuda_xchg_free(pickle_cuda_xchg_t* x) {
     cudaSetDevice(x->device);
     cudaDeviceSynchronize();
     for (int p = 0; p < x->world; ++p)
-        if (p != x->rank && x->opened[p] && x->peer[p]) cudaIpcCloseMemHandle(x->peer[p]);
+        if (p != x->rank && x->ipc_mapped[p] && x->peer[p]) cudaIpcCloseMemHandle(x->peer[p]);
     cudaFree(x->region);
     cudaFree(x->err_dev);
     delete x;

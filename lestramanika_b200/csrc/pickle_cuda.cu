@@ -12,8 +12,10 @@
 #include <mutex>
 
 #include "decode_splitkv.cuh"
+#include "decode_xchg.cuh"
 #include "prefill_common.cuh"
 #include "prefill_tc.cuh"
+#include "xchg_internal.cuh"
 
 namespace {
 
@@ -31,6 +33,7 @@ struct pickle_cuda_impl;
 
 struct pickle_cuda {
     int n_layers, H, HK, D, G, half, max_seq, n_seqs, rope_len, device, num_sms;
+    int l2_ahead = kDefaultL2Ahead;   // decode tiles kept requested into L2 ahead of the ring
     size_t head_stride, seq_stride, layer_stride;   // floats
     float* kc = nullptr;
     float* vc = nullptr;
@@ -161,6 +164,7 @@ DecodeArgs base_args(pickle_cuda* h, int layer) {
     a.half = h->half;
     a.vec = h->half % 4 == 0;                 // table rows then start on 16-byte boundaries
     a.n_q = 1;
+    a.l2_ahead = h->l2_ahead;
     a.scale = 1.0f / sqrtf((float)h->D);      // src/pickle_fast.c:1959
     a.ws_m = h->ws_m;
     a.ws_l = h->ws_l;
@@ -191,11 +195,11 @@ int launch_decode(pickle_cuda* h, DecodeArgs& a, int n_z, cudaStream_t st) {
     return PICKLE_OK;
 }
 
-// Decode of n_seqs queries at `pos` over `hist` cached rows, optionally
-// appending the new row at `append_idx`.
-int decode_common(pickle_cuda* h, int layer, int n_seqs, size_t pos, long long hist, int append,
-                  long long append_idx, const float* q, const float* k, const float* v, float* ao,
-                  float* m_out, float* l_out, int out_mode, cudaStream_t st) {
+// Arguments of the split kernel for n_seqs queries at `pos` over `hist`
+// cached rows, optionally appending the new row at `append_idx`.
+int decode_args(pickle_cuda* h, int layer, int n_seqs, size_t pos, long long hist, int append,
+                long long append_idx, const float* q, const float* k, const float* v, float* ao,
+                float* m_out, float* l_out, int out_mode, DecodeArgs* out) {
     int rc = prepare_kernel(h, h->decode);
     if (rc != PICKLE_OK) return rc;
     const long long groups = (long long)n_seqs * h->HK;
@@ -204,7 +208,8 @@ int decode_common(pickle_cuda* h, int layer, int n_seqs, size_t pos, long long h
         snprintf(h->last_error, sizeof(h->last_error), "q, k, v and output rows must be 16-byte aligned");
         return PICKLE_ERR_ARG;
     }
-    DecodeArgs a = base_args(h, layer);
+    DecodeArgs& a = *out;
+    a = base_args(h, layer);
     a.q = q;
     a.k_new = k;
     a.v_new = v;
@@ -220,7 +225,57 @@ int decode_common(pickle_cuda* h, int layer, int n_seqs, size_t pos, long long h
     a.ao = ao;
     a.out_m = m_out;
     a.out_l = l_out;
+    return PICKLE_OK;
+}
+
+// Decode of n_seqs queries: the split kernel and, with several splits, the merge.
+int decode_common(pickle_cuda* h, int layer, int n_seqs, size_t pos, long long hist, int append,
+                  long long append_idx, const float* q, const float* k, const float* v, float* ao,
+                  float* m_out, float* l_out, int out_mode, cudaStream_t st) {
+    DecodeArgs a;
+    int rc = decode_args(h, layer, n_seqs, pos, hist, append, append_idx, q, k, v, ao, m_out, l_out, out_mode, &a);
+    if (rc != PICKLE_OK) return rc;
     return launch_decode(h, a, n_seqs, st);
+}
+
+// An exchange every rank of which is reachable, on the handle's device.
+int check_xchg(pickle_cuda* h, pickle_cuda_xchg* x) {
+    if (!x) return PICKLE_ERR_ARG;
+    if (x->device != h->device) {
+        snprintf(h->last_error, sizeof(h->last_error), "exchange on device %d, handle on device %d", x->device,
+                 h->device);
+        return PICKLE_ERR_ARG;
+    }
+    if (x->broken) {
+        snprintf(h->last_error, sizeof(h->last_error), "exchange broken by an earlier wait that gave up: recreate it");
+        return PICKLE_ERR_DEVICE;
+    }
+    for (int p = 0; p < x->world; ++p)
+        if (!x->opened[p]) {
+            snprintf(h->last_error, sizeof(h->last_error), "peer %d's region is not open", p);
+            return PICKLE_ERR_ARG;
+        }
+    return PICKLE_OK;
+}
+
+// The split kernel writing partials (one split included), then the fused
+// merge + exchange as its programmatic dependent.
+int launch_decode_xchg(pickle_cuda* h, pickle_cuda_xchg* x, DecodeArgs& a, int n_z, XchgMergeArgs& xm,
+                       cudaStream_t st) {
+    a.force_partials = 1;
+    dim3 grid((unsigned)a.n_splits, (unsigned)h->HK, (unsigned)n_z);
+    void* params[] = {&a};
+    PCU_CHECK(h, cudaLaunchKernel(h->decode.fn, grid, dim3(h->decode.threads), params, h->decode.smem, st));
+    memset(&xm.m, 0, sizeof(xm.m));
+    xm.m.ws_m = a.ws_m;
+    xm.m.ws_l = a.ws_l;
+    xm.m.ws_acc = a.ws_acc;
+    xm.m.n_splits = a.n_splits;
+    xm.px = xchg_peers(x);
+    xm.n_rows = n_z * h->H;
+    xm.err = x->err_dev;
+    PCU_CHECK(h, launch_decode_merge_xchg(h->D, xm, st));
+    return PICKLE_OK;
 }
 
 int ensure_stage(pickle_cuda* h, size_t floats) {
@@ -294,6 +349,11 @@ int pickle_cuda_init(const pickle_cuda_params_t* p, int device, pickle_cuda_t** 
     h->rope_len = p->rope_len > 0 ? p->rope_len : p->max_seq;
     h->device = device;
     h->decode = info;
+    // Tuning knob for sweeps of the L2 look-ahead (tiles, 0 turns it off).
+    if (const char* env = getenv("PICKLE_CUDA_L2_AHEAD")) {
+        const int v = atoi(env);
+        if (v >= 0 && v <= 64) h->l2_ahead = v;
+    }
     h->head_stride = (size_t)p->max_seq * p->head_dim;
     h->seq_stride = h->head_stride * p->n_kv_heads;
     h->layer_stride = h->seq_stride * p->n_seqs;
@@ -432,6 +492,60 @@ int pickle_cuda_decode_partial_dev(pickle_cuda_t* h, int layer, int n_seqs, size
     if (pos >= (size_t)h->rope_len) return PICKLE_ERR_RANGE;
     return decode_common(h, layer, n_seqs, pos, (long long)n_local, append ? 1 : 0, (long long)n_local,
                          q, k, v, acc_out, m_out, l_out, 1, (cudaStream_t)stream);
+}
+
+int pickle_cuda_decode_gather_dev(pickle_cuda_t* h, pickle_cuda_xchg_t* x, int layer, int n_seqs, size_t pos,
+                                  const float* q, const float* k, const float* v, size_t dst_offset,
+                                  size_t dst_row_stride, void* stream) {
+    int rc = check_layer(h, layer, n_seqs);
+    if (rc != PICKLE_OK) return rc;
+    if (!q || !k || !v) return PICKLE_ERR_ARG;
+    if (pos >= (size_t)h->max_seq || pos >= (size_t)h->rope_len) return PICKLE_ERR_RANGE;
+    rc = check_xchg(h, x);
+    if (rc != PICKLE_OK) return rc;
+    const size_t row_bytes = (size_t)h->H * h->D * sizeof(float);
+    if (dst_offset % 16 || dst_row_stride % 16 || (n_seqs > 1 && dst_row_stride < row_bytes)) return PICKLE_ERR_ARG;
+    if ((size_t)n_seqs * h->H > (size_t)kXchgMaxRows ||
+        dst_offset + (size_t)(n_seqs - 1) * dst_row_stride + row_bytes > x->buf_bytes)
+        return PICKLE_ERR_RANGE;
+    DecodeArgs a;
+    // ao is unused: the partials go to the workspace; any aligned pointer passes the check.
+    rc = decode_args(h, layer, n_seqs, pos, (long long)pos, 1, (long long)pos, q, k, v, h->ws_acc, nullptr,
+                     nullptr, 0, &a);
+    if (rc != PICKLE_OK) return rc;
+    XchgMergeArgs xm;
+    memset(&xm, 0, sizeof(xm));
+    xm.mode = 0;
+    xm.rows_per_z = h->H;
+    xm.dst_offset = dst_offset;
+    xm.dst_row_stride = n_seqs > 1 ? dst_row_stride : row_bytes;
+    return launch_decode_xchg(h, x, a, n_seqs, xm, (cudaStream_t)stream);
+}
+
+int pickle_cuda_decode_seqshard_dev(pickle_cuda_t* h, pickle_cuda_xchg_t* x, int layer, int n_seqs, size_t pos,
+                                    size_t n_local, int append, const float* q, const float* k, const float* v,
+                                    float* out, void* stream) {
+    int rc = check_layer(h, layer, n_seqs);
+    if (rc != PICKLE_OK) return rc;
+    if (!q || !out || (append && (!k || !v))) return PICKLE_ERR_ARG;
+    if (n_local + (append ? 1 : 0) > (size_t)h->max_seq) return PICKLE_ERR_RANGE;
+    if (n_local == 0 && !append) return PICKLE_ERR_ARG;
+    if (pos >= (size_t)h->rope_len) return PICKLE_ERR_RANGE;
+    rc = check_xchg(h, x);
+    if (rc != PICKLE_OK) return rc;
+    const size_t rows = (size_t)n_seqs * h->H;
+    const size_t part_bytes = (rows * (h->D + 2) * sizeof(float) + 15) / 16 * 16;
+    if (rows > (size_t)kXchgMaxRows || 2 * (size_t)x->world * part_bytes > x->buf_bytes) return PICKLE_ERR_RANGE;
+    DecodeArgs a;
+    rc = decode_args(h, layer, n_seqs, pos, (long long)n_local, append ? 1 : 0, (long long)n_local, q, k, v, out,
+                     nullptr, nullptr, 1, &a);
+    if (rc != PICKLE_OK) return rc;
+    XchgMergeArgs xm;
+    memset(&xm, 0, sizeof(xm));
+    xm.mode = 1;
+    xm.part_bytes = part_bytes;
+    xm.out = out;
+    return launch_decode_xchg(h, x, a, n_seqs, xm, (cudaStream_t)stream);
 }
 
 int pickle_cuda_lse_merge_dev(int n_parts, int n_rows, int head_dim, const float* m_in, const float* l_in,

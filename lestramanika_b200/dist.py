@@ -15,10 +15,13 @@ one host with OpenMP over heads only, src/pickle_fast.c:1960):
 
 The per-rank compute is a callable so the same orchestration runs with the
 B200 kernels (device tensors) and, in the CPU tests, with a CPU computation
-over gloo. On GPUs the exchange step is either an NCCL all-gather or the
-library's NVLink peer exchange (open_exchange / pickle_cuda_xchg_put_dev):
-each rank stores its rows straight into every rank's receive buffer at
-their final place, so the head slices need no relayout. All ranks take the same collective steps in the same
+over gloo. On GPUs the exchange step is an NCCL all-gather or the library's
+NVLink peer exchange (open_exchange): each rank stores its rows straight
+into every rank's receive buffer at their final place, so the head slices
+need no relayout. The exchange is either its own launch
+(pickle_cuda_xchg_put_dev) or fused into the decode's split-merge launch
+(pickle_cuda_decode_gather_dev, pickle_cuda_decode_seqshard_dev; the
+benchmarks below). All ranks take the same collective steps in the same
 order; process groups are created with a short timeout so a rank that
 stops participating turns into an error on the others instead of a hang.
 """
@@ -228,81 +231,175 @@ def _timed(fn, steps, warmup, device, graph=False):
     return _max_over_ranks(e0.elapsed_time(e1) / steps, device)
 
 
-def bench_head_sharded(w, rank, world, device, steps, warmup):
+def _fill_rows(kt, vt, rows, g, B):
+    """Seeded N(0, 1) cache rows [0, rows) of every sequence and KV head of a
+    [B][heads][max_seq][D] view, drawn contiguously (so the values depend
+    only on the generator, not on the view's strides)."""
     import torch
+    for b in range(B):
+        shape = (kt.shape[1], rows, kt.shape[3])
+        kt[b, :, :rows].copy_(torch.randn(shape, generator=g, device=kt.device))
+        vt[b, :, :rows].copy_(torch.randn(shape, generator=g, device=vt.device))
+
+
+def head_shard_data(w, world, rank, kt, vt):
+    """Rank `rank`'s KV-head shard of workload w: its cache rows into kt/vt
+    ([B][HK/N][>= ctx][D] views) and its q [B][H/N][D], k, v [B][HK/N][D]."""
+    import torch
+    (h0, h1), (k0, k1) = head_shard(w, world, rank)
+    g = torch.Generator(device=kt.device)
+    g.manual_seed(1000 + rank)
+    _fill_rows(kt, vt, w.ctx, g, w.B)
+    q = torch.randn((w.B, h1 - h0, w.D), generator=g, device=kt.device)
+    k = torch.randn((w.B, k1 - k0, w.D), generator=g, device=kt.device)
+    v = torch.randn((w.B, k1 - k0, w.D), generator=g, device=kt.device)
+    return q, k, v
+
+
+def seq_shard_data(w, world, rank, kt, vt):
+    """Rank `rank`'s cache chunk of workload w into kt/vt ([B][HK][>= n_local][D]
+    views); q/k/v are the same on every rank."""
+    import torch
+    p0, p1 = seq_shard(w.ctx, world, rank)
+    g = torch.Generator(device=kt.device)
+    g.manual_seed(2000 + rank)
+    _fill_rows(kt, vt, p1 - p0, g, w.B)
+    g.manual_seed(7)
+    q = torch.randn((w.B, w.H, w.D), generator=g, device=kt.device)
+    k = torch.randn((w.B, w.HK, w.D), generator=g, device=kt.device)
+    v = torch.randn((w.B, w.HK, w.D), generator=g, device=kt.device)
+    return q, k, v
+
+
+def _one_gpu_reference(w, world, device, steps, warmup, kind):
+    """Rank 0 only: the whole workload on this one GPU, its cache assembled
+    from every rank's seeded shard - the unsharded decode's output (the
+    parity reference of the sharded run) and its device time per step."""
+    import torch
+    from .api import PickleCuda
+    cu = PickleCuda(1, w.H, w.HK, w.D, w.ctx + 1, rope_theta=w.theta, n_seqs=w.B, device=device)
+    kt, vt = cu.kv_tensors(0)
+    dev = torch.device("cuda", device)
+    q = torch.empty((w.B, w.H, w.D), device=dev)
+    k = torch.empty((w.B, w.HK, w.D), device=dev)
+    v = torch.empty((w.B, w.HK, w.D), device=dev)
+    for r in range(world):
+        if kind == "head":
+            (h0, h1), (k0, k1) = head_shard(w, world, r)
+            qr, kr, vr = head_shard_data(w, world, r, kt[:, k0:k1], vt[:, k0:k1])
+            q[:, h0:h1], k[:, k0:k1], v[:, k0:k1] = qr, kr, vr
+        else:
+            p0, p1 = seq_shard(w.ctx, world, r)
+            q, k, v = seq_shard_data(w, world, r, kt[:, :, p0:p1], vt[:, :, p0:p1])
+    out = torch.empty((w.B, w.H, w.D), device=dev)
+    st = torch.cuda.current_stream(device)
+    for _ in range(warmup):
+        cu.decode_batch_dev(0, w.B, w.ctx, q, k, v, out, st)
+    cu.sync(st)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(steps):
+            cu.decode_batch_dev(0, w.B, w.ctx, q, k, v, out, torch.cuda.current_stream(device))
+    g.replay()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    g.replay()
+    e1.record(st)
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / steps
+    del g
+    cu.decode_batch_dev(0, w.B, w.ctx, q, k, v, out, st)
+    cu.sync(st)
+    cu.close()
+    return out, ms
+
+
+def _rel_err(got, ref):
+    return float(((got - ref).abs().max() / ref.abs().max()).item())
+
+
+def bench_head_sharded(w, rank, world, device, steps, warmup):
+    """KV-head shard of w on `world` ranks: the decode with the head
+    exchange fused into its merge launch (pickle_cuda_decode_gather_dev) is
+    the headline; timed beside it: the same decode with an NCCL all-gather,
+    the per-GPU decode kernel alone, and the end-to-end step from host
+    buffers. Rank 0 checks the gathered output against the whole problem
+    decoded on one GPU and times that too (the 1-GPU point of the strong
+    scaling)."""
+    import torch
+    import torch.distributed as dist
     from .api import PickleCuda
     (h0, h1), (k0, k1) = head_shard(w, world, rank)
     H, HK = h1 - h0, k1 - k0
     cu = PickleCuda(1, H, HK, w.D, w.ctx + 1, rope_theta=w.theta, n_seqs=w.B, device=device)
     kt, vt = cu.kv_tensors(0)
-    g = torch.Generator(device=f"cuda:{device}")
-    g.manual_seed(1000 + rank)
-    for b in range(w.B):
-        kt[b, :, :w.ctx].normal_(generator=g)
-        vt[b, :, :w.ctx].normal_(generator=g)
-    dev = torch.device("cuda", device)
-    q = torch.randn((w.B, H, w.D), generator=g, device=dev)
-    k = torch.randn((w.B, HK, w.D), generator=g, device=dev)
-    v = torch.randn((w.B, HK, w.D), generator=g, device=dev)
+    q, k, v = head_shard_data(w, world, rank, kt, vt)
     st = torch.cuda.current_stream(device)
 
     def compute(qq, kk, vv, out):
         cu.decode_batch_dev(0, w.B, w.ctx, qq, kk, vv, out, torch.cuda.current_stream(device))
 
-    # NCCL all-gather for reference, then the NVLink peer exchange (the headline).
     hs_nccl = HeadShardedDecode(w.B, w.H, w.HK, w.D, rank, world, compute, device=device)
     nccl_ms = _timed(lambda: hs_nccl.step(q, k, v), steps, warmup, device, graph=True)
-    ref_out = hs_nccl.step(q, k, v).clone()
     x = open_exchange(rank, world, w.B * w.H * w.D * 4, device)
-    hs = HeadShardedDecode(w.B, w.H, w.HK, w.D, rank, world, compute, device=device, exchange=x)
-    ms = _timed(lambda: hs.step(q, k, v), steps, warmup, device, graph=True)
-    same = bool(torch.equal(hs.step(q, k, v), ref_out))
-    kernel_ms = _timed(lambda: compute(q, k, v, hs.local), steps, warmup, device, graph=True)
-    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
-    hout = torch.empty(hs.out.shape).pin_memory()
+    out = x.buffer((w.B, w.H, w.D))
+
+    def fused():
+        cu.decode_gather_dev(x, 0, w.B, w.ctx, q, k, v, h0 * w.D * 4, w.H * w.D * 4,
+                             torch.cuda.current_stream(device))
+
+    ms = _timed(fused, steps, warmup, device, graph=True)
+    local = torch.empty((w.B, H, w.D), device=torch.device("cuda", device))
+    kernel_ms = _timed(lambda: compute(q, k, v, local), steps, warmup, device, graph=True)
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hout = torch.empty(out.shape).pin_memory()
 
     def e2e_step():
         q.copy_(hq, non_blocking=True)
         k.copy_(hk, non_blocking=True)
         v.copy_(hv, non_blocking=True)
-        hout.copy_(hs.step(q, k, v), non_blocking=True)
+        fused()
+        hout.copy_(out, non_blocking=True)
 
     e2e_ms = _timed(e2e_step, steps, warmup, device)
+    fused()
     cu.sync(st)
     x.sync(st)
+    got = out.clone()
     splits = cu.decode_plan(w.B, w.ctx)[0]
     cu.close()
-    import torch.distributed as dist
+    dist.barrier()
+    ref = None
+    if rank == 0:
+        ref_out, one_ms = _one_gpu_reference(w, world, device, steps, warmup, "head")
+        ref = {"max_rel_err_vs_one_gpu": _rel_err(got, ref_out), "one_gpu_ms": one_ms}
     dist.barrier()
     x.close()
     per_gpu = w.kv_bytes / world
     return {"ms": ms, "kernel_ms": kernel_ms, "kernel_GBps_per_gpu": per_gpu / (kernel_ms * 1e-3) / 1e9,
-            "launches_per_step": (2 if splits > 1 else 1) + 1, "splits": splits,
-            "nccl_all_gather_ms": nccl_ms, "exchange_matches_nccl": same,
+            "launches_per_step": 2, "splits": splits, "nccl_all_gather_ms": nccl_ms, "one_gpu": ref,
             "e2e": {"value": w.kv_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
-                    "h2d_bytes_per_step": sum(x.numel() * 4 for x in (hq, hk, hv)),
+                    "h2d_bytes_per_step": sum(t.numel() * 4 for t in (hq, hk, hv)),
                     "d2h_bytes_per_step": hout.numel() * 4, "ms_per_step": e2e_ms}}
 
 
 def bench_seq_sharded(w, rank, world, device, steps, warmup):
+    """Sequence-chunk shard of w on `world` ranks: the partial decode with
+    the triple exchange and log-sum-exp merge fused into its merge launch
+    (pickle_cuda_decode_seqshard_dev); the NCCL all-gather + merge variant
+    timed beside it; rank 0 checks the output against the whole problem on
+    one GPU and times that."""
     import torch
-    from .api import PickleCuda, lse_merge_packed_dev
+    import torch.distributed as dist
+    from .api import PeerExchange, PickleCuda, lse_merge_packed_dev
     p0, p1 = seq_shard(w.ctx, world, rank)
     n_local = p1 - p0
     append = rank == world - 1
     cu = PickleCuda(1, w.H, w.HK, w.D, n_local + 1, rope_theta=w.theta, n_seqs=w.B, rope_len=w.ctx + 1,
                     device=device)
     kt, vt = cu.kv_tensors(0)
-    g = torch.Generator(device=f"cuda:{device}")
-    g.manual_seed(2000 + rank)
-    for b in range(w.B):
-        kt[b, :, :n_local].normal_(generator=g)
-        vt[b, :, :n_local].normal_(generator=g)
-    dev = torch.device("cuda", device)
-    g.manual_seed(7)                       # q / new k, v identical on every rank
-    q = torch.randn((w.B, w.H, w.D), generator=g, device=dev)
-    k = torch.randn((w.B, w.HK, w.D), generator=g, device=dev)
-    v = torch.randn((w.B, w.HK, w.D), generator=g, device=dev)
+    q, k, v = seq_shard_data(w, world, rank, kt, vt)
     st = torch.cuda.current_stream(device)
 
     def compute(qq, kk, vv, m, l, acc):
@@ -314,15 +411,28 @@ def bench_seq_sharded(w, rank, world, device, steps, warmup):
 
     ss_nccl = SeqShardedDecode(w.B, w.H, w.D, w.ctx, rank, world, compute, merge=merge, device=device)
     nccl_ms = _timed(lambda: ss_nccl.step(q, k, v), steps, warmup, device, graph=True)
-    ref_out = ss_nccl.step(q, k, v).clone()
-    x = open_exchange(rank, world, world * ss_nccl.stride * 4, device)
-    ss = SeqShardedDecode(w.B, w.H, w.D, w.ctx, rank, world, compute, merge=merge, device=device, exchange=x)
-    ms = _timed(lambda: ss.step(q, k, v), steps, warmup, device, graph=True)
-    same = bool(torch.equal(ss.step(q, k, v), ref_out))
+    x = open_exchange(rank, world, PeerExchange.seqshard_bytes(world, w.B, w.H, w.D), device)
+    out = torch.empty((w.B, w.H, w.D), device=torch.device("cuda", device))
+
+    def fused():
+        cu.decode_seqshard_dev(x, 0, w.B, w.ctx, n_local, append, q, k, v, out, torch.cuda.current_stream(device))
+
+    ms = _timed(fused, steps, warmup, device, graph=True)
+    m_, l_ = torch.empty(w.B * w.H, device=out.device), torch.empty(w.B * w.H, device=out.device)
+    acc_ = torch.empty((w.B * w.H, w.D), device=out.device)
+    kernel_ms = _timed(lambda: compute(q, k, v, m_, l_, acc_), steps, warmup, device, graph=True)
+    fused()
     cu.sync(st)
     x.sync(st)
+    got = out.clone()
     cu.close()
-    import torch.distributed as dist
+    dist.barrier()
+    ref = None
+    if rank == 0:
+        ref_out, one_ms = _one_gpu_reference(w, world, device, steps, warmup, "seq")
+        ref = {"max_rel_err_vs_one_gpu": _rel_err(got, ref_out), "one_gpu_ms": one_ms}
     dist.barrier()
     x.close()
-    return {"ms": ms, "nccl_all_gather_ms": nccl_ms, "exchange_matches_nccl": same}
+    per_gpu = w.kv_bytes / world
+    return {"ms": ms, "kernel_ms": kernel_ms, "kernel_GBps_per_gpu": per_gpu / (kernel_ms * 1e-3) / 1e9,
+            "nccl_all_gather_ms": nccl_ms, "one_gpu": ref}

@@ -55,6 +55,9 @@ C2_B8 = Decode("llama3-8b decode B=8 ctx=4096", 8, 32, 8, 128, 4096, 500000.0)
 C2_B64 = Decode("llama3-8b decode B=64 ctx=4096", 64, 32, 8, 128, 4096, 500000.0)
 C3 = Prefill("llama2-7b causal prefill B=4 T=2048", 4, 2048, 32, 32, 128, 10000.0)
 C4 = Decode("llama3-70b decode B=16 ctx=32768 (kv-head shard)", 16, 64, 8, 128, 32768, 500000.0)
+# The 70B-shaped decode at B=2: the per-GPU share of C4 on 8 GPUs (537 MB,
+# one wave of CTAs) and the size the ncu captures of that kernel are taken at.
+C4_SMALL = Decode("llama3-70b decode B=2 ctx=32768 (per-GPU share at 8 GPUs)", 2, 64, 8, 128, 32768, 500000.0)
 C5 = Decode("long-context decode B=1 ctx=131072 (seq-chunk shard)", 1, 32, 8, 128, 131072, 500000.0)
 
 

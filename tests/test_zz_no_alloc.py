@@ -5,9 +5,10 @@ that routes every allocation through pickle_alloc_t).
 
 It must give the same outputs as the allocating entry point
 pickle_cuda_decode_batch_dev (within the FP32 tolerance of the other tests,
-1e-4 relative) on two calls in a row, through the C ABI, with the KV cache,
-RoPE tables, inputs and outputs all owned by the caller and its split-KV
-scratch taken from the library's fixed device array.
+1e-4 relative) on two calls in a row, and the CPU oracle's on the first,
+through the C ABI, with the KV cache, RoPE tables, inputs and outputs all
+owned by the caller and its split-KV scratch taken from the library's fixed
+device array.
 
 This file is collected last so that a stop-at-first-failure run has run every
 other test before it.
@@ -53,6 +54,8 @@ def test_noalloc_matches_allocating_entry_point(B, H, HK, D, ctx):
     err = torch.zeros(1, dtype=torch.int32, device=dev)
 
     splits = cu.decode_plan(B, ctx)[0]
+    kc0 = kt.permute(0, 2, 1, 3)[:, :ctx + 1].cpu().numpy().copy()     # pos-major copies for the oracle
+    vc0 = vt.permute(0, 2, 1, 3)[:, :ctx + 1].cpu().numpy().copy()
     for step, pos in enumerate((ctx, ctx + 1)):                # two calls in a row
         q, k, v = _inputs(100 + step, B, H, HK, D)
         ao_ref = torch.empty((B, H, D), device=dev)
@@ -63,6 +66,10 @@ def test_noalloc_matches_allocating_entry_point(B, H, HK, D, ctx):
         torch.cuda.synchronize()
         assert int(err.item()) == 0
         assert_rel(ao.cpu().numpy(), ao_ref.cpu().numpy(), what=f"call {step} pos {pos} (splits {splits})")
+        if step == 0:       # and the reference's own arithmetic (src/pickle_fast.c:1910-2094)
+            ref = oracle.decode_batch(H, HK, D, pos, s[pos], c[pos], kc0, vc0, q.cpu().numpy(), k.cpu().numpy(),
+                                      v.cpu().numpy())
+            assert_rel(ao.cpu().numpy(), ref, what=f"call {step} vs oracle")
         np.testing.assert_array_equal(k_cache[:, :, pos].cpu().numpy(), kt[:, :, pos].cpu().numpy())
         np.testing.assert_array_equal(v_cache[:, :, pos].cpu().numpy(), vt[:, :, pos].cpu().numpy())
     cu.close()
