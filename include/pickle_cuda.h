@@ -446,41 +446,45 @@ PICKLE_CUDA_API int  pickle_cuda_xchg_set_wait(pickle_cuda_xchg_t* x, unsigned l
 /* ---- Sharded decodes with the exchange fused into the launch ----
  * No counterpart in the reference (one host, OpenMP over heads,
  * src/pickle_fast.c:1960). Each is two launches on `stream`: the split-KV
- * decode of this rank's share, then one kernel that merges its splits and
+ * decode of this rank's share, then one kernel that merges its splits,
  * stores the result straight into every rank's exchange buffer with plain
- * peer stores (no multicast), meeting the other ranks on per-row flags.
- * All ranks make the same calls with the same n_seqs; q/k/v are this
- * rank's inputs as for pickle_cuda_decode_batch_dev /
- * pickle_cuda_decode_partial_dev. Decode errors are reported by
- * pickle_cuda_sync(h), exchange waits that gave up by
- * pickle_cuda_xchg_sync(x). n_seqs * n_heads (of this handle) <= 4096.
+ * peer stores (no multicast) as epoch-tagged words, and assembles this
+ * rank's output from what all ranks stored - no fence, flag or extra
+ * launch. All ranks make the same calls with the same n_seqs; q/k/v are
+ * this rank's inputs as for pickle_cuda_decode_batch_dev /
+ * pickle_cuda_decode_partial_dev. The exchange buffer must hold
+ * pickle_cuda_decode_xchg_bytes(...) bytes (calls alternate between its
+ * two halves). Decode errors are reported by pickle_cuda_sync(h), exchange
+ * waits that gave up by pickle_cuda_xchg_sync(x). n_seqs * n_heads (of
+ * this handle) <= 4096.
  *
- * KV-head shard: this handle holds this rank's KV heads and their
- * n_heads query heads (kv_head = h * HK / H keeps them together,
- * src/pickle_fast.c:1963). Output row (z, local head hl) lands at byte
- * offset dst_offset + z * dst_row_stride + hl * head_dim * 4 of every
- * rank's exchange buffer (16-byte multiples); with dst_offset = this
- * rank's first head * head_dim * 4 and dst_row_stride = all heads *
- * head_dim * 4 the buffer holds [n_seqs][all heads][head_dim] once the
- * call completes on the stream. Before storing into a rank's buffer the
- * call waits until that rank has started the same call, so consume the
- * buffer on the stream that makes the next call. */
+ * KV-head shard: this handle holds this rank's KV heads and their n_heads
+ * query heads (kv_head = h * HK / H keeps them together,
+ * src/pickle_fast.c:1963); rank r's heads are [r * n_heads, (r+1) * n_heads)
+ * of the model. out [n_seqs][world * n_heads][head_dim] (this rank's device
+ * memory) receives every rank's head outputs. */
+#define PICKLE_CUDA_SHARD_HEADS 0
+#define PICKLE_CUDA_SHARD_SEQ   1
 PICKLE_CUDA_API int  pickle_cuda_decode_gather_dev(pickle_cuda_t* h, pickle_cuda_xchg_t* x, int layer, int n_seqs,
                                                    size_t pos, const float* q, const float* k, const float* v,
-                                                   size_t dst_offset, size_t dst_row_stride, void* stream);
+                                                   float* out, void* stream);
 
 /* Sequence-chunk shard: this handle holds this rank's n_local cache rows
  * of every sequence (append != 0 on the rank that also stores the new
  * token at local row n_local); queries rotate at absolute position pos.
  * The triples (max, sum, acc) of every rank are exchanged and merged by
  * log-sum-exp into out [n_seqs][n_heads][head_dim] (this rank's device
- * memory). The exchange buffer must hold 2 * world * part bytes, part =
- * n_seqs * n_heads * (head_dim + 2) * 4 rounded up to 16: calls alternate
- * between its two halves. */
+ * memory). */
 PICKLE_CUDA_API int  pickle_cuda_decode_seqshard_dev(pickle_cuda_t* h, pickle_cuda_xchg_t* x, int layer,
                                                      int n_seqs, size_t pos, size_t n_local, int append,
                                                      const float* q, const float* k, const float* v, float* out,
                                                      void* stream);
+
+/* Exchange buffer bytes the fused sharded decodes need:
+ * sharding = PICKLE_CUDA_SHARD_HEADS (n_heads = this rank's query heads)
+ * or PICKLE_CUDA_SHARD_SEQ (n_heads = all query heads). */
+PICKLE_CUDA_API int  pickle_cuda_decode_xchg_bytes(int sharding, int world, int n_seqs, int n_heads, int head_dim,
+                                                   size_t* bytes);
 
 #ifdef __cplusplus
 }

@@ -119,7 +119,8 @@ SIGNATURES = {
     "pickle_cuda_xchg_free": ([_vp], None),
     "pickle_cuda_xchg_attach": ([_vp, _i, _vp], _i),
     "pickle_cuda_xchg_set_wait": ([_vp, ctypes.c_ulonglong], _i),
-    "pickle_cuda_decode_gather_dev": ([_vp, _vp, _i, _i, _sz, _vp, _vp, _vp, _sz, _sz, _vp], _i),
+    "pickle_cuda_decode_gather_dev": ([_vp, _vp, _i, _i, _sz, _vp, _vp, _vp, _vp, _vp], _i),
+    "pickle_cuda_decode_xchg_bytes": ([_i, _i, _i, _i, _i, ctypes.POINTER(_sz)], _i),
     "pickle_cuda_decode_seqshard_dev": ([_vp, _vp, _i, _i, _sz, _sz, _i, _vp, _vp, _vp, _vp, _vp], _i),
 }
 
@@ -272,11 +273,11 @@ class PickleCuda:
                                                          _stream(stream)),
                     "pickle_cuda_decode_partial_dev")
 
-    def decode_gather_dev(self, xchg, layer, n_seqs, pos, q, k, v, dst_offset, dst_row_stride, stream=None):
-        """pickle_cuda_decode_gather_dev: this rank's heads decoded and stored into every
-        rank's exchange buffer (bytes dst_offset + z * dst_row_stride + local head * D * 4)."""
+    def decode_gather_dev(self, xchg, layer, n_seqs, pos, q, k, v, out, stream=None):
+        """pickle_cuda_decode_gather_dev: this rank's heads decoded and exchanged; out
+        [n_seqs][world * H][D] receives every rank's head outputs."""
         self._check(lib().pickle_cuda_decode_gather_dev(self._h, xchg._x, layer, n_seqs, pos, _ptr(q), _ptr(k),
-                                                        _ptr(v), dst_offset, dst_row_stride, _stream(stream)),
+                                                        _ptr(v), _ptr(out), _stream(stream)),
                     "pickle_cuda_decode_gather_dev")
 
     def decode_seqshard_dev(self, xchg, layer, n_seqs, pos, n_local, append, q, k, v, out, stream=None):
@@ -457,13 +458,20 @@ class PeerExchange:
         """Bound of every flag wait of this exchange's kernels (ns)."""
         self._check(lib().pickle_cuda_xchg_set_wait(self._x, int(wait_ns)), "pickle_cuda_xchg_set_wait")
 
-    @staticmethod
-    def seqshard_bytes(world, n_seqs, n_heads, head_dim):
-        """Buffer bytes pickle_cuda_decode_seqshard_dev needs: two halves of world parts."""
-        part = (n_seqs * n_heads * (head_dim + 2) * 4 + 15) // 16 * 16
-        return 2 * world * part
-
     def close(self):
         if self._x:
             lib().pickle_cuda_xchg_free(self._x)
             self._x = None
+
+
+SHARD_HEADS, SHARD_SEQ = 0, 1
+
+
+def decode_xchg_bytes(sharding, world, n_seqs, n_heads, head_dim):
+    """pickle_cuda_decode_xchg_bytes: exchange buffer bytes of the fused sharded decodes
+    (SHARD_HEADS: n_heads = this rank's query heads; SHARD_SEQ: all query heads)."""
+    n = _sz()
+    rc = lib().pickle_cuda_decode_xchg_bytes(sharding, world, n_seqs, n_heads, head_dim, ctypes.byref(n))
+    if rc != PICKLE_OK:
+        raise PickleError(rc, "pickle_cuda_decode_xchg_bytes")
+    return n.value

@@ -61,12 +61,14 @@ def build_lib(force=False, verbose=False):
     return LIB
 
 
-def build_oracle(with_cuda_harness=True):
-    """Build the parity checkers under oracle/ (test infrastructure)."""
-    ref = os.environ.get("PICKLE_REF", "/root/reference")
+def build_oracle(with_cuda_harness=True, ref=None):
+    """Build the parity checkers under oracle/ (test infrastructure). The
+    reference's own objects are compiled only when its sources are given
+    (`ref`, or the PICKLE_REF environment variable)."""
+    ref = ref or os.environ.get("PICKLE_REF", "")
     make = ["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={ref}"]
     subprocess.run(make + ["oracle"], check=True)
-    if os.path.isdir(os.path.join(ref, "src")):
+    if ref and os.path.isdir(os.path.join(ref, "src")):
         subprocess.run(make + ["ref"], check=True)
         if with_cuda_harness:
             subprocess.run(make + ["cuda"], check=True)
@@ -75,5 +77,5 @@ def build_oracle(with_cuda_harness=True):
 if __name__ == "__main__":
     build_lib(force="--force" in sys.argv, verbose="-v" in sys.argv)
     if "--all" in sys.argv:
-        build_oracle()
+        build_oracle(ref=next((a.split("=", 1)[1] for a in sys.argv if a.startswith("--ref=")), None))
     print(LIB)

@@ -1,39 +1,33 @@
 // decode_xchg.cuh - the split merge of the sharded decodes fused with their
-// exchange over NVLink: one launch merges a rank's split partials and
-// stores the result straight into every rank's receive buffer (plain peer
-// stores through CUDA IPC mappings, no multicast), so the exchange costs
-// no launch and no local copy of its own.
+// exchange over NVLink: one launch merges a rank's split partials, stores
+// the result straight into every rank's receive buffer (plain peer stores
+// through CUDA IPC mappings, no multicast), and assembles the final rows
+// from what the other ranks stored, so the exchange costs no launch, no
+// fence and no flag of its own.
 //
 // The reference decodes on one host (lee-muriithi-kingori/lestramanika
 // src/pickle_fast.c:1946-2094, OpenMP over heads at :1960); the two shards
 // split that block's work across GPUs:
 //   gather (KV-head shard): CTA r merges output row r = (query z, local
-//     head hl) of this rank's heads, normalised, and stores it at
-//     dst_offset + z * dst_row_stride + hl * D * 4 in every rank's buffer,
-//     i.e. straight into its place in [n_seqs][H][D];
+//     head hl) of this rank's heads, normalised, and sends it to every rank;
+//     it then writes row r of every rank p to out[z][p * n_heads + hl].
 //   seqshard (sequence-chunk shard): CTA r merges the unnormalised triple
-//     (M, L, acc[D]) of row r over this rank's cache chunk, stores it into
-//     slot [rank] of every rank's buffer, and once all ranks' triples of
-//     row r have arrived merges them by log-sum-exp into out[r]:
+//     (M, L, acc[D]) of row r over this rank's cache chunk and sends it to
+//     every rank; it then merges the triples of row r of all ranks by
+//     log-sum-exp into out[r]:
 //       M* = max_p M_p, o = sum_p e^(M_p - M*) acc_p / sum_p e^(M_p - M*) L_p.
 //
-// Per-row handshake (flags [sender][row] in each region, one counter per
-// row in the own region, so CUDA-graph replays stay correct):
-//   e = ++row_epoch[r];
-//   gather: row_ready[rank][r] = e in every rank's region, before
-//     griddepcontrol.wait: this rank has started the call, so what read its
-//     buffer before (stream order) is done. The stores into rank p's
-//     buffer wait until rank p's ready flag for row r has reached e.
-//   seqshard: no ready flags. Calls alternate between two halves of the
-//     buffer (parity of e). A rank reaching call e + 2, which writes the
-//     half this call reads, has first seen this rank's done flag of call
-//     e + 1, raised after this call finished reading.
-//   Then, after a system-scope fence, row_done[rank][r] = e in every
-//   rank's region, and the CTA waits until every rank's done flag for row
-//   r has reached e: all rows r have arrived here.
-// Every wait is bounded (the exchange's wait limit); giving up records an
-// error in the exchange's error word (pickle_cuda_xchg_sync) and the CTA
-// skips what depends on it.
+// Wire format ("LL": each 8-byte word is 4 bytes of data and the 4-byte
+// call epoch, written by one 16-byte store of two such words): a receiver
+// polls the words themselves until every epoch field equals this call's e,
+// so data and its arrival flag can never be seen apart and no memory fence
+// is needed. Slot [half][sender][row] of the receive buffer, half = e & 1:
+// a rank reaching call e + 2, which overwrites the half call e reads, has
+// received every rank's rows of call e + 1, sent after their call e had
+// finished reading. Epochs come from per-row counters in the own region,
+// so CUDA-graph replays stay correct. Every wait is bounded (the exchange's
+// wait limit); giving up records an error in the exchange's error word
+// (pickle_cuda_xchg_sync) and the row is left unwritten.
 #pragma once
 #include "decode_splitkv.cuh"
 #include "xchg_internal.cuh"
@@ -44,18 +38,43 @@ struct XchgMergeArgs {
     int mode;                        // 0: gather, 1: seqshard
     int n_rows;                      // rows of this rank (the grid)
     int rows_per_z;                  // gather: this rank's query heads per query
-    unsigned long long dst_offset;   // gather: bytes
-    unsigned long long dst_row_stride;
-    unsigned long long part_bytes;   // seqshard: one rank's slot: rows * (D + 2) * 4, 16-byte multiple
-    float* out;                      // seqshard: merged rows [n_rows][D] (local)
+    unsigned long long row_bytes;    // one row's slot: D * 8 (gather), (D + 2) * 8 (seqshard)
+    float* out;                      // gather: [n_z][world * rows_per_z][D]; seqshard: [n_rows][D]
     int* err;                        // the exchange's error word
 };
+
+// Two (data, epoch) words in one 16-byte store / load.
+PCU_DEV void st_ll(unsigned char* p, float a, float b, unsigned e) {
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(__float_as_uint(a)), "r"(e),
+                 "r"(__float_as_uint(b)), "r"(e)
+                 : "memory");
+}
+
+// Poll two words at p until both carry epoch e; false after wait_ns.
+PCU_DEV bool ld_ll(const unsigned char* p, unsigned e, unsigned long long wait_ns, float& a, float& b) {
+    unsigned x, fx, y, fy;
+    uint64_t t0 = 0;
+    for (;;) {
+        asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(x), "=r"(fx), "=r"(y), "=r"(fy)
+                     : "l"(p)
+                     : "memory");
+        if (fx == e && fy == e) break;
+        const uint64_t t = global_timer_ns();
+        if (t0 == 0) t0 = t;
+        else if (t - t0 > wait_ns) return false;
+    }
+    a = __uint_as_float(x);
+    b = __uint_as_float(y);
+    return true;
+}
 
 template <int D>
 __global__ void __launch_bounds__(kMergeThreads) decode_merge_xchg_kernel(const XchgMergeArgs a) {
     constexpr int NCH = D / 4;
     __shared__ MergeSmem<D> sm;
     __shared__ unsigned s_e;
+    __shared__ float s_m[kXchgMaxRanks], s_l[kXchgMaxRanks];
     __shared__ int s_ok;
     const int tid = threadIdx.x, row = blockIdx.x;
     const XchgPeers& px = a.px;
@@ -66,74 +85,84 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_xchg_kernel(const 
         *ep = e;
         s_e = e;
         s_ok = 1;
-        if (a.mode == 0)
-            for (int p = 0; p < px.world; ++p) st_release_sys(row_flag(px.base[p], px.row_ready_off, px.rank, row), e);
     }
     griddep_wait();                                     // the split kernel's partials are visible
-    const float4 T = merge_splits<D>(a.m, row, sm);     // ends with a CTA barrier: s_e, s_ok visible
+    const float4 T = merge_splits<D>(a.m, row, sm);     // ends with a CTA barrier: s_e visible
     const unsigned e = s_e;
-    const int parity = (int)(e & 1u);
-    if (a.mode == 0) {
-        if (tid == 0) {
-            for (int p = 0; p < px.world && s_ok; ++p)
-                s_ok = wait_epoch(row_flag(own, px.row_ready_off, p, row), e, px.wait_ns);
-        }
-        __syncthreads();
-        if (s_ok && tid < NCH) {
+    const size_t half = (size_t)(e & 1u) * px.world * a.n_rows * a.row_bytes;
+    // Send: this rank's row r into slot [half][rank][r] of every rank.
+    const size_t my_slot = half + ((size_t)px.rank * a.n_rows + row) * a.row_bytes;
+    if (tid < NCH) {
+        float4 v = T;
+        if (a.mode == 0) {
             const float inv = 1.0f / (sm.L == 0.0f ? 1.0f : sm.L);
-            const float4 v = make_float4(T.x * inv, T.y * inv, T.z * inv, T.w * inv);
+            v = make_float4(T.x * inv, T.y * inv, T.z * inv, T.w * inv);
+        }
+        for (int p = 0; p < px.world; ++p) {
+            unsigned char* dst = px.base[p] + my_slot + (size_t)tid * 32;
+            st_ll(dst, v.x, v.y, e);
+            st_ll(dst + 16, v.z, v.w, e);
+        }
+    } else if (tid == NCH && a.mode == 1) {
+        for (int p = 0; p < px.world; ++p) st_ll(px.base[p] + my_slot + (size_t)D * 8, sm.M, sm.L, e);
+    }
+    // Receive row r of every rank.
+    bool ok = true;
+    if (a.mode == 0) {
+        if (tid < NCH) {
             const int z = row / a.rows_per_z, hl = row % a.rows_per_z;
-            const size_t off = a.dst_offset + (size_t)z * a.dst_row_stride + ((size_t)hl * D + 4 * tid) * 4;
-            for (int p = 0; p < px.world; ++p) *reinterpret_cast<float4*>(px.base[p] + off) = v;
-        }
-    } else {
-        const size_t slot = ((size_t)parity * px.world + px.rank) * a.part_bytes;
-        if (tid < NCH)
-            for (int p = 0; p < px.world; ++p)
-                reinterpret_cast<float4*>(px.base[p] + slot + (size_t)row * D * 4)[tid] = T;
-        if (tid == 0)
-            for (int p = 0; p < px.world; ++p) {
-                float* ml = reinterpret_cast<float*>(px.base[p] + slot + (size_t)a.n_rows * D * 4);
-                ml[row] = sm.M;
-                ml[a.n_rows + row] = sm.L;
+            for (int p = 0; p < px.world && ok; ++p) {
+                const unsigned char* src = own + half + ((size_t)p * a.n_rows + row) * a.row_bytes + (size_t)tid * 32;
+                float4 v;
+                ok = ld_ll(src, e, px.wait_ns, v.x, v.y) && ld_ll(src + 16, e, px.wait_ns, v.z, v.w);
+                if (ok) {
+                    const size_t orow = ((size_t)z * px.world + p) * a.rows_per_z + hl;
+                    reinterpret_cast<float4*>(a.out + orow * D)[tid] = v;
+                }
             }
-    }
-    // Every thread's stores are ordered before the done flags by the barrier
-    // and the system-scope fence of the thread that publishes them.
-    __syncthreads();
-    if (tid == 0) {
-        if (s_ok) {
-            __threadfence_system();
-            for (int p = 0; p < px.world; ++p) st_release_sys(row_flag(px.base[p], px.row_done_off, px.rank, row), e);
-            for (int p = 0; p < px.world && s_ok; ++p)
-                s_ok = wait_epoch(row_flag(own, px.row_done_off, p, row), e, px.wait_ns);
         }
-        if (!s_ok) record_error(a.err, PCU_DEVERR_PEER_WAIT);
+        if (!ok) record_error(a.err, PCU_DEVERR_PEER_WAIT);
+        return;
+    }
+    if (tid < px.world) {
+        const unsigned char* src = own + half + ((size_t)tid * a.n_rows + row) * a.row_bytes + (size_t)D * 8;
+        float mv = -INFINITY, lv = 0.f;
+        if (!ld_ll(src, e, px.wait_ns, mv, lv)) s_ok = 0;
+        s_m[tid] = mv;
+        s_l[tid] = lv;
     }
     __syncthreads();
-    if (a.mode != 1 || !s_ok || tid >= NCH) return;
-    // Log-sum-exp merge of the world triples of row r, read past L1 (other
-    // GPUs wrote them).
-    const unsigned char* half = own + (size_t)parity * px.world * a.part_bytes;
-    float mp[kXchgMaxRanks];
-    float M = -INFINITY;
-    for (int p = 0; p < px.world; ++p) {
-        mp[p] = __ldcg(reinterpret_cast<const float*>(half + p * a.part_bytes + (size_t)a.n_rows * D * 4) + row);
-        M = fmaxf(M, mp[p]);
+    if (!s_ok) {
+        if (tid == 0) record_error(a.err, PCU_DEVERR_PEER_WAIT);
+        return;
     }
+    if (tid >= NCH) return;
+    float M = -INFINITY;
+    for (int p = 0; p < px.world; ++p) M = fmaxf(M, s_m[p]);
     float L = 0.f;
     float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int p = 0; p < px.world; ++p) {
-        if (mp[p] == -INFINITY) continue;
-        const unsigned char* part = half + p * a.part_bytes;
-        const float w = expf(mp[p] - M);
-        L = fmaf(__ldcg(reinterpret_cast<const float*>(part + (size_t)a.n_rows * D * 4) + a.n_rows + row), w, L);
-        const float4 x = __ldcg(reinterpret_cast<const float4*>(part + (size_t)row * D * 4) + tid);
+    for (int p = 0; p < px.world && ok; ++p) {
+        const unsigned char* src = own + half + ((size_t)p * a.n_rows + row) * a.row_bytes + (size_t)tid * 32;
+        float4 x;
+        ok = ld_ll(src, e, px.wait_ns, x.x, x.y) && ld_ll(src + 16, e, px.wait_ns, x.z, x.w);
+        if (!ok || s_m[p] == -INFINITY) continue;
+        const float w = expf(s_m[p] - M);
+        L = fmaf(s_l[p], w, L);
         A.x = fmaf(w, x.x, A.x); A.y = fmaf(w, x.y, A.y);
         A.z = fmaf(w, x.z, A.z); A.w = fmaf(w, x.w, A.w);
     }
+    if (!ok) {
+        record_error(a.err, PCU_DEVERR_PEER_WAIT);
+        return;
+    }
     const float inv = 1.0f / (L == 0.0f ? 1.0f : L);
     reinterpret_cast<float4*>(a.out + (size_t)row * D)[tid] = make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv);
+}
+
+// Bytes of the receive buffer a fused exchange of n_rows rows per rank needs.
+inline size_t decode_xchg_bytes(int mode, int world, int n_rows, int D) {
+    const size_t row = (size_t)(mode == 0 ? D : D + 2) * 8;
+    return 2 * (size_t)world * n_rows * row;
 }
 
 // Host: the fused merge launch, as a programmatic dependent of the split

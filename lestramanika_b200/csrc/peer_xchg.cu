@@ -24,7 +24,7 @@
 // call counters no longer agree, so it must be recreated.
 // The fused decode exchanges (pickle_cuda_decode_gather_dev,
 // pickle_cuda_decode_seqshard_dev, in pickle_cuda.cu) use the same regions
-// with per-row flags.
+// with per-row call counters and epoch-tagged data words.
 #include "pickle_cuda.h"
 
 #include <cstdint>
@@ -110,9 +110,7 @@ PICKLE_CUDA_API int pickle_cuda_xchg_create(int rank, int world, size_t buf_byte
     x->ready_off = buf_bytes;
     x->done_off = x->ready_off + kMaxRanks * sizeof(unsigned);
     x->epoch_off = x->done_off + kMaxRanks * sizeof(unsigned);
-    x->row_ready_off = (buf_bytes + 256 + 255) / 256 * 256;
-    x->row_done_off = x->row_ready_off + (size_t)kMaxRanks * kXchgMaxRows * sizeof(unsigned);
-    x->row_epoch_off = x->row_done_off + (size_t)kMaxRanks * kXchgMaxRows * sizeof(unsigned);
+    x->row_epoch_off = (buf_bytes + 256 + 255) / 256 * 256;
     x->region_bytes = x->row_epoch_off + (size_t)kXchgMaxRows * sizeof(unsigned);
     if (cudaSetDevice(device) != cudaSuccess || cudaMalloc(&x->region, x->region_bytes) != cudaSuccess ||
         cudaMemset(x->region, 0, x->region_bytes) != cudaSuccess ||

@@ -495,30 +495,28 @@ int pickle_cuda_decode_partial_dev(pickle_cuda_t* h, int layer, int n_seqs, size
 }
 
 int pickle_cuda_decode_gather_dev(pickle_cuda_t* h, pickle_cuda_xchg_t* x, int layer, int n_seqs, size_t pos,
-                                  const float* q, const float* k, const float* v, size_t dst_offset,
-                                  size_t dst_row_stride, void* stream) {
+                                  const float* q, const float* k, const float* v, float* out, void* stream) {
     int rc = check_layer(h, layer, n_seqs);
     if (rc != PICKLE_OK) return rc;
-    if (!q || !k || !v) return PICKLE_ERR_ARG;
+    if (!q || !k || !v || !out) return PICKLE_ERR_ARG;
+    if ((uintptr_t)out % 16) return PICKLE_ERR_ARG;
     if (pos >= (size_t)h->max_seq || pos >= (size_t)h->rope_len) return PICKLE_ERR_RANGE;
     rc = check_xchg(h, x);
     if (rc != PICKLE_OK) return rc;
-    const size_t row_bytes = (size_t)h->H * h->D * sizeof(float);
-    if (dst_offset % 16 || dst_row_stride % 16 || (n_seqs > 1 && dst_row_stride < row_bytes)) return PICKLE_ERR_ARG;
-    if ((size_t)n_seqs * h->H > (size_t)kXchgMaxRows ||
-        dst_offset + (size_t)(n_seqs - 1) * dst_row_stride + row_bytes > x->buf_bytes)
+    const int n_rows = n_seqs * h->H;
+    if (n_rows > kXchgMaxRows || decode_xchg_bytes(0, x->world, n_rows, h->D) > x->buf_bytes)
         return PICKLE_ERR_RANGE;
     DecodeArgs a;
-    // ao is unused: the partials go to the workspace; any aligned pointer passes the check.
-    rc = decode_args(h, layer, n_seqs, pos, (long long)pos, 1, (long long)pos, q, k, v, h->ws_acc, nullptr,
-                     nullptr, 0, &a);
+    // ao is unused: the partials go to the workspace; `out` passes the alignment check.
+    rc = decode_args(h, layer, n_seqs, pos, (long long)pos, 1, (long long)pos, q, k, v, out, nullptr, nullptr, 0,
+                     &a);
     if (rc != PICKLE_OK) return rc;
     XchgMergeArgs xm;
     memset(&xm, 0, sizeof(xm));
     xm.mode = 0;
     xm.rows_per_z = h->H;
-    xm.dst_offset = dst_offset;
-    xm.dst_row_stride = n_seqs > 1 ? dst_row_stride : row_bytes;
+    xm.row_bytes = (unsigned long long)h->D * 8;
+    xm.out = out;
     return launch_decode_xchg(h, x, a, n_seqs, xm, (cudaStream_t)stream);
 }
 
@@ -533,9 +531,9 @@ int pickle_cuda_decode_seqshard_dev(pickle_cuda_t* h, pickle_cuda_xchg_t* x, int
     if (pos >= (size_t)h->rope_len) return PICKLE_ERR_RANGE;
     rc = check_xchg(h, x);
     if (rc != PICKLE_OK) return rc;
-    const size_t rows = (size_t)n_seqs * h->H;
-    const size_t part_bytes = (rows * (h->D + 2) * sizeof(float) + 15) / 16 * 16;
-    if (rows > (size_t)kXchgMaxRows || 2 * (size_t)x->world * part_bytes > x->buf_bytes) return PICKLE_ERR_RANGE;
+    const int n_rows = n_seqs * h->H;
+    if (n_rows > kXchgMaxRows || decode_xchg_bytes(1, x->world, n_rows, h->D) > x->buf_bytes)
+        return PICKLE_ERR_RANGE;
     DecodeArgs a;
     rc = decode_args(h, layer, n_seqs, pos, (long long)n_local, append ? 1 : 0, (long long)n_local, q, k, v, out,
                      nullptr, nullptr, 1, &a);
@@ -543,9 +541,18 @@ int pickle_cuda_decode_seqshard_dev(pickle_cuda_t* h, pickle_cuda_xchg_t* x, int
     XchgMergeArgs xm;
     memset(&xm, 0, sizeof(xm));
     xm.mode = 1;
-    xm.part_bytes = part_bytes;
+    xm.row_bytes = (unsigned long long)(h->D + 2) * 8;
     xm.out = out;
     return launch_decode_xchg(h, x, a, n_seqs, xm, (cudaStream_t)stream);
+}
+
+int pickle_cuda_decode_xchg_bytes(int sharding, int world, int n_seqs, int n_heads, int head_dim, size_t* bytes) {
+    if ((sharding != PICKLE_CUDA_SHARD_HEADS && sharding != PICKLE_CUDA_SHARD_SEQ) || world < 1 ||
+        world > kXchgMaxRanks || n_seqs < 1 || n_heads < 1 || head_dim < 4 || head_dim % 4 || !bytes)
+        return PICKLE_ERR_ARG;
+    if ((size_t)n_seqs * n_heads > (size_t)kXchgMaxRows) return PICKLE_ERR_RANGE;
+    *bytes = decode_xchg_bytes(sharding == PICKLE_CUDA_SHARD_HEADS ? 0 : 1, world, n_seqs * n_heads, head_dim);
+    return PICKLE_OK;
 }
 
 int pickle_cuda_lse_merge_dev(int n_parts, int n_rows, int head_dim, const float* m_in, const float* l_in,

@@ -8,9 +8,8 @@
 // used directly):
 //   [0, buf_bytes)                 receive buffer
 //   ready[8], done[8], epoch[8]    flags of pickle_cuda_xchg_put_dev, one word per sender
-//   row_ready[8][kXchgMaxRows]     per-row flags of the fused decode exchanges,
-//   row_done[8][kXchgMaxRows]        word [sender][row]
-//   row_epoch[kXchgMaxRows]        this rank's call counter of each row
+//   row_epoch[kXchgMaxRows]        this rank's call counter of each row of the fused
+//                                  decode exchanges (their data words carry the epoch)
 #pragma once
 #include <cstddef>
 #include <cstdint>
@@ -24,7 +23,7 @@ constexpr int kXchgMaxRows = 4096;
 struct pickle_cuda_xchg {
     int rank = 0, world = 0, device = 0;
     size_t buf_bytes = 0, ready_off = 0, done_off = 0, epoch_off = 0, region_bytes = 0;
-    size_t row_ready_off = 0, row_done_off = 0, row_epoch_off = 0;
+    size_t row_epoch_off = 0;
     unsigned char* region = nullptr;                 // this rank's allocation
     unsigned char* peer[kXchgMaxRanks] = {};         // mapped regions (peer[rank] = region)
     bool opened[kXchgMaxRanks] = {};
@@ -38,7 +37,7 @@ struct pickle_cuda_xchg {
 // What an exchanging kernel needs to reach every rank's region.
 struct XchgPeers {
     unsigned char* base[kXchgMaxRanks];
-    unsigned long long row_ready_off, row_done_off, row_epoch_off;
+    unsigned long long row_epoch_off;
     unsigned long long wait_ns;
     int rank, world;
 };
@@ -46,8 +45,6 @@ struct XchgPeers {
 inline XchgPeers xchg_peers(const pickle_cuda_xchg* x) {
     XchgPeers p{};
     for (int r = 0; r < x->world; ++r) p.base[r] = x->peer[r];
-    p.row_ready_off = x->row_ready_off;
-    p.row_done_off = x->row_done_off;
     p.row_epoch_off = x->row_epoch_off;
     p.wait_ns = x->wait_ns;
     p.rank = x->rank;
@@ -63,20 +60,4 @@ PCU_DEV unsigned ld_acquire_sys(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
-}
-
-// Wait until *f has reached epoch e (counters only grow, wrap-safe);
-// false after wait_ns.
-PCU_DEV bool wait_epoch(const unsigned* f, unsigned e, unsigned long long wait_ns) {
-    if ((int)(ld_acquire_sys(f) - e) >= 0) return true;
-    const uint64_t t0 = global_timer_ns();
-    for (;;) {
-        if ((int)(ld_acquire_sys(f) - e) >= 0) return true;
-        if (global_timer_ns() - t0 > wait_ns) return false;
-    }
-}
-
-// Word [sender][row] of a region's per-row flag array at `off`.
-PCU_DEV unsigned* row_flag(unsigned char* region, unsigned long long off, int sender, int row) {
-    return reinterpret_cast<unsigned*>(region + off) + (size_t)sender * kXchgMaxRows + row;
 }

@@ -329,7 +329,7 @@ def bench_head_sharded(w, rank, world, device, steps, warmup):
     scaling)."""
     import torch
     import torch.distributed as dist
-    from .api import PickleCuda
+    from .api import SHARD_HEADS, PickleCuda, decode_xchg_bytes
     (h0, h1), (k0, k1) = head_shard(w, world, rank)
     H, HK = h1 - h0, k1 - k0
     cu = PickleCuda(1, H, HK, w.D, w.ctx + 1, rope_theta=w.theta, n_seqs=w.B, device=device)
@@ -342,12 +342,11 @@ def bench_head_sharded(w, rank, world, device, steps, warmup):
 
     hs_nccl = HeadShardedDecode(w.B, w.H, w.HK, w.D, rank, world, compute, device=device)
     nccl_ms = _timed(lambda: hs_nccl.step(q, k, v), steps, warmup, device, graph=True)
-    x = open_exchange(rank, world, w.B * w.H * w.D * 4, device)
-    out = x.buffer((w.B, w.H, w.D))
+    x = open_exchange(rank, world, decode_xchg_bytes(SHARD_HEADS, world, w.B, H, w.D), device)
+    out = torch.empty((w.B, w.H, w.D), device=torch.device("cuda", device))
 
     def fused():
-        cu.decode_gather_dev(x, 0, w.B, w.ctx, q, k, v, h0 * w.D * 4, w.H * w.D * 4,
-                             torch.cuda.current_stream(device))
+        cu.decode_gather_dev(x, 0, w.B, w.ctx, q, k, v, out, torch.cuda.current_stream(device))
 
     ms = _timed(fused, steps, warmup, device, graph=True)
     local = torch.empty((w.B, H, w.D), device=torch.device("cuda", device))
@@ -392,7 +391,7 @@ def bench_seq_sharded(w, rank, world, device, steps, warmup):
     one GPU and times that."""
     import torch
     import torch.distributed as dist
-    from .api import PeerExchange, PickleCuda, lse_merge_packed_dev
+    from .api import SHARD_SEQ, PickleCuda, decode_xchg_bytes, lse_merge_packed_dev
     p0, p1 = seq_shard(w.ctx, world, rank)
     n_local = p1 - p0
     append = rank == world - 1
@@ -411,7 +410,7 @@ def bench_seq_sharded(w, rank, world, device, steps, warmup):
 
     ss_nccl = SeqShardedDecode(w.B, w.H, w.D, w.ctx, rank, world, compute, merge=merge, device=device)
     nccl_ms = _timed(lambda: ss_nccl.step(q, k, v), steps, warmup, device, graph=True)
-    x = open_exchange(rank, world, PeerExchange.seqshard_bytes(world, w.B, w.H, w.D), device)
+    x = open_exchange(rank, world, decode_xchg_bytes(SHARD_SEQ, world, w.B, w.H, w.D), device)
     out = torch.empty((w.B, w.H, w.D), device=torch.device("cuda", device))
 
     def fused():

@@ -17,6 +17,13 @@ The data of a [out][in] weight is row-major with `in` contiguous, which is
 how pickle_fast_matmul_f32 reads it.
 
 Also returns the 16-token prompt (ids uniform in [3, 32000) from the seed).
+
+With vocab=True the file also carries a tokenizer.ggml.* vocabulary of
+32000 pieces, so the reference's own CLI (`pickle infer`, which tokenises
+its prompt with pickle_tok_init / pickle_tok_encode,
+src/pickle_tokenizer.c:162-470) can run the model: <unk>, <s>, </s>
+(control), the 256 byte-fallback pieces <0x00>..<0xFF>, then distinct
+word pieces. The weights, and so every logit, are the same either way.
 """
 import struct
 import sys
@@ -26,7 +33,7 @@ import numpy as np
 HIDDEN, N_LAYERS, N_HEADS, N_KV_HEADS, HEAD_DIM = 288, 6, 6, 6, 48
 FFN, VOCAB, CTX, THETA, EPS = 768, 32000, 256, 10000.0, 1e-5
 ALIGN = 32
-GGUF_U32, GGUF_F32, GGUF_BOOL, GGUF_STR = 4, 6, 7, 8
+GGUF_U32, GGUF_I32, GGUF_F32, GGUF_BOOL, GGUF_STR, GGUF_ARR = 4, 5, 6, 7, 8, 9
 
 
 def _tensors():
@@ -62,6 +69,15 @@ def write_gguf(path, meta, tensors):
         head += _s(key) + struct.pack("<I", typ)
         if typ == GGUF_STR:
             head += _s(val)
+        elif typ == GGUF_ARR:
+            etyp, items = val
+            head += struct.pack("<IQ", etyp, len(items))
+            if etyp == GGUF_STR:
+                head += b"".join(_s(x) for x in items)
+            elif etyp == GGUF_F32:
+                head += struct.pack(f"<{len(items)}f", *items)
+            else:
+                head += struct.pack(f"<{len(items)}i", *items)
         elif typ == GGUF_U32:
             head += struct.pack("<I", val)
         elif typ == GGUF_F32:
@@ -106,9 +122,32 @@ def llama_meta(n_layers, hidden, ffn, n_heads, n_kv_heads, head_dim, vocab, ctx,
     ]
 
 
-def write_model(path, seed=0):
+BOS_ID, EOS_ID, UNK_ID = 1, 2, 0
+
+
+def vocab_meta(vocab=VOCAB):
+    """tokenizer.ggml.* keys: control pieces, byte fallback, distinct word pieces."""
+    pieces = ["<unk>", "<s>", "</s>"] + [f"<0x{b:02X}>" for b in range(256)]
+    types = [2, 3, 3] + [6] * 256
+    pieces += ["\u2581w%05d" % i for i in range(len(pieces), vocab)]
+    types += [1] * (vocab - len(types))
+    scores = [0.0] * 3 + [0.0] * 256 + [-float(i) for i in range(259, vocab)]
+    return [
+        ("tokenizer.ggml.model", GGUF_STR, "llama"),
+        ("tokenizer.ggml.tokens", GGUF_ARR, (GGUF_STR, pieces)),
+        ("tokenizer.ggml.scores", GGUF_ARR, (GGUF_F32, scores)),
+        ("tokenizer.ggml.token_type", GGUF_ARR, (GGUF_I32, types)),
+        ("tokenizer.ggml.bos_token_id", GGUF_U32, BOS_ID),
+        ("tokenizer.ggml.eos_token_id", GGUF_U32, EOS_ID),
+        ("tokenizer.ggml.unknown_token_id", GGUF_U32, UNK_ID),
+    ]
+
+
+def write_model(path, seed=0, vocab=False):
     rng = np.random.Generator(np.random.Philox(seed))
     meta = llama_meta(N_LAYERS, HIDDEN, FFN, N_HEADS, N_KV_HEADS, HEAD_DIM, VOCAB, CTX)
+    if vocab:
+        meta += vocab_meta()
     tensors = _tensors()
     datas = [rng.standard_normal(int(np.prod(shape)), dtype=np.float32) * np.float32(0.02)
              for _, shape in tensors]

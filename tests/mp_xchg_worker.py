@@ -13,7 +13,7 @@ import torch.distributed as dist
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 from lestramanika_b200 import PickleCuda, lse_merge_packed_dev  # noqa: E402
-from lestramanika_b200.api import PeerExchange  # noqa: E402
+from lestramanika_b200.api import SHARD_HEADS, SHARD_SEQ, decode_xchg_bytes  # noqa: E402
 from lestramanika_b200.dist import HeadShardedDecode, SeqShardedDecode, init_group, open_exchange  # noqa: E402
 from lestramanika_b200.workloads import Decode, head_shard, seq_shard  # noqa: E402
 
@@ -40,14 +40,13 @@ def main():
         cu.decode_batch_dev(0, w.B, w.ctx, qq, kk, vv, out, torch.cuda.current_stream(dev_i))
 
     x = open_exchange(rank, world, w.B * w.H * w.D * 4, dev_i)
-    xf = open_exchange(rank, world, w.B * w.H * w.D * 4, dev_i)
-    fused_out = xf.buffer((w.B, w.H, w.D))
+    xf = open_exchange(rank, world, decode_xchg_bytes(SHARD_HEADS, world, w.B, h1 - h0, w.D), dev_i)
+    fused_out = torch.empty((w.B, w.H, w.D), device=dev)
     a = HeadShardedDecode(w.B, w.H, w.HK, w.D, rank, world, compute, device=dev_i)
     b = HeadShardedDecode(w.B, w.H, w.HK, w.D, rank, world, compute, device=dev_i, exchange=x)
 
     def fused_step(qq, kk, vv):
-        cu.decode_gather_dev(xf, 0, w.B, w.ctx, qq, kk, vv, h0 * w.D * 4, w.H * w.D * 4,
-                             torch.cuda.current_stream(dev_i))
+        cu.decode_gather_dev(xf, 0, w.B, w.ctx, qq, kk, vv, fused_out, torch.cuda.current_stream(dev_i))
 
     for step in range(3):
         q = torch.randn((w.B, h1 - h0, w.D), generator=g, device=dev)
@@ -99,7 +98,7 @@ def main():
     sa = SeqShardedDecode(w.B, w.H, w.D, w.ctx, rank, world, pcompute, merge=merge, device=dev_i)
     x2 = open_exchange(rank, world, world * sa.stride * 4, dev_i)
     sb = SeqShardedDecode(w.B, w.H, w.D, w.ctx, rank, world, pcompute, merge=merge, device=dev_i, exchange=x2)
-    xs = open_exchange(rank, world, PeerExchange.seqshard_bytes(world, w.B, w.H, w.D), dev_i)
+    xs = open_exchange(rank, world, decode_xchg_bytes(SHARD_SEQ, world, w.B, w.H, w.D), dev_i)
     sout = torch.empty((w.B, w.H, w.D), device=dev)
 
     def fused_seq(qq, kk, vv):

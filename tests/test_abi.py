@@ -58,3 +58,13 @@ def test_hook_patch_is_minimal():
     body = [l for l in patch.splitlines() if l.startswith(("+", "-")) and not l.startswith(("+++", "---"))]
     assert all(l.startswith("+") for l in body)
     assert sum(l.startswith("+#ifdef PICKLE_CUDA") for l in body) == 3
+
+
+def test_python_handles_have_their_methods():
+    """The Python mirror's handle classes expose every call the tests and the bench use."""
+    for name in ("handle", "open", "attach", "set_wait", "buffer", "put", "sync", "close"):
+        assert callable(getattr(api.PeerExchange, name, None)), name
+    for name in ("decode_batch_dev", "decode_gather_dev", "decode_seqshard_dev", "decode_partial_dev",
+                 "prefill_dev", "sync", "close", "kv_tensors"):
+        assert callable(getattr(api.PickleCuda, name, None)), name
+    assert callable(api.decode_xchg_bytes)

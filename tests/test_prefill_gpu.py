@@ -159,3 +159,32 @@ def test_prefill_bf16_batched_long_prompt_matches_f32_path():
     assert np.isfinite(outs[1]).all()
     err = float(np.max(np.abs(outs[1] - outs[0])))
     assert err <= BF16_ABS_TOL, err
+
+
+def test_prefill_bf16_exact_c3_config_against_oracle():
+    """The benchmark's prefill configuration as a whole: B=4 sequences x
+    T=2048 tokens x 32 MHA heads (Llama-2-7B-shaped), one pickle_cuda_prefill_dev
+    call on the tensor cores. Two heads of every sequence (a different pair
+    per sequence) are checked against the oracle's token-by-token prefill
+    (src/pickle_fast.c:1881 over :1910-2094) within the BF16 bar, and the
+    KV-cache rows the call wrote for those heads equal the oracle's rotated k
+    (1e-5) and v (exactly)."""
+    B, T, H, HK, D, theta = 4, 2048, 32, 32, 128, 10000.0
+    dev = torch.device("cuda", 0)
+    q, k, v = normal(14, (B, T, H, D), 1), normal(14, (B, T, HK, D), 2), normal(14, (B, T, HK, D), 3)
+    qd, kd, vd = (torch.from_numpy(x).to(dev) for x in (q, k, v))
+    cu = PickleCuda(1, H, HK, D, T, rope_theta=theta, n_seqs=B)
+    ao = torch.full((B, T, H, D), float("nan"), device=dev)
+    cu.prefill_dev(0, B, 0, T, qd, kd, vd, ao, PREFILL_BF16)
+    cu.sync()
+    kt, vt = cu.kv_tensors(0)
+    got = ao.cpu().numpy()
+    assert np.isfinite(got).all()
+    for b, heads in enumerate(((0, 31), (7, 20), (13, 26), (3, 17))):
+        for h in heads:
+            ref, kc, vc = _oracle_prefill(1, 1, D, T, theta, q[b, :, h], k[b, :, h], v[b, :, h])
+            err = float(np.max(np.abs(got[b, :, h] - ref)))
+            assert err <= BF16_ABS_TOL, (b, h, err)
+            np.testing.assert_allclose(kt[b, h].cpu().numpy(), kc[:, 0], atol=1e-5, rtol=0)
+            np.testing.assert_array_equal(vt[b, h].cpu().numpy(), vc[:, 0])
+    cu.close()

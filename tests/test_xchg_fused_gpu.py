@@ -2,7 +2,8 @@
 (pickle_cuda_decode_gather_dev, pickle_cuda_decode_seqshard_dev), on one GPU:
 
 * with one rank, the data path - split partials, the fused merge, the
-  stores into the exchange buffer, the per-row flags - must reproduce the
+  epoch-tagged stores into the exchange buffer and the assembly of the
+  output from it - must reproduce the
   unsharded decode and the oracle (src/pickle_fast.c:1910-2094), on calls in
   a row and from a replayed CUDA graph;
 * failure detection: a rank whose peer never arrives gives up after the
@@ -18,7 +19,7 @@ import torch
 import oracle
 from gpu_util import assert_rel, normal
 from lestramanika_b200 import PickleCuda
-from lestramanika_b200.api import PeerExchange, PickleError
+from lestramanika_b200.api import SHARD_HEADS, SHARD_SEQ, PeerExchange, PickleError, decode_xchg_bytes
 
 pytestmark = pytest.mark.gpu
 
@@ -50,11 +51,11 @@ def test_gather_one_rank_matches_decode_and_oracle(B, H, HK, ctx):
     D = 128
     cu, kc, vc = _handle_with_cache(B, H, HK, D, ctx, 300 + ctx)
     ref_cu, _, _ = _handle_with_cache(B, H, HK, D, ctx, 300 + ctx)
-    x = PeerExchange(0, 1, B * H * D * 4, 0)
-    out = x.buffer((B, H, D))
+    x = PeerExchange(0, 1, decode_xchg_bytes(SHARD_HEADS, 1, B, H, D), 0)
+    out = torch.empty((B, H, D), device=DEV)
     for step, pos in enumerate((ctx, ctx + 1)):                 # two calls in a row
         q, k, v = (normal(310 + step, s, 3) for s in ((B, H, D), (B, HK, D), (B, HK, D)))
-        cu.decode_gather_dev(x, 0, B, pos, _dev(q), _dev(k), _dev(v), 0, H * D * 4)
+        cu.decode_gather_dev(x, 0, B, pos, _dev(q), _dev(k), _dev(v), out)
         want = torch.empty((B, H, D), device=DEV)
         ref_cu.decode_batch_dev(0, B, pos, _dev(q), _dev(k), _dev(v), want)
         cu.sync()
@@ -71,18 +72,18 @@ def test_gather_graph_replays_stay_correct():
     B, H, HK, D, ctx = 2, 32, 8, 128, 1500
     cu, _, _ = _handle_with_cache(B, H, HK, D, ctx, 41)
     ref_cu, _, _ = _handle_with_cache(B, H, HK, D, ctx, 41)
-    x = PeerExchange(0, 1, B * H * D * 4, 0)
-    out = x.buffer((B, H, D))
+    x = PeerExchange(0, 1, decode_xchg_bytes(SHARD_HEADS, 1, B, H, D), 0)
+    out = torch.empty((B, H, D), device=DEV)
     q, k, v = (_dev(normal(42, s, 1)) for s in ((B, H, D), (B, HK, D), (B, HK, D)))
     want = torch.empty((B, H, D), device=DEV)
     ref_cu.decode_batch_dev(0, B, ctx, q, k, v, want)
     st = torch.cuda.Stream(device=DEV)
     with torch.cuda.stream(st):
-        cu.decode_gather_dev(x, 0, B, ctx, q, k, v, 0, H * D * 4, st)      # warm-up outside capture
+        cu.decode_gather_dev(x, 0, B, ctx, q, k, v, out, st)                # warm-up outside capture
         st.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=st):
-            cu.decode_gather_dev(x, 0, B, ctx, q, k, v, 0, H * D * 4, torch.cuda.current_stream())
+            cu.decode_gather_dev(x, 0, B, ctx, q, k, v, out, torch.cuda.current_stream())
     for rep in range(3):
         out.zero_()
         g.replay()
@@ -100,7 +101,7 @@ def test_seqshard_one_rank_matches_decode_and_oracle(B, H, HK, ctx, n_local):
     D = 128
     cu, kc, vc = _handle_with_cache(B, H, HK, D, ctx, 500 + ctx)
     ref_cu, _, _ = _handle_with_cache(B, H, HK, D, ctx, 500 + ctx)
-    x = PeerExchange(0, 1, PeerExchange.seqshard_bytes(1, B, H, D), 0)
+    x = PeerExchange(0, 1, decode_xchg_bytes(SHARD_SEQ, 1, B, H, D), 0)
     out = torch.empty((B, H, D), device=DEV)
     want = torch.empty((B, H, D), device=DEV)
     for step, pos in enumerate((ctx, ctx + 1)):
@@ -121,29 +122,32 @@ def test_seqshard_one_rank_matches_decode_and_oracle(B, H, HK, ctx, n_local):
 def test_absent_peer_times_out_breaks_the_exchange_and_leaves_the_gpu_usable():
     B, H, HK, D, ctx = 2, 16, 4, 128, 300
     cu, kc, vc = _handle_with_cache(B, H, HK, D, ctx, 61)
-    nb = B * H * D * 4
+    nb = decode_xchg_bytes(SHARD_HEADS, 2, B, H, D)
     x0, x1 = PeerExchange(0, 2, nb, 0), PeerExchange(1, 2, nb, 0)
     x0.attach(1, x1)                        # rank 1 exists but never makes the call
     x0.set_wait(20_000_000)                 # 20 ms
     q, k, v = (normal(62, s, 1) for s in ((B, H, D), (B, HK, D), (B, HK, D)))
-    cu.decode_gather_dev(x0, 0, B, ctx, _dev(q), _dev(k), _dev(v), 0, H * D * 4)
+    # This handle plays rank 0 of a KV-head shard of 2 x H heads.
+    out = torch.empty((B, 2 * H, D), device=DEV)
+    cu.decode_gather_dev(x0, 0, B, ctx, _dev(q), _dev(k), _dev(v), out)
     cu.sync()                               # the decode itself is fine
     with pytest.raises(PickleError) as e:
         x0.sync()
     assert e.value.code == -9
     with pytest.raises(PickleError) as e:   # broken: the ranks' counters no longer agree
-        cu.decode_gather_dev(x0, 0, B, ctx, _dev(q), _dev(k), _dev(v), 0, H * D * 4)
+        cu.decode_gather_dev(x0, 0, B, ctx, _dev(q), _dev(k), _dev(v), out)
     assert e.value.code == -9
     # The unfused exchange gives up the same way.
     y0, y1 = PeerExchange(0, 2, nb, 0), PeerExchange(1, 2, nb, 0)
     y0.attach(1, y1)
     y0.set_wait(20_000_000)
     src = torch.zeros((B, H, D), device=DEV)
-    y0.put(src, 1, nb // 2, nb // 2, 0, nb // 2)
+    row = B * H * D * 4
+    y0.put(src, 1, row, row, 0, row)
     with pytest.raises(PickleError):
         y0.sync()
     with pytest.raises(PickleError):
-        y0.put(src, 1, nb // 2, nb // 2, 0, nb // 2)
+        y0.put(src, 1, row, row, 0, row)
     # The GPU still decodes correctly.
     ao = torch.empty((B, H, D), device=DEV)
     cu.decode_batch_dev(0, B, ctx, _dev(q), _dev(k), _dev(v), ao)
