@@ -843,6 +843,17 @@ def matvec_cpu_baseline(types=("F16", "Q8_0", "Q6_K", "Q4_K", "Q4_0"), seconds=2
 REF_CACHE_BYTES = 1 << 30     # distinct host caches cycled through by the CPU reference: above the host's L3
 
 
+def host_cpu():
+    """The host's CPU model (first /proc/cpuinfo entry), for the baseline record."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.lower().startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
 def config_of(w):
     """The workload description both arms print (identical dicts)."""
     return {"workload": w.name, "B": w.B, "H": w.H, "HK": w.HK, "D": w.D, "ctx": w.ctx,
@@ -893,7 +904,7 @@ def ref_decode(w, steps, warmup):
     dt = time.perf_counter() - t0
     blk.close()
     return {"value": w.kv_bytes * steps / dt / 1e9, "unit": "GB/s", "cores": ncores, "kind": kind,
-            "ms_per_step": dt / steps * 1e3,
+            "ms_per_step": dt / steps * 1e3, "cpu": host_cpu(),
             "sample": f"{steps} whole steps of {w.name}: {w.B} calls each, one per sequence, cycling over "
                       f"{R} distinct {per_layer / 1e6:.0f} MB caches ({R * per_layer / 1e9:.2f} GB)"}
 
@@ -928,7 +939,7 @@ def prefill_cpu(w, n_pos=16):
     blk.close()
     ms = per_call * w.B * w.T * 1e3
     return {"value": w.flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "kind": kind,
-            "cores": int(os.environ["OMP_NUM_THREADS"]),
+            "cores": int(os.environ["OMP_NUM_THREADS"]), "cpu": host_cpu(),
             "sample": f"{n_pos} block calls at positions spread over the {w.T}-token prompt, "
                       f"extrapolated to {w.B} x {w.T} calls"}
 
@@ -1128,7 +1139,7 @@ def run_reference(args, rank):
            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
            "data": "synthetic N(0,1) cache and q/k/v, seeded", "config": config_of(w),
            "cpu_baseline": {"value": r["value"], "unit": "GB/s", "cores": r["cores"], "kind": r["kind"],
-                            "sample": r["sample"]},
+                            "sample": r["sample"], "cpu": r["cpu"]},
            "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 

@@ -101,6 +101,26 @@ PCU_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_d
 
 PCU_DEV bool tid_is_first() { return threadIdx.x == 0; }
 
+// NeoX rotation of one float4 chunk pair (x0 = x[i..i+3], x1 = x[i+half..])
+// by the table row's sin/cos (src/pickle_fast.c:1917-1924):
+//   lo = c*x0 - s*x1, hi = s*x0 + c*x1,
+// with the roundings fixed (one product, then one fused multiply-add), so
+// every kernel that writes rotated rows writes the same bits.
+PCU_DEV void rope_pair4(const float4& x0, const float4& x1, const float4& sn, const float4& cs, float4& lo,
+                        float4& hi) {
+    lo = make_float4(fmaf(cs.x, x0.x, -(sn.x * x1.x)), fmaf(cs.y, x0.y, -(sn.y * x1.y)),
+                     fmaf(cs.z, x0.z, -(sn.z * x1.z)), fmaf(cs.w, x0.w, -(sn.w * x1.w)));
+    hi = make_float4(fmaf(sn.x, x0.x, cs.x * x1.x), fmaf(sn.y, x0.y, cs.y * x1.y),
+                     fmaf(sn.z, x0.z, cs.z * x1.z), fmaf(sn.w, x0.w, cs.w * x1.w));
+}
+
+// Four floats as BF16 (round to nearest even), packed for one 8-byte store.
+PCU_DEV uint2 pack_bf16x4(float4 x, float scale) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(x.x * scale, x.y * scale);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(x.z * scale, x.w * scale);
+    return make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+}
+
 PCU_DEV void record_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
 }

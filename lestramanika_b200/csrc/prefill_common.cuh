@@ -64,12 +64,6 @@ __global__ void rope_append_kernel(const RopeAppendArgs a) {
     }
 }
 
-PCU_DEV uint2 pack_bf16x4(float4 x, float scale) {
-    __nv_bfloat162 lo = __floats2bfloat162_rn(x.x * scale, x.y * scale);
-    __nv_bfloat162 hi = __floats2bfloat162_rn(x.z * scale, x.w * scale);
-    return make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
-}
-
 // Same result as rope_append_kernel with 16-byte accesses: one thread takes a
 // rotation pair of float4 chunks (d..d+3, d+half..d+half+3), an unrotated
 // float4 chunk past 2*half, or a float4 chunk of v. Needs D % 4 == 0 and
@@ -96,12 +90,8 @@ __global__ void __launch_bounds__(128) rope_append_vec_kernel(const RopeAppendAr
                 d_hi = d_lo + half;
                 const float4 x0 = *reinterpret_cast<const float4*>(row + d_lo);
                 const float4 x1 = *reinterpret_cast<const float4*>(row + d_hi);
-                const float4 sv = sr[c], cv = cr[c];
                 // src/pickle_fast.c:1917-1924: x' = c*x0 - s*x1, x'' = s*x0 + c*x1
-                lo_out = make_float4(cv.x * x0.x - sv.x * x1.x, cv.y * x0.y - sv.y * x1.y,
-                                     cv.z * x0.z - sv.z * x1.z, cv.w * x0.w - sv.w * x1.w);
-                hi_out = make_float4(sv.x * x0.x + cv.x * x1.x, sv.y * x0.y + cv.y * x1.y,
-                                     sv.z * x0.z + cv.z * x1.z, sv.w * x0.w + cv.w * x1.w);
+                rope_pair4(x0, x1, sr[c], cr[c], lo_out, hi_out);
             } else {
                 d_lo = 2 * half + 4 * (c - NP);
                 lo_out = *reinterpret_cast<const float4*>(row + d_lo);

@@ -187,13 +187,6 @@ PCU_DEV void tmem_st64(uint32_t taddr, const uint32_t (&v)[64]) {
         : "memory");
 }
 
-PCU_DEV void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
-        :: "r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-        : "memory");
-}
-
 PCU_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 2^x with one MUFU instruction (relative error ~2^-22, far below BF16 P).
@@ -201,6 +194,13 @@ PCU_DEV float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// max(a, b, c) in one sm_100 instruction (three-input max.f32).
+PCU_DEV float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
 }
 
 // Two FP32 operations per instruction (sm_100 f32x2): same rounding as two
@@ -470,31 +470,24 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
                     for (int c = 0; c < BN; ++c)
                         if (k0 + c > q || k0 + c >= a.T) s[c] = -INFINITY;
                 }
-                float mx[8];
+                // Row maximum with three-input max (sm_100): 63 instructions
+                // for 128 columns, four independent chains.
+                float mx[4];
                 #pragma unroll
-                for (int i = 0; i < 8; ++i) mx[i] = s[i];
+                for (int i = 0; i < 4; ++i) mx[i] = s[i];
                 #pragma unroll
-                for (int c = 8; c < BN; ++c) mx[c & 7] = fmaxf(mx[c & 7], s[c]);
-                const float m_all = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                          fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                for (int c = 4; c < BN - 4; c += 8) {
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) mx[i] = fmax3(mx[i], s[c + 2 * i], s[c + 2 * i + 1]);
+                }
+                const float m_all = fmax3(fmax3(mx[0], s[BN - 4], s[BN - 3]), fmax3(mx[1], s[BN - 2], s[BN - 1]),
+                                          fmaxf(mx[2], mx[3]));
                 const float m_tile = m_all * a.scale_log2;
                 float alpha = 1.0f;
                 const bool grow = m_tile > m_run + RESCALE_THRESHOLD || m_run == -INFINITY;
                 if (grow) {
                     alpha = fast_exp2(m_run - m_tile);
                     m_run = m_tile;
-                }
-                // S_FULL_X(j) implies PV_X(j-1) finished: O_X is stable here.
-                if (j > 0 && __any_sync(0xffffffffu, grow)) {
-                    #pragma unroll
-                    for (int c = 0; c < HD / 32; ++c) {
-                        float o[32];
-                        tmem_ld32(o_tm + c * 32, o);
-                        uint32_t ou[32];
-                        #pragma unroll
-                        for (int i = 0; i < 32; ++i) ou[i] = __float_as_uint(o[i] * alpha);
-                        tmem_st32u(o_tm + c * 32, ou);
-                    }
                 }
                 // Column pairs: x * scale - m and the row-sum additions as f32x2
                 // (one instruction per pair instead of two).
@@ -513,6 +506,20 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
                 const float2 t = fadd2(fadd2(sm2[0], sm2[1]), fadd2(sm2[2], sm2[3]));
                 l_run = l_run * alpha + (t.x + t.y);
                 tmem_st64(s_tm, pk);                              // P_X over S_X columns [0, 64)
+                // O_X rescale, once the S row is dead (held together with the S
+                // row it spilled to local memory): S_FULL_X(j) implies PV_X(j-1)
+                // finished, and PV_X(j) waits for this warp's P_FULL arrival
+                // below, so O_X is stable here.
+                if (j > 0 && __any_sync(0xffffffffu, grow)) {
+                    #pragma unroll
+                    for (int c = 0; c < HD / 32; ++c) {
+                        float o[32];
+                        tmem_ld32(o_tm + c * 32, o);
+                        #pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                        tmem_st32(o_tm + c * 32, o);
+                    }
+                }
                 tmem_st_wait();
                 tc_fence_before();
                 __syncwarp();

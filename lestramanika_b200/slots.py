@@ -18,7 +18,10 @@ n_seqs cache slots of one PickleCuda handle:
   * release(req) returns the slot.
 
 Positions live on the host; the device copies of the (position, slot)
-arrays of a batch are rebuilt when the batch or the positions change.
+arrays of a batch are rebuilt when the batch or the positions change. They
+are made on the stream the decode runs on, and marked as used there, so
+the caching allocator does not hand their memory to another tensor while
+a decode on that stream may still read it.
 """
 
 
@@ -70,22 +73,30 @@ class KVSlots:
         self.cu.prefill_slot_dev(layer, self.slot_of[req], self.pos[req], T, q, k, v, ao,
                                  PREFILL_F32 if precision is None else precision, stream)
 
-    def batch_arrays(self, reqs):
-        """Device int32 (positions, slots) of `reqs` and the largest position."""
+    def batch_arrays(self, reqs, stream=None):
+        """Device int32 (positions, slots) of `reqs` and the largest position,
+        made on `stream` (a torch.cuda.Stream; torch's current stream otherwise)."""
         import torch
         key = tuple(reqs)
         if key != self._batch_key:
             pos = [self.pos[r] for r in reqs]
             slots = [self.slot_of[r] for r in reqs]
             dev = torch.device("cuda", self.cu.device)
-            self._dev = (torch.tensor(pos, dtype=torch.int32, device=dev),
-                         torch.tensor(slots, dtype=torch.int32, device=dev), max(pos))
+            st = stream if isinstance(stream, torch.cuda.Stream) else torch.cuda.current_stream(dev)
+            with torch.cuda.stream(st):
+                p = torch.tensor(pos, dtype=torch.int32, device=dev)
+                s = torch.tensor(slots, dtype=torch.int32, device=dev)
+            self._dev = (p, s, max(pos))
             self._batch_key = key
+        if isinstance(stream, torch.cuda.Stream):
+            # A batch made on another stream is also read on this one.
+            self._dev[0].record_stream(stream)
+            self._dev[1].record_stream(stream)
         return self._dev
 
     def decode(self, layer, reqs, q, k, v, ao, stream=None):
         """One decode step of `reqs` (q [n][H][D], k/v [n][HK][D], ao [n][H][D])."""
-        pos, slots, max_pos = self.batch_arrays(reqs)
+        pos, slots, max_pos = self.batch_arrays(reqs, stream)
         if max_pos >= self.cu.max_seq:
             raise SlotError("a request is at max_seq")
         self.cu.decode_ragged_dev(layer, pos, q, k, v, ao, slots=slots, max_pos=max_pos, stream=stream)
