@@ -203,13 +203,24 @@ PCU_DEV void rs_level(float (&v)[32], int lane) {
     }
 }
 
-// After this, lane l holds the warp-wide sum of value index l.
+// The same level when lane l's values are stored at index (value ^ l): every
+// lane keeps its lower half and sends its upper half, with no selects.
+template <int W>
+PCU_DEV void rs_level_xor(float (&v)[32]) {
+    #pragma unroll
+    for (int i = 0; i < W; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i + W], W);
+}
+
+// After this, lane l holds the warp-wide sum of value index l. Value indices
+// are row * GS + head; lane l stores the value of row r at index
+// ((r ^ (l / GS)) * GS + head), so the row levels (W >= GS) run select-free.
+template <int GS>
 PCU_DEV float reduce_scatter32(float (&v)[32], int lane) {
-    rs_level<16>(v, lane);
-    rs_level<8>(v, lane);
-    rs_level<4>(v, lane);
-    rs_level<2>(v, lane);
-    rs_level<1>(v, lane);
+    rs_level_xor<16>(v);
+    if constexpr (GS <= 8) rs_level_xor<8>(v); else rs_level<8>(v, lane);
+    if constexpr (GS <= 4) rs_level_xor<4>(v); else rs_level<4>(v, lane);
+    if constexpr (GS <= 2) rs_level_xor<2>(v); else rs_level<2>(v, lane);
+    if constexpr (GS <= 1) rs_level_xor<1>(v); else rs_level<1>(v, lane);
     return v[0];
 }
 
@@ -222,14 +233,16 @@ PCU_DEV void attend_rows(const float* __restrict__ Kw, const float* __restrict__
                          float* pw, float scale, int lane) {
     using C = DecodeCfg<D, G>;
     float vals[32];
+    const int rx = lane / G;                         // this lane's row permutation (reduce_scatter32)
     #pragma unroll
     for (int r = 0; r < C::RPW; ++r) {
+        const int row = r ^ rx;                      // the row whose values go to index r * G + g
         float4 kr[C::CPL];
         #pragma unroll
         for (int i = 0; i < C::CPL; ++i) {
             const int c = lane + 32 * i;
-            kr[i] = (r < nvalid && c < C::NCH) ? reinterpret_cast<const float4*>(Kw + r * D)[c]
-                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            kr[i] = (row < nvalid && c < C::NCH) ? reinterpret_cast<const float4*>(Kw + row * D)[c]
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         #pragma unroll
         for (int g = 0; g < G; ++g) {
@@ -242,7 +255,7 @@ PCU_DEV void attend_rows(const float* __restrict__ Kw, const float* __restrict__
             vals[r * G + g] = s2.x + s2.y;
         }
     }
-    float s = reduce_scatter32(vals, lane);          // lane l: row l / G, head l % G
+    float s = reduce_scatter32<G>(vals, lane);       // lane l: row l / G, head l % G
     s = (lane / G < nvalid) ? s * scale : -INFINITY;
     float tmax = s;
     #pragma unroll
