@@ -285,8 +285,13 @@ PCU_DEV void attend_rows(const float* __restrict__ Kw, const float* __restrict__
     for (int r = 0; r < C::RPW; ++r) {
         if (r < nvalid) {
             float pr[G];
-            #pragma unroll
-            for (int g = 0; g < G; ++g) pr[g] = pw[r * G + g];
+            if constexpr (G == 4) {         // one 16-byte shared load (pw rows are 16-byte aligned)
+                const float4 p4 = *reinterpret_cast<const float4*>(pw + r * 4);
+                pr[0] = p4.x; pr[1] = p4.y; pr[2] = p4.z; pr[3] = p4.w;
+            } else {
+                #pragma unroll
+                for (int g = 0; g < G; ++g) pr[g] = pw[r * G + g];
+            }
             #pragma unroll
             for (int i = 0; i < C::CPL; ++i) {
                 const int c = lane + 32 * i;
