@@ -175,14 +175,7 @@ extern "C" PICKLE_CUDA_API int pickle_cuda_decode_noalloc(
         if (max_s > kMaxSplits) max_s = kMaxSplits;
         const long long cap = row_cap / (groups * G);
         if (max_s > cap) max_s = cap;
-        double best = -1.0;
-        for (long long s = 1; s <= max_s; ++s) {
-            const long long chunk = (hist + s - 1) / s;
-            if ((hist + chunk - 1) / chunk != s) continue;
-            const double waves = (double)(groups * s) / (double)slots;
-            const double score = waves / std::ceil(waves) - 0.002 * (double)s;
-            if (score > best + 1e-9) { best = score; n_splits = (int)s; }
-        }
+        n_splits = plan_decode_splits(groups, hist, slots, max_s, G, head_dim);
     }
     const size_t part_rows = (size_t)groups * G * n_splits;
 

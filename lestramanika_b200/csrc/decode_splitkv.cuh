@@ -30,7 +30,15 @@
 // it is launched as a programmatic dependent of the split kernel, so its
 // CTAs are resident before the split kernel retires and start merging as
 // soon as the partials are visible. Spreading the merge over one CTA per
-// output row keeps it off a single SM's L2 bandwidth.
+// output row keeps it off a single SM's L2 bandwidth (a merge by the last
+// split CTA of each group, which pulls the group's partials through one
+// SM, measured 2-4 us slower a step at B=1 and B=8).
+//
+// The split kernel itself waits in griddepcontrol.wait before its first
+// global access, so it can be launched as a programmatic dependent of the
+// kernel before it on the stream (the previous decode step, or the
+// projection that wrote q / k / v): its CTAs become resident while that
+// kernel's last CTAs run.
 #pragma once
 #include <cfloat>
 #include <cmath>
@@ -85,6 +93,56 @@ constexpr int kMaxSplits = 256;
 // (the extra L2 traffic competes with the ring's own copies), so they
 // take none.
 constexpr int kDefaultL2Ahead = 2;
+
+// Host: the split count for `groups` independent (query, KV head) streams
+// of `hist` cached rows of D floats, on `slots` resident CTA slots, among
+// split counts 1..max_s that cut hist into exactly that many pieces. A
+// plan's estimated time: each wave of CTAs streams its K/V chunk at
+// min(one CTA's rate, HBM bandwidth / CTAs in the wave), each wave costs a
+// fixed ramp, and several splits add the merge launch. One CTA (two per SM,
+// eight consumer warps) streams at most ~33 GB/s with four query heads per
+// KV head and ~22 GB/s with eight (issue-bound), so a partial last wave
+// runs at that rate alone, while one wave of fewer CTAs than slots can
+// still fill HBM. The constants were fitted on B200 to split-count sweeps
+// of six decode shapes (GQA 4: B=1/8/64 at ctx 4096, B=1 at ctx 131072;
+// GQA 8: B=2 and B=16 at ctx 32768); in each the plan below picks the
+// measured fastest count.
+inline double decode_plan_time(long long groups, long long hist, long long slots, long long s, int G, int D) {
+    const double hbm = 6.5e12;                          // bytes/s
+    const double cta_rate = G > 4 ? 22e9 : 33e9;        // bytes/s of one CTA
+    const double wave_cost = 3e-6, merge_cost = 4e-6;   // seconds
+    const long long chunk = (hist + s - 1) / s;
+    const long long n = groups * s, full = n / slots, rem = n % slots;
+    const double bytes = (double)chunk * 2.0 * D * sizeof(float);
+    const double full_rate = cta_rate < hbm / (double)slots ? cta_rate : hbm / (double)slots;
+    double t = (double)full * bytes / full_rate;
+    if (rem) {
+        const double rem_rate = cta_rate < hbm / (double)rem ? cta_rate : hbm / (double)rem;
+        t += bytes / rem_rate;
+    }
+    t += wave_cost * (double)(full + (rem ? 1 : 0));
+    if (s > 1) t += merge_cost;
+    return t;
+}
+
+// Among counts within 0.5 % of the fastest estimate, the most splits: where
+// a wave saturates HBM either way, more CTAs hide more latency (measured:
+// 37 splits over 30 at B=1, ctx 4096).
+inline int plan_decode_splits(long long groups, long long hist, long long slots, long long max_s, int G, int D) {
+    if (hist <= 0 || groups <= 0 || slots <= 0) return 1;
+    if (max_s < 1) max_s = 1;
+    auto exact = [&](long long s) { const long long c = (hist + s - 1) / s; return (hist + c - 1) / c == s; };
+    double best_t = -1.0;
+    for (long long s = 1; s <= max_s; ++s) {
+        if (!exact(s)) continue;
+        const double t = decode_plan_time(groups, hist, slots, s, G, D);
+        if (best_t < 0 || t < best_t) best_t = t;
+    }
+    int best = 1;
+    for (long long s = 1; s <= max_s; ++s)
+        if (exact(s) && decode_plan_time(groups, hist, slots, s, G, D) <= best_t * 1.005) best = (int)s;
+    return best;
+}
 
 template <int D, int G>
 struct DecodeCfg {
@@ -337,6 +395,10 @@ decode_splitkv_kernel(const DecodeArgs a) {
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, kvh = blockIdx.y, z = blockIdx.z;
+    // Launched as a programmatic dependent of the kernel before it on the
+    // stream: nothing that kernel writes (q / k / v, the cache) is touched
+    // before it completes.
+    griddep_wait();
     int seq = z / a.n_q;
     const int t = z % a.n_q;
     long long hist = a.hist_len0 + (long long)t * a.hist_step;
@@ -374,7 +436,7 @@ decode_splitkv_kernel(const DecodeArgs a) {
     float m_run = -INFINITY, l_run = 0.f;
     int first_issued = 0;
 
-    griddep_launch_dependents();                        // the merge kernel may take free SM slots now
+    griddep_launch_dependents();                        // the next kernel's CTAs may take free SM slots now
 
     // Prologue. The producer lane sets up the ring and puts the first
     // STAGES tile copies in flight at once; meanwhile the consumer warps
@@ -701,6 +763,7 @@ template <int D>
 __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const MergeArgs a) {
     __shared__ MergeSmem<D> sm;
     const int tid = threadIdx.x, row = blockIdx.x;
+    griddep_launch_dependents();                        // the next decode step's CTAs may become resident
     griddep_wait();                                     // the split kernel's partials are visible
     const float4 T = merge_splits<D>(a, row, sm);
     if (tid < D / 4) {

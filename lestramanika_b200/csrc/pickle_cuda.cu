@@ -34,6 +34,8 @@ struct pickle_cuda_impl;
 struct pickle_cuda {
     int n_layers, H, HK, D, G, half, max_seq, n_seqs, rope_len, device, num_sms;
     int l2_ahead = kDefaultL2Ahead;   // decode tiles kept requested into L2 ahead of the ring
+    int pdl = 1;              // split kernel launched as a programmatic dependent of the kernel before it
+    int force_splits = 0;     // > 0: split count for every decode (tuning sweeps), else planned
     size_t head_stride, seq_stride, layer_stride;   // floats
     float* kc = nullptr;
     float* vc = nullptr;
@@ -118,8 +120,8 @@ int prepare_kernel(pickle_cuda* h, KernelInfo& k) {
 }
 
 // Pick the number of KV splits for `groups` independent (seq, kv_head)
-// streams of `hist` rows: enough CTAs to fill every SM slot, with the CTA
-// count close to a whole number of waves, and at least two tiles a split.
+// streams of `hist` rows (the cost model of plan_decode_splits), with at
+// least two tiles a split and no more partial rows than the workspace holds.
 int plan_splits(const pickle_cuda* h, long long groups, long long hist) {
     const long long slots = (long long)h->num_sms * h->decode.occupancy;
     const long long tile = h->decode.tile_rows;
@@ -129,20 +131,12 @@ int plan_splits(const pickle_cuda* h, long long groups, long long hist) {
     const long long cap = (long long)(h->ws_rows / (size_t)h->G) / (groups > 0 ? groups : 1);
     if (max_s > cap) max_s = cap;
     if (max_s < 1) max_s = 1;
-    int best = 1;
-    double best_score = -1.0;
-    for (long long s = 1; s <= max_s; ++s) {
+    if (h->force_splits > 0) {
+        const long long s = h->force_splits < max_s ? h->force_splits : max_s;
         const long long chunk = (hist + s - 1) / s;
-        const long long real_s = chunk > 0 ? (hist + chunk - 1) / chunk : 1;
-        if (real_s != s) continue;
-        const double ctas = (double)(groups * s);
-        const double waves = ctas / (double)slots;
-        const double eff = waves / std::ceil(waves);
-        // Prefer full waves; among equals, fewer splits (less merge work).
-        const double score = eff - 0.002 * (double)s;
-        if (score > best_score + 1e-9) { best_score = score; best = (int)s; }
+        return (int)((hist + chunk - 1) / chunk);
     }
-    return best;
+    return plan_decode_splits(groups, hist, slots, max_s, h->G, h->D);
 }
 
 int check_layer(pickle_cuda* h, int layer, int n_seqs) {
@@ -176,9 +170,20 @@ DecodeArgs base_args(pickle_cuda* h, int layer) {
 int launch_decode(pickle_cuda* h, DecodeArgs& a, int n_z, cudaStream_t st) {
     int rc = prepare_kernel(h, h->decode);
     if (rc != PICKLE_OK) return rc;
-    dim3 grid((unsigned)a.n_splits, (unsigned)h->HK, (unsigned)n_z);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)a.n_splits, (unsigned)h->HK, (unsigned)n_z);
+    cfg.blockDim = dim3(h->decode.threads);
+    cfg.dynamicSmemBytes = h->decode.smem;
+    cfg.stream = st;
+    // The kernel waits for the kernel before it (griddepcontrol.wait) before
+    // its first global access, so its CTAs may become resident early.
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = h->pdl ? 1 : 0;
     void* params[] = {&a};
-    PCU_CHECK(h, cudaLaunchKernel(h->decode.fn, grid, dim3(h->decode.threads), params, h->decode.smem, st));
+    PCU_CHECK(h, cudaLaunchKernelExC(&cfg, h->decode.fn, params));
     if (a.n_splits > 1) {
         MergeArgs m;
         memset(&m, 0, sizeof(m));
@@ -354,6 +359,10 @@ int pickle_cuda_init(const pickle_cuda_params_t* p, int device, pickle_cuda_t** 
         const int v = atoi(env);
         if (v >= 0 && v <= 64) h->l2_ahead = v;
     }
+    // Knob for A/B timing of the dependent launch (0 turns it off).
+    if (const char* env = getenv("PICKLE_CUDA_PDL")) h->pdl = atoi(env) != 0;
+    // Knob for split-count sweeps (the planner's choice when unset).
+    if (const char* env = getenv("PICKLE_CUDA_SPLITS")) h->force_splits = atoi(env);
     h->head_stride = (size_t)p->max_seq * p->head_dim;
     h->seq_stride = h->head_stride * p->n_kv_heads;
     h->layer_stride = h->seq_stride * p->n_seqs;

@@ -34,6 +34,7 @@ struct RopeAppendArgs {
 
 __global__ void rope_append_kernel(const RopeAppendArgs a) {
     const int t = blockIdx.x, seq = blockIdx.y;
+    griddep_launch_dependents();        // the attention launch may take SM slots as this grid drains
     const long long pos = a.pos0 + t;
     const float* sr = a.sin_tab + (size_t)pos * a.half;
     const float* cr = a.cos_tab + (size_t)pos * a.half;
@@ -70,6 +71,7 @@ __global__ void rope_append_kernel(const RopeAppendArgs a) {
 // half % 4 == 0 (checked by the host). One CTA per token.
 __global__ void __launch_bounds__(128) rope_append_vec_kernel(const RopeAppendArgs a) {
     const int t = blockIdx.x, seq = blockIdx.y;
+    griddep_launch_dependents();        // the attention launch may take SM slots as this grid drains
     const long long pos = a.pos0 + t;
     const int D = a.D, half = a.half;
     const int NP = half / 4, NT = (D - 2 * half) / 4, NU = NP + NT, NC = D / 4;

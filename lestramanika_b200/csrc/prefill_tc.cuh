@@ -314,6 +314,9 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // Launched as a programmatic dependent of the producer: the set-up above
+    // overlaps its last CTAs; its q / k / v copies are read only after it ends.
+    griddep_wait();
     const uint32_t tmem = *tmem_slot;
     auto aborted = [&]() { return *(volatile int*)&s_abort != 0; };
     auto fail = [&](int code) { record_error(a.err, code); s_abort = 1; };
@@ -677,8 +680,17 @@ inline int prefill_tc_launch(const __nv_bfloat16* q, const __nv_bfloat16* k, con
     a.next_item = next_item;
     a.err = err;
     const int grid = a.n_items < sms ? a.n_items : sms;
-    tc::prefill_tc_kernel<<<grid, tc::THREADS, tc::SMEM_BYTES, st>>>(tq, tk, tv, a);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(tc::THREADS);
+    cfg.dynamicSmemBytes = tc::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, tc::prefill_tc_kernel, tq, tk, tv, a);
     if (e != cudaSuccess) {
         snprintf(msg, msg_len, "prefill_tc launch: %s", cudaGetErrorString(e));
         return -9;

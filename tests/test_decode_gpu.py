@@ -222,3 +222,78 @@ def test_decode_rejects_unaligned_rows():
         cu.decode_batch_dev(0, B, 3, torch.zeros((B, H, D), device=dev), k, k, out_bad)
     assert e.value.code == -6
     cu.close()
+
+
+def _handle_with(env, *args, **kw):
+    """A handle created with the given PICKLE_CUDA_* knobs set (read at creation)."""
+    import os
+    old = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
+    try:
+        return PickleCuda(*args, **kw)
+    finally:
+        for k, v in old.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+
+
+@pytest.mark.parametrize("B,H,HK,D,ctx", [
+    (1, 32, 8, 128, 4096),    # 37 splits
+    (2, 64, 8, 128, 2049),    # G=8
+    (8, 32, 8, 128, 4096),    # two waves
+    (2, 6, 6, 48, 255),       # D=48, G=1
+    (1, 16, 2, 256, 300),     # D=256
+])
+def test_dependent_launch_agrees_bit_for_bit(B, H, HK, D, ctx):
+    """The split kernel is launched as a programmatic dependent of the kernel
+    before it (griddepcontrol.wait before its first global access). Steps
+    that chain on one another through the cache (each appends the row the
+    next attends over) must give the same bits as plain launches
+    (PICKLE_CUDA_PDL=0), eagerly and in graph replay."""
+    dev = torch.device("cuda", 0)
+    kc, vc, q, k, v = _cache_case(B, H, HK, D, ctx, seed=ctx + 17)
+    handles = [_handle_with(env, 1, H, HK, D, ctx + 8, rope_theta=500000.0, n_seqs=B)
+               for env in ({}, {"PICKLE_CUDA_PDL": "0"})]
+    for cu in handles:
+        for b in range(B):
+            cu.kv_write(0, b, 0, kc[b, :ctx], vc[b, :ctx])
+    qd, kd, vd = (torch.from_numpy(x).to(dev) for x in (q, k, v))
+    outs = [[] for _ in handles]
+    # Back-to-back steps with different split counts; step j + 1 attends the
+    # row step j appended.
+    steps = [(B, ctx), (B, ctx + 1), (max(1, B // 2), ctx + 2), (1, 33), (B, ctx + 3)]
+    for i, cu in enumerate(handles):
+        for n, p in steps:
+            ao = torch.empty((n, H, D), dtype=torch.float32, device=dev)
+            cu.decode_batch_dev(0, n, p, qd[:n], kd[:n], vd[:n], ao)
+            outs[i].append(ao)
+        cu.sync()
+    for j, (n, p) in enumerate(steps):
+        splits = handles[0].decode_plan(n, p)[0]
+        assert torch.equal(outs[0][j], outs[1][j]), f"step {j} (n={n}, pos={p}, splits={splits})"
+    # The last step again (it re-appends the same row, so the cache no longer
+    # changes), twice per graph, replayed.
+    cu = handles[0]
+    n, p = steps[-1]
+    ao = torch.empty((n, H, D), dtype=torch.float32, device=dev)
+    st = torch.cuda.Stream(dev)
+    st.wait_stream(torch.cuda.current_stream(dev))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(st):
+        cu.decode_batch_dev(0, n, p, qd, kd, vd, ao, stream=st)
+        st.synchronize()
+        with torch.cuda.graph(g, stream=st):
+            cu.decode_batch_dev(0, n, p, qd, kd, vd, ao, stream=st)
+            cu.decode_batch_dev(0, n, p, qd, kd, vd, ao, stream=st)
+    for rep in range(3):
+        ao.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(ao, outs[1][-1]), f"graph replay {rep}"
+    del g
+    for cu in handles:
+        cu.close()
+    ref = _run_batch(B, H, HK, D, ctx, seed=ctx + 17)[1]
+    assert_rel(outs[0][0].cpu().numpy(), ref, what=f"B={B} D={D} ctx={ctx}")
