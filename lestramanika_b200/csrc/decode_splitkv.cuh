@@ -320,23 +320,30 @@ PCU_DEV void attend_rows(const float* __restrict__ Kw, const float* __restrict__
     for (int m = G; m < 32; m <<= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, m));
     const float m_new = fmaxf(m_run, tmax);
     const float p = expf(s - m_new);
-    const float alpha = expf(m_run - m_new);
     float psum = p;
     #pragma unroll
     for (int m = G; m < 32; m <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, m);
-    l_run = l_run * alpha + psum;
-    m_run = m_new;
-    #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const float ag = __shfl_sync(0xffffffffu, alpha, g);
-        const float2 a2 = make_float2(ag, ag);
+    // The sum and the accumulators are rescaled only when some head's running
+    // maximum grew (after the first tiles it rarely does); otherwise the
+    // factor is 1 and is skipped.
+    if (__any_sync(0xffffffffu, m_new != m_run)) {
+        const float alpha = expf(m_run - m_new);
+        l_run = l_run * alpha + psum;
         #pragma unroll
-        for (int i = 0; i < C::CPL; ++i) {
-            const float2 lo = mul2(make_float2(acc[g][i].x, acc[g][i].y), a2);
-            const float2 hi = mul2(make_float2(acc[g][i].z, acc[g][i].w), a2);
-            acc[g][i] = make_float4(lo.x, lo.y, hi.x, hi.y);
+        for (int g = 0; g < G; ++g) {
+            const float ag = __shfl_sync(0xffffffffu, alpha, g);
+            const float2 a2 = make_float2(ag, ag);
+            #pragma unroll
+            for (int i = 0; i < C::CPL; ++i) {
+                const float2 lo = mul2(make_float2(acc[g][i].x, acc[g][i].y), a2);
+                const float2 hi = mul2(make_float2(acc[g][i].z, acc[g][i].w), a2);
+                acc[g][i] = make_float4(lo.x, lo.y, hi.x, hi.y);
+            }
         }
+    } else {
+        l_run += psum;
     }
+    m_run = m_new;
     pw[lane] = p;
     __syncwarp();
     #pragma unroll
