@@ -29,7 +29,9 @@
 //               domain (rescaling its O row in TMEM only when the max grows by
 //               more than 2^8), writes P as packed BF16 over the first 64
 //               columns of its S row (tcgen05.st). At the item's end it reads
-//               its O row, releases O_X and stores the normalised row.
+//               its O row, releases O_X and writes the normalised rows out
+//               with TMA tensor stores (32 rows x 32 columns per store,
+//               through a 4 KB per-warp shared-memory stage).
 // MMAs issued by one thread execute in order, so S_FULL_X(j) also means
 // PV_X(j-1) is complete (O_X may be rescaled), and S_X(j+1) cannot overwrite
 // P_X(j) before PV_X(j) has read it. While one tile's softmax runs, the
@@ -94,6 +96,20 @@ PCU_DEV void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
         : "memory");
 }
+
+// TMA tensor store of one box from shared memory (bulk async group; rows
+// past the tensor's bounds are not written).
+PCU_DEV void tma_store_4d(uint32_t src, const CUtensorMap* map, int x, int y, int z, int w) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4}], [%5];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(src) : "memory");
+}
+PCU_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// This thread's committed stores have finished reading shared memory.
+PCU_DEV void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// This thread's committed stores are complete.
+PCU_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Generic-proxy writes to shared memory become visible to the TMA (async proxy).
+PCU_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 PCU_DEV void tmem_alloc(uint32_t* slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
@@ -279,7 +295,8 @@ PCU_DEV void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, bool fi
 
 __global__ void __launch_bounds__(THREADS, 1)
 prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const PrefillTcArgs a) {
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                  const PrefillTcArgs a) {
     extern __shared__ unsigned char smem_raw[];
     // 1024-byte aligned base (128-byte swizzle atoms).
     const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -545,33 +562,37 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars[B_O_FREE + x]);
-            // The warp's 32 rows go out 32 columns at a time through a 4 KB
-            // stage: lane r writes row r (16-byte chunk i at i ^ (r & 7), no
-            // bank conflicts), then eight lanes per row read it back so each
-            // store instruction writes four whole 128-byte row segments. Rows
-            // >= T are padding and not stored.
+            // The warp's 32 rows go out 32 columns at a time through its 4 KB
+            // stage, laid out as the 128-byte swizzle of a 32 x 32 F32 box
+            // (16-byte chunk i of row r at i ^ (r & 7), no bank conflicts),
+            // then one TMA store per chunk. The stores drain asynchronously:
+            // the warp waits only before it rewrites the stage, so the last
+            // chunk's drain overlaps the next item. Rows >= T lie outside the
+            // tensor map and are not written.
             const float inv = 1.0f / (l_run == 0.0f ? 1.0f : l_run);
             unsigned char* stage = base + SMEM_OUT + warp * OUT_STAGE_BYTES;
+            const uint32_t stage_u32 = base_u32 + SMEM_OUT + warp * OUT_STAGE_BYTES;
             const int row_base = qx0 + (warp & 3) * 32;
             #pragma unroll
             for (int c = 0; c < HD / 32; ++c) {
+                if (lane == 0) bulk_wait_read_all();
+                __syncwarp();
                 #pragma unroll
                 for (int i = 0; i < 8; ++i)
                     *reinterpret_cast<float4*>(stage + lane * 128 + ((i ^ (lane & 7)) << 4)) =
                         make_float4(o[c * 32 + 4 * i] * inv, o[c * 32 + 4 * i + 1] * inv,
                                     o[c * 32 + 4 * i + 2] * inv, o[c * 32 + 4 * i + 3] * inv);
+                fence_proxy_async_smem();
                 __syncwarp();
-                #pragma unroll
-                for (int r4 = 0; r4 < 8; ++r4) {
-                    const int r = r4 * 4 + (lane >> 3), ch = lane & 7;
-                    const float4 v4 = *reinterpret_cast<const float4*>(stage + r * 128 + ((ch ^ (r & 7)) << 4));
-                    const int qr = row_base + r;
-                    if (qr < a.T)
-                        reinterpret_cast<float4*>(a.ao + (((size_t)it.seq * a.T + qr) * a.H + it.h) * HD + c * 32)[ch] = v4;
+                if (lane == 0) {
+                    tma_store_4d(stage_u32, &tm_o, c * 32, it.h, row_base, it.seq);
+                    bulk_commit();
                 }
-                __syncwarp();
             }
         }
+        // Stores still in flight must finish before the CTA (and its shared
+        // memory) goes away.
+        if (lane == 0) bulk_wait_all();
         if (!ok && lane == 0) fail(PCU_DEVERR_FULL_WAIT);
     }
     tc_fence_before();
@@ -596,18 +617,24 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
 
 inline bool prefill_tc_supported(int D, int G) { return D == tc::HD && G >= 1 && G <= 8; }
 
-// 3-D tensor map over a head-major BF16 tensor [n_heads][T][D]: box 64 x 128 x 1.
-inline int make_tmap(CUtensorMap* map, const void* ptr, int T, int n_heads, char* msg, size_t msg_len) {
+inline PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder(char* msg, size_t msg_len) {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     if (!encode) {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn) {
             snprintf(msg, msg_len, "cuTensorMapEncodeTiled not available");
-            return -9;
+            return nullptr;
         }
         encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
+    return encode;
+}
+
+// 3-D tensor map over a head-major BF16 tensor [n_heads][T][D]: box 64 x 128 x 1.
+inline int make_tmap(CUtensorMap* map, const void* ptr, int T, int n_heads, char* msg, size_t msg_len) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tmap_encoder(msg, msg_len);
+    if (!encode) return -9;
     const cuuint64_t dims[3] = {(cuuint64_t)tc::HD, (cuuint64_t)T, (cuuint64_t)n_heads};
     const cuuint64_t strides[2] = {(cuuint64_t)tc::HD * 2, (cuuint64_t)T * tc::HD * 2};
     const cuuint32_t box[3] = {64, (cuuint32_t)tc::BM, 1};
@@ -617,6 +644,27 @@ inline int make_tmap(CUtensorMap* map, const void* ptr, int T, int n_heads, char
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         snprintf(msg, msg_len, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return -9;
+    }
+    return 0;
+}
+
+// 4-D tensor map over the F32 output ao [n_seqs][T][H][D] (dims D, H, T,
+// n_seqs): box 32 x 1 x 32 x 1, i.e. 32 columns of one head for 32 rows,
+// with the 128-byte swizzle of the epilogue's stage. The T bound keeps the
+// rows past a sequence's end from being written.
+inline int make_out_tmap(CUtensorMap* map, float* ao, int n_seqs, int T, int H, char* msg, size_t msg_len) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tmap_encoder(msg, msg_len);
+    if (!encode) return -9;
+    const cuuint64_t dims[4] = {(cuuint64_t)tc::HD, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)n_seqs};
+    const cuuint64_t strides[3] = {(cuuint64_t)tc::HD * 4, (cuuint64_t)H * tc::HD * 4, (cuuint64_t)T * H * tc::HD * 4};
+    const cuuint32_t box[4] = {32, 1, 32, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ao, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        snprintf(msg, msg_len, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
         return -9;
     }
     return 0;
@@ -640,9 +688,9 @@ inline int prefill_tc_launch(const __nv_bfloat16* q, const __nv_bfloat16* k, con
         snprintf(msg, msg_len, "output must be 16-byte aligned");
         return -6;
     }
-    alignas(64) CUtensorMap tq, tk, tv;
+    alignas(64) CUtensorMap tq, tk, tv, to;
     if (make_tmap(&tq, q, T, n_seqs * H, msg, msg_len) || make_tmap(&tk, k, T, n_seqs * HK, msg, msg_len) ||
-        make_tmap(&tv, v, T, n_seqs * HK, msg, msg_len))
+        make_tmap(&tv, v, T, n_seqs * HK, msg, msg_len) || make_out_tmap(&to, ao, n_seqs, T, H, msg, msg_len))
         return -9;
     int device = 0, sms = 0;
     if (cudaGetDevice(&device) != cudaSuccess ||
@@ -690,7 +738,7 @@ inline int prefill_tc_launch(const __nv_bfloat16* q, const __nv_bfloat16* k, con
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, tc::prefill_tc_kernel, tq, tk, tv, a);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, tc::prefill_tc_kernel, tq, tk, tv, to, a);
     if (e != cudaSuccess) {
         snprintf(msg, msg_len, "prefill_tc launch: %s", cudaGetErrorString(e));
         return -9;

@@ -109,7 +109,7 @@ def test_prefill_bf16_full_length_subset_of_heads():
         assert err <= BF16_ABS_TOL, (h, err)
 
 
-@pytest.mark.parametrize("B,T,H,HK", [(2, 384, 4, 2), (1, 200, 8, 8)])
+@pytest.mark.parametrize("B,T,H,HK", [(2, 384, 4, 2), (1, 200, 8, 8), (3, 300, 4, 4)])
 def test_prefill_attn_bf16_entry_matches_torch_fp32(B, T, H, HK):
     """pickle_cuda_prefill_attn_bf16_dev against a plain PyTorch fp32 causal
     attention of the same BF16 operands."""
