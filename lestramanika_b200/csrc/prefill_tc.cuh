@@ -28,7 +28,10 @@
 //               (tcgen05.ld), masks, keeps the running max in the log2
 //               domain (rescaling its O row in TMEM only when the max grows by
 //               more than 2^8), writes P as packed BF16 over the first 64
-//               columns of its S row (tcgen05.st). At the item's end it reads
+//               columns of its S row (tcgen05.st) in two halves, keys 0-63
+//               then 64-127, arriving on P_FULL_X after the first and P_HI_X
+//               after the second: the MMA warp issues the first half of
+//               P V while the second half is computed. At the item's end it reads
 //               its O row, releases O_X and writes the normalised rows out
 //               with TMA tensor stores (32 rows x 32 columns per store,
 //               through a 4 KB per-warp shared-memory stage).
@@ -59,7 +62,7 @@ constexpr int SMEM_KV = SMEM_Q + 2 * TILE_BYTES;             // stage s: K at +2
 constexpr int SMEM_OUT = SMEM_KV + STAGES * 2 * TILE_BYTES;  // per softmax warp: 32 rows x 32 floats
 constexpr int OUT_STAGE_BYTES = 32 * 32 * 4;
 constexpr int SMEM_BAR = SMEM_OUT + 8 * OUT_STAGE_BYTES;
-constexpr int N_BARS = 20;
+constexpr int N_BARS = 22;
 constexpr int SMEM_BYTES = SMEM_BAR + N_BARS * 8 + 16 + 1024; // + TMEM address slot + alignment slack
 static_assert(SMEM_BYTES <= 232448, "dynamic shared memory of one CTA on sm_100");
 constexpr int WARP_TMA = 8, WARP_MMA = 9;
@@ -69,7 +72,7 @@ constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: rescale O only when th
 
 // Barrier slots (+x: tile A / B, +s: ring stage, +i: item slot).
 enum { B_Q_FULL = 0, B_Q_FREE = 1, B_KV_FULL = 2, B_KV_EMPTY = 4, B_S_FULL = 6, B_P_FULL = 8, B_O_DONE = 10,
-       B_O_FREE = 12, B_ITEM_FULL = 14, B_ITEM_EMPTY = 16, B_DRAIN = 18 };
+       B_O_FREE = 12, B_ITEM_FULL = 14, B_ITEM_EMPTY = 16, B_DRAIN = 18, B_P_HI = 20 };
 constexpr int SOFTMAX_WARPS = 8;
 
 // tcgen05 instruction descriptor, kind::f16: F32 accumulate, BF16 A and B,
@@ -285,10 +288,10 @@ PCU_DEV void issue_qk(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr) {
 }
 
 // O_X += P_X V_j: A = P_X in TMEM (16 keys = 8 columns per step), B = V_j MN-major.
-PCU_DEV void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, bool first) {
+PCU_DEV void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, bool first, int ks0, int ks1) {
     const uint32_t id = idesc_bf16(HD, 1);
     #pragma unroll
-    for (int ks = 0; ks < BN / 16; ++ks)
+    for (int ks = ks0; ks < ks1; ++ks)
         mma_bf16_ts(o_tmem, p_tmem + ks * 8, smem_desc(v_addr + ks * 16 * 128, HALF_BYTES, 1024), id,
                     (!first || ks > 0));
 }
@@ -316,6 +319,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
             mbar_init(&bars[B_KV_EMPTY + x], 1);
             mbar_init(&bars[B_S_FULL + x], 1);
             mbar_init(&bars[B_P_FULL + x], 4);
+            mbar_init(&bars[B_P_HI + x], 4);
             mbar_init(&bars[B_O_DONE + x], 1);
             mbar_init(&bars[B_O_FREE + x], 4);
             mbar_init(&bars[B_ITEM_FULL + x], 1);
@@ -424,7 +428,11 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
                         if (ok && j == 0 && k > 0) ok = mbar_wait(&bars[B_O_FREE + 0], (k - 1) & 1);
                         if (!ok) break;
                         tc_fence_after();
-                        issue_pv(oA, sA, vaddr, j == 0);
+                        issue_pv(oA, sA, vaddr, j == 0, 0, BN / 32);
+                        ok = mbar_wait(&bars[B_P_HI + 0], (pa - 1) & 1);     // same phase as P_FULL_A
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue_pv(oA, sA, vaddr, j == 0, BN / 32, BN / 16);
                         if (j + 1 == it.n_kv_A) mma_commit(&bars[B_O_DONE + 0]);
                         if (j + 1 < it.n_kv_A) {
                             wait_kv(g + 1);
@@ -438,7 +446,11 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
                     if (ok && j == 0 && k > 0) ok = mbar_wait(&bars[B_O_FREE + 1], (k - 1) & 1);
                     if (!ok) break;
                     tc_fence_after();
-                    issue_pv(oB, sB, vaddr, j == 0);
+                    issue_pv(oB, sB, vaddr, j == 0, 0, BN / 32);
+                    ok = mbar_wait(&bars[B_P_HI + 1], (pb - 1) & 1);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_pv(oB, sB, vaddr, j == 0, BN / 32, BN / 16);
                     if (j + 1 == it.n_kv_B) mma_commit(&bars[B_O_DONE + 1]);
                     if (j + 1 < it.n_kv_B) {
                         wait_kv(g + 1);
@@ -510,26 +522,26 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
                     m_run = m_tile;
                 }
                 // Column pairs: x * scale - m and the row-sum additions as f32x2
-                // (one instruction per pair instead of two).
+                // (one instruction per pair instead of two). P goes out in two
+                // halves (keys 0-63, then 64-127), each followed by an arrival,
+                // so the first half of P V runs while the second half is made.
                 float2 sm2[4];
                 #pragma unroll
                 for (int i = 0; i < 4; ++i) sm2[i] = make_float2(0.f, 0.f);
-                uint32_t pk[BN / 2];
                 const float2 sc2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-m_run, -m_run);
-                #pragma unroll
-                for (int c = 0; c < BN; c += 2) {
-                    const float2 xx = ffma2(make_float2(s[c], s[c + 1]), sc2, nm2);
-                    const float2 p = make_float2(fast_exp2(xx.x), fast_exp2(xx.y));
-                    sm2[(c >> 1) & 3] = fadd2(sm2[(c >> 1) & 3], p);
-                    pk[c >> 1] = pack_bf16x2(p.x, p.y);
+                {
+                    float pk[BN / 4];
+                    #pragma unroll
+                    for (int c = 0; c < BN / 2; c += 2) {
+                        const float2 xx = ffma2(make_float2(s[c], s[c + 1]), sc2, nm2);
+                        const float2 p = make_float2(fast_exp2(xx.x), fast_exp2(xx.y));
+                        sm2[(c >> 1) & 3] = fadd2(sm2[(c >> 1) & 3], p);
+                        pk[c >> 1] = __uint_as_float(pack_bf16x2(p.x, p.y));
+                    }
+                    tmem_st32(s_tm, pk);                          // P_X keys [0, 64) over S_X columns [0, 32)
                 }
-                const float2 t = fadd2(fadd2(sm2[0], sm2[1]), fadd2(sm2[2], sm2[3]));
-                l_run = l_run * alpha + (t.x + t.y);
-                tmem_st64(s_tm, pk);                              // P_X over S_X columns [0, 64)
-                // O_X rescale, once the S row is dead (held together with the S
-                // row it spilled to local memory): S_FULL_X(j) implies PV_X(j-1)
-                // finished, and PV_X(j) waits for this warp's P_FULL arrival
-                // below, so O_X is stable here.
+                // O_X rescale before the first half's arrival: S_FULL_X(j)
+                // implies PV_X(j-1) finished, and PV_X(j) waits for it.
                 if (j > 0 && __any_sync(0xffffffffu, grow)) {
                     #pragma unroll
                     for (int c = 0; c < HD / 32; ++c) {
@@ -544,6 +556,23 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars[B_P_FULL + x]);
+                {
+                    float pk[BN / 4];
+                    #pragma unroll
+                    for (int c = BN / 2; c < BN; c += 2) {
+                        const float2 xx = ffma2(make_float2(s[c], s[c + 1]), sc2, nm2);
+                        const float2 p = make_float2(fast_exp2(xx.x), fast_exp2(xx.y));
+                        sm2[(c >> 1) & 3] = fadd2(sm2[(c >> 1) & 3], p);
+                        pk[(c - BN / 2) >> 1] = __uint_as_float(pack_bf16x2(p.x, p.y));
+                    }
+                    tmem_st32(s_tm + BN / 4, pk);                 // keys [64, 128) over columns [32, 64)
+                }
+                const float2 t = fadd2(fadd2(sm2[0], sm2[1]), fadd2(sm2[2], sm2[3]));
+                l_run = l_run * alpha + (t.x + t.y);
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars[B_P_HI + x]);
             }
             if (!ok) break;
             // Item epilogue: read the O row out of TMEM and release O_X for
