@@ -79,6 +79,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_xchg_kernel(const 
     const int tid = threadIdx.x, row = blockIdx.x;
     const XchgPeers& px = a.px;
     unsigned char* own = px.base[px.rank];
+    griddep_launch_dependents();                        // the next decode step's CTAs may become resident
     if (tid == 0) {
         unsigned* ep = reinterpret_cast<unsigned*>(own + px.row_epoch_off) + row;
         const unsigned e = *ep + 1u;

@@ -268,9 +268,21 @@ int check_xchg(pickle_cuda* h, pickle_cuda_xchg* x) {
 int launch_decode_xchg(pickle_cuda* h, pickle_cuda_xchg* x, DecodeArgs& a, int n_z, XchgMergeArgs& xm,
                        cudaStream_t st) {
     a.force_partials = 1;
-    dim3 grid((unsigned)a.n_splits, (unsigned)h->HK, (unsigned)n_z);
+    // As in launch_decode: the split kernel is a programmatic dependent of
+    // the kernel before it (the previous step's merge-exchange launch, which
+    // triggers at its start), so its CTAs become resident while that one ends.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)a.n_splits, (unsigned)h->HK, (unsigned)n_z);
+    cfg.blockDim = dim3(h->decode.threads);
+    cfg.dynamicSmemBytes = h->decode.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = h->pdl ? 1 : 0;
     void* params[] = {&a};
-    PCU_CHECK(h, cudaLaunchKernel(h->decode.fn, grid, dim3(h->decode.threads), params, h->decode.smem, st));
+    PCU_CHECK(h, cudaLaunchKernelExC(&cfg, h->decode.fn, params));
     memset(&xm.m, 0, sizeof(xm.m));
     xm.m.ws_m = a.ws_m;
     xm.m.ws_l = a.ws_l;
