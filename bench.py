@@ -35,7 +35,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from lestramanika_b200.workloads import C2_B1, C2_B8, C2_B64, C3, C4, C4_SMALL, C5  # noqa: E402
+from lestramanika_b200.workloads import C2_B1, C2_B8, C2_B64, C3, C4, C4_SMALL, C5, C5_SMALL  # noqa: E402
 
 MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS = 6650.0, 1590.0
@@ -1079,7 +1079,7 @@ def run_ours_multi(args, rank, world, local_rank):
 
 
 ONLY = {"c2b1": (C2_B1, True), "c2b8": (C2_B8, False), "c2b64": (C2_B64, False), "c4": (C4, False),
-        "c4s": (C4_SMALL, False), "c5": (C5, False), "c3": (C3, None), "mv": (None, None), "mm": (None, None),
+        "c4s": (C4_SMALL, False), "c5": (C5, False), "c5s": (C5_SMALL, False), "c3": (C3, None), "mv": (None, None), "mm": (None, None),
         "pl": (None, None), "fw": (None, None), "fwd": (None, None), "fwb": (None, None),
         "fwb32": (None, None), "mmb": (None, None)}
 

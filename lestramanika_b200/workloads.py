@@ -59,6 +59,7 @@ C4 = Decode("llama3-70b decode B=16 ctx=32768 (kv-head shard)", 16, 64, 8, 128, 
 # one wave of CTAs) and the size the ncu captures of that kernel are taken at.
 C4_SMALL = Decode("llama3-70b decode B=2 ctx=32768 (per-GPU share at 8 GPUs)", 2, 64, 8, 128, 32768, 500000.0)
 C5 = Decode("long-context decode B=1 ctx=131072 (seq-chunk shard)", 1, 32, 8, 128, 131072, 500000.0)
+C5_SMALL = Decode("long-context decode B=1 ctx=16384 (per-GPU share at 8 GPUs)", 1, 32, 8, 128, 16384, 500000.0)
 
 
 def head_shard(w: Decode, world: int, rank: int):
