@@ -65,6 +65,7 @@ struct DecodeArgs {
     int hist_step;           // query t attends hist_len0 + t * hist_step rows
     int n_splits;
     int l2_ahead;            // short splits: tiles requested into L2 beyond the shared-memory copies
+    int early_l2;            // tiles of the split requested into L2 before griddepcontrol.wait (0: none)
     long long chunk;         // history rows per split
     float scale;             // 1 / sqrtf(D)
     int out_mode;            // 0: ao = normalised output; 1: unnormalised (m, l, acc)
@@ -406,8 +407,21 @@ decode_splitkv_kernel(const DecodeArgs a) {
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, kvh = blockIdx.y, z = blockIdx.z;
+    // While the kernel before it finishes, the producer lane asks L2 for the
+    // split's first cached rows. A prefetch only warms L2, which every write
+    // reaches, so it cannot return stale data; the copies that read the rows
+    // are issued after the wait. (Not for ragged batches: their positions are
+    // in device memory the kernel before may write.)
+    if (a.early_l2 > 0 && !a.seq_pos && warp == C::NCW && lane == 0) {
+        const long long h0 = a.hist_len0 + (long long)(z % a.n_q) * a.hist_step;
+        const long long r0 = (long long)split * a.chunk;
+        const long long r1 = r0 + a.chunk < h0 ? r0 + a.chunk : h0;
+        const int nr = r1 > r0 ? (int)(r1 - r0) : 0;
+        const size_t off = (size_t)(z / a.n_q) * a.seq_stride + (size_t)kvh * a.head_stride + (size_t)r0 * D;
+        prefetch_l2_tiles<C>(a.kc + off, a.vc + off, nr, 0, min((nr + C::TP - 1) / C::TP, a.early_l2));
+    }
     // Launched as a programmatic dependent of the kernel before it on the
-    // stream: nothing that kernel writes (q / k / v, the cache) is touched
+    // stream: nothing that kernel writes (q / k / v, the cache) is read
     // before it completes.
     griddep_wait();
     int seq = z / a.n_q;

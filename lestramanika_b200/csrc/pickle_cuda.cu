@@ -34,6 +34,7 @@ struct pickle_cuda_impl;
 struct pickle_cuda {
     int n_layers, H, HK, D, G, half, max_seq, n_seqs, rope_len, device, num_sms;
     int l2_ahead = kDefaultL2Ahead;   // decode tiles kept requested into L2 ahead of the ring
+    int early_l2 = 3;         // decode tiles requested into L2 before the dependent-launch wait (measured best of 0, 3, 6)
     int pdl = 1;              // split kernel launched as a programmatic dependent of the kernel before it
     int force_splits = 0;     // > 0: split count for every decode (tuning sweeps), else planned
     size_t head_stride, seq_stride, layer_stride;   // floats
@@ -159,6 +160,7 @@ DecodeArgs base_args(pickle_cuda* h, int layer) {
     a.vec = h->half % 4 == 0;                 // table rows then start on 16-byte boundaries
     a.n_q = 1;
     a.l2_ahead = h->l2_ahead;
+    a.early_l2 = h->early_l2;
     a.scale = 1.0f / sqrtf((float)h->D);      // src/pickle_fast.c:1959
     a.ws_m = h->ws_m;
     a.ws_l = h->ws_l;
@@ -370,6 +372,10 @@ int pickle_cuda_init(const pickle_cuda_params_t* p, int device, pickle_cuda_t** 
     if (const char* env = getenv("PICKLE_CUDA_L2_AHEAD")) {
         const int v = atoi(env);
         if (v >= 0 && v <= 64) h->l2_ahead = v;
+    }
+    if (const char* env = getenv("PICKLE_CUDA_EARLY_L2")) {
+        const int v = atoi(env);
+        if (v >= 0 && v <= 64) h->early_l2 = v;
     }
     // Knob for A/B timing of the dependent launch (0 turns it off).
     if (const char* env = getenv("PICKLE_CUDA_PDL")) h->pdl = atoi(env) != 0;
