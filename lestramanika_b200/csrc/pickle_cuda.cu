@@ -34,7 +34,7 @@ struct pickle_cuda_impl;
 struct pickle_cuda {
     int n_layers, H, HK, D, G, half, max_seq, n_seqs, rope_len, device, num_sms;
     int l2_ahead = kDefaultL2Ahead;   // decode tiles kept requested into L2 ahead of the ring
-    int early_l2 = 3;         // decode tiles requested into L2 before the dependent-launch wait (measured best of 0, 3, 6)
+    int early_l2 = 2;         // decode tiles requested into L2 before the dependent-launch wait (measured best of 0, 2, 3, 4, 6)
     int pdl = 1;              // split kernel launched as a programmatic dependent of the kernel before it
     int force_splits = 0;     // > 0: split count for every decode (tuning sweeps), else planned
     size_t head_stride, seq_stride, layer_stride;   // floats
